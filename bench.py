@@ -1,0 +1,340 @@
+#!/usr/bin/env python
+"""Benchmark of the MoE FFN hot path on B200.
+
+Metric: MoE-layer tokens/s (one step = one forward of one MoE layer over T
+tokens), with the HBM-roofline fraction of the dominant kernel. Default
+workload: config 2 of the benchmark set (Qwen3-MoE layer, hidden 2048, 128
+experts, top-8, intermediate 768, Q4_K weights), decode batch T=64, seeded
+synthetic inputs; the T=1..64 sweep is reported beside it.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+--impl reference times the CPU restatement of the reference MoE path (the
+reference is Rust and cannot be built here) on this host's cores, on the same
+workload. Under torchrun with N>1, each rank runs its own replica of the
+layer on its own T tokens (weak scaling) and rank 0 prints the line.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "jero-engine_b200"))
+
+FLUSH_BYTES = 256 << 20   # > 126 MB L2
+FALLBACK_HBM_GBS = 6650.0
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=30)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--config", type=int, default=2)
+    ap.add_argument("--tokens", type=int, default=0, help="T of the headline workload (default: largest of the config)")
+    ap.add_argument("--no-sweep", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    return ap.parse_args()
+
+
+def rank_info():
+    return int(os.environ.get("RANK", 0)), int(os.environ.get("LOCAL_RANK", 0)), int(os.environ.get("WORLD_SIZE", 1))
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 100 ms."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu):
+        self.gpu = gpu
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        try:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.f.close()
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        with open(self.path) as f:
+            for line in f:
+                c = [x.strip() for x in line.split(",")]
+                if len(c) < 9:
+                    continue
+                try:
+                    sm.append(float(c[1]))
+                    smax.append(float(c[2]))
+                except ValueError:
+                    continue
+                for n, v in zip(names, c[5:9]):
+                    if v.lower().startswith("active"):
+                        reasons.add(n)
+        os.unlink(self.path)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def kernel_bytes(cfg, weights, sel_idx, T):
+    """Algorithmic bytes per launch of the expert kernels and of the whole layer.
+    Weights of each routed expert are read once; activations travel as int8
+    blocks (1 byte + 8 bytes of scales per 32 values = 1.25 B/value)."""
+    import numpy as np
+    U = len(np.unique(sel_idx[sel_idx >= 0]))
+    slots = T * cfg.k + (T if cfg.S else 0)
+    per = {m: weights.tensor(f"blk.0.ffn_{m}_exps.weight").data.nbytes // cfg.E for m in ("gate", "up", "down")}
+    sh = {m: (weights.tensor(f"blk.0.ffn_{m}_shexp.weight").data.nbytes if cfg.S else 0)
+          for m in ("gate", "up", "down")}
+    W = max(cfg.I, cfg.S)
+    gate_up = U * (per["gate"] + per["up"]) + sh["gate"] + sh["up"] + T * cfg.H * 1.25 + slots * W * 1.25
+    down = U * per["down"] + sh["down"] + slots * W * 1.25 + slots * cfg.H * 4
+    layer = (U * sum(per.values()) + sum(sh.values()) + cfg.E * cfg.H * 4 + 2 * T * cfg.H * 4 + T * cfg.k * 8)
+    return {"gate_up": gate_up, "down": down, "layer": layer, "U": U}
+
+
+def cpu_baseline(cfg, weights, x, seconds, threads):
+    """The CPU oracle (restatement of the reference path, one token at a time,
+    matvec rows split over a persistent pool) on rows of the same workload."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as orc
+    L = orc.Layer(weights, 0, cfg.E, cfg.k, cfg.S > 0, cfg.route, hidden=cfg.H)
+    L.forward(x[:1], threads)
+    done, t0 = 0, time.perf_counter()
+    while True:
+        L.forward(x, threads)
+        done += x.shape[0]
+        el = time.perf_counter() - t0
+        if el >= seconds:
+            break
+    return done / el, done, el
+
+
+def run_reference(args):
+    rank, _, world = rank_info()
+    if rank != 0:
+        return
+    import synth
+    cfg = synth.CONFIGS[args.config]
+    T = args.tokens or max(cfg.tokens)
+    threads = os.cpu_count() or 1
+    weights = synth.build_weights(cfg)
+    x = synth.gen_x(cfg, T)
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as orc
+    L = orc.Layer(weights, 0, cfg.E, cfg.k, cfg.S > 0, cfg.route, hidden=cfg.H)
+    for _ in range(args.warmup):
+        L.forward(x[:1], threads)
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        L.forward(x, threads)
+        times.append(time.perf_counter() - t0)
+    total = sum(times)
+    value = T * args.steps / total
+    line = {
+        "impl": "reference", "metric": "MoE-layer tokens/s", "value": round(value, 3), "unit": "tokens/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(1e3 * total / args.steps, 3), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+        "config": {"workload": f"{cfg.name} T={T}", "T": T, "H": cfg.H, "E": cfg.E, "k": cfg.k, "I": cfg.I,
+                   "quant": "Q4_K" if cfg.quant == 12 else "Q8_0"},
+        "cpu_baseline": {"value": round(value, 3), "unit": "tokens/s", "cores": threads, "kind": "port",
+                         "sample": f"{T} tokens per step, {args.steps} steps, one token at a time"},
+        "e2e": {"value": round(value, 3), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args):
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    import jeromoe as jm
+    import synth
+
+    rank, local_rank, world = rank_info()
+    torch.cuda.set_device(local_rank)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=torch.device("cuda", local_rank))
+    cfg = synth.CONFIGS[args.config]
+    T = args.tokens or max(cfg.tokens)
+    sweep_T = [] if args.no_sweep else [t for t in cfg.tokens if t != T]
+    weights = synth.build_weights(cfg)
+    x_host = synth.gen_x(cfg, max([T] + sweep_T))
+    ctx = jm.Context(local_rank, max([T] + sweep_T), 1)
+    d, keep = synth.desc_for(cfg, weights)
+    ctx.upload(0, d)
+    stream = torch.cuda.current_stream()
+    ctx.set_stream(stream.cuda_stream)
+    flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device="cuda")
+    x_dev = torch.from_numpy(x_host).cuda()
+    out_dev = torch.empty_like(x_dev)
+    si_dev = torch.empty((x_dev.shape[0], cfg.k), dtype=torch.int32, device="cuda")
+    sw_dev = torch.empty((x_dev.shape[0], cfg.k), dtype=torch.float32, device="cuda")
+
+    def step(t):
+        ctx.forward_ptrs(0, t, x_dev.data_ptr(), out_dev.data_ptr(), si_dev.data_ptr(), sw_dev.data_ptr())
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local_rank])
+
+    def timed(t, steps, profile):
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+        barrier()
+        torch.cuda.synchronize()
+        if profile:
+            ctx.set_profiling(True)
+        for i in range(steps):
+            flush.fill_(i & 0xFF)
+            evs[i][0].record(stream)
+            step(t)
+            evs[i][1].record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        prof = None
+        if profile:
+            prof = ctx.profile_read()
+            ctx.set_profiling(False)
+        return [a.elapsed_time(b) for a, b in evs], prof
+
+    for i in range(args.warmup):
+        flush.fill_(i & 0xFF)
+        step(T)
+    torch.cuda.synchronize()
+    sel = si_dev[:T].cpu().numpy()
+    kb = kernel_bytes(cfg, weights, sel, T)
+
+    sampler = ClockSampler(local_rank)
+    sampler.start()
+    step_ms, (prof, n_fwd) = timed(T, args.steps, True)
+    clocks = sampler.stop()
+    total_ms = sum(step_ms)
+    if world > 1:
+        tt = torch.tensor([total_ms], device="cuda")
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        total_ms = float(tt.item())
+    value = world * T * args.steps / (total_ms / 1e3)
+    hbm, peak_kind = peaks()
+    dom = max(("gate_up", "down"), key=lambda k: prof.get(k, (0, 1))[0])
+    dom_ms = prof[dom][0] / prof[dom][1]
+    achieved = kb[dom] / (dom_ms / 1e3) / 1e9
+    layer_ms = total_ms / args.steps
+    kernels = {k: {"avg_us": round(1e3 * v[0] / v[1], 2), "launches": v[1]} for k, v in prof.items()}
+    launches = sum(v[1] for v in prof.values())
+
+    sweep = []
+    for t in sweep_T:
+        ms, _ = timed(t, 10, False)
+        for _ in range(2):
+            step(t)
+        torch.cuda.synchronize()
+        selt = si_dev[:t].cpu().numpy()
+        b = kernel_bytes(cfg, weights, selt, t)["layer"]
+        m = statistics.median(ms)
+        sweep.append({"T": t, "tokens_per_s": round(t / (m / 1e3), 1), "us_per_layer": round(1e3 * m, 2),
+                      "layer_gbs": round(b / (m / 1e3) / 1e9, 1), "layer_hbm_frac": round(b / (m / 1e3) / 1e9 / hbm, 4)})
+
+    # end to end through the C ABI with pinned host buffers (copies inside the timed region)
+    xh = torch.from_numpy(x_host[:T].copy()).pin_memory()
+    oh = torch.empty_like(xh).pin_memory()
+    sih = torch.empty((T, cfg.k), dtype=torch.int32).pin_memory()
+    swh = torch.empty((T, cfg.k), dtype=torch.float32).pin_memory()
+    e2e_s = 0.0
+    for i in range(args.steps):
+        flush.fill_(i & 0xFF)
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        ctx.forward_ptrs(0, T, xh.data_ptr(), oh.data_ptr(), sih.data_ptr(), swh.data_ptr(), jm.PTR_HOST)
+        e2e_s += time.perf_counter() - t0
+    if world > 1:
+        tt = torch.tensor([e2e_s], device="cuda")
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        e2e_s = float(tt.item())
+    e2e = world * T * args.steps / e2e_s
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        threads = os.cpu_count() or 1
+        v, n, el = cpu_baseline(cfg, weights, x_host[:T], args.cpu_seconds, threads)
+        cpu = {"value": round(v, 3), "unit": "tokens/s", "cores": threads, "kind": "port",
+               "sample": f"{n} tokens of the T={T} workload in {el:.1f} s (oracle, one token at a time)"}
+
+    if rank == 0:
+        line = {
+            "metric": "MoE-layer tokens/s", "value": round(value, 1), "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(layer_ms, 5),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
+            "data": "synthetic (seeded N(0,1) activations, N(0,0.02) weights quantised to GGUF blocks)",
+            "config": {"workload": f"{cfg.name} T={T}", "T": T, "H": cfg.H, "E": cfg.E, "k": cfg.k, "I": cfg.I,
+                       "S": cfg.S, "quant": "Q4_K" if cfg.quant == 12 else "Q8_0",
+                       "experts_routed": kb["U"], "global_batch": world * T,
+                       "parallelism": f"replicas{world}" if world > 1 else "single",
+                       "l2": "flushed between timed steps (256 MiB write); per-step CUDA events"},
+            "roofline": {"bound": "hbm", "kernel": dom, "achieved": round(achieved, 1), "peak": hbm,
+                         "unit": "GB/s", "frac": round(achieved / hbm, 4), "traffic": None,
+                         "peak_source": peak_kind, "algorithmic_bytes_per_launch": int(kb[dom])},
+            "layer_roofline": {"bytes": int(kb["layer"]), "gbs": round(kb["layer"] / (layer_ms / 1e3) / 1e9, 1),
+                               "frac": round(kb["layer"] / (layer_ms / 1e3) / 1e9 / hbm, 4)},
+            "kernels": kernels,
+            "gpu_launches": int(launches),
+            "e2e": {"value": round(e2e, 1), "unit": "tokens/s",
+                    "h2d_bytes_per_step": int(T * cfg.H * 4),
+                    "d2h_bytes_per_step": int(T * cfg.H * 4 + T * cfg.k * 8)},
+            "sweep": sweep,
+            "cpu_baseline": cpu,
+            "clocks": clocks,
+        }
+        print(json.dumps(line), flush=True)
+    ctx.close()
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def main():
+    args = parse()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,223 @@
+/*
+ * jeromoe.h -- C ABI of the B200 (sm_100a) mixture-of-experts FFN path.
+ *
+ * This is the drop-in boundary for jero-engine's MoE block. Each entry point
+ * names the reference interface it replaces (paths relative to the
+ * jero-engine source tree). Plain pointers and sizes only; no CUDA or torch
+ * types appear in the signatures (streams are passed as void*).
+ *
+ * Threading: one context per model and device, one CUDA stream per context.
+ * Calls on one context must be serialised by the caller (the reference runs
+ * the block under the engine's cycle-exclusive step, src/engine.rs:251-274).
+ * No entry point aborts the process; every failure returns a status code and
+ * leaves a message for moe_last_error_message().
+ */
+#ifndef JEROMOE_H
+#define JEROMOE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MOE_ABI_VERSION 1
+
+/* Status codes. Values follow the worker exit codes that the reference maps
+ * its K3Error variants to (src/worker/error.rs:10-32); device-side failures
+ * get codes of their own. */
+typedef enum moe_status {
+    MOE_OK = 0,
+    MOE_ERR_INVALID_ARGS = 2,          /* null pointer, bad count, unknown flag */
+    MOE_ERR_CAPABILITY_MISMATCH = 10,  /* K3Error::CapabilityMismatch: unsupported quant/shape */
+    MOE_ERR_INSUFFICIENT_MEMORY = 11,  /* K3Error::InsufficientLockableMemory, for device HBM */
+    MOE_ERR_RESOURCE_EXHAUSTED = 12,   /* no CUDA device, allocation failure */
+    MOE_ERR_CONTEXT_LENGTH = 15,       /* K3Error::ContextLengthExceeded: T > max_tokens */
+    MOE_ERR_TENSOR_BOUNDS = 14,        /* K3Error::TensorBoundsError: byte size/shape mismatch */
+    MOE_ERR_NOT_UPLOADED = 16,         /* forward on a layer that was never uploaded */
+    MOE_ERR_CUDA = 20,                 /* CUDA runtime error (message has the name) */
+    MOE_ERR_NCCL = 21,                 /* NCCL error in expert-parallel mode */
+    MOE_ERR_TIMEOUT = 22               /* a bounded device or collective wait ran out */
+} moe_status;
+
+/* GGUF ggml_type ids, as the reference's QuantType (jero-core) names them. */
+typedef enum moe_quant {
+    MOE_QUANT_F32 = 0,
+    MOE_QUANT_Q8_0 = 8,   /* 32 values / 34 B: f16 d, 32 x int8 */
+    MOE_QUANT_Q4_K = 12   /* 256 values / 144 B: f16 d, f16 dmin, 12 B scales, 128 B nibbles */
+} moe_quant;
+
+/* A weight tensor as the reference's jero_core::TensorView describes it: GGUF
+ * bytes (host memory, e.g. a view into the mlocked mmap) plus quant and shape.
+ * shape[] is in GGUF order: [in, out] for matrices, [in, out, experts] for the
+ * stacked expert tensors (src/qwen_deepseek.rs:2684-2698). data == NULL means
+ * the tensor is absent (ModelWeights::contains_tensor == false). */
+typedef struct moe_tensor {
+    const void *data;
+    uint64_t nbytes;
+    int32_t quant;
+    int32_t n_dims;
+    int64_t shape[4];
+} moe_tensor;
+
+/* Routing modes. MOE_ROUTE_SOFTMAX_TOPK with normalize=1 is the reference's
+ * only mode (select_top_k_experts, src/gemma.rs:362-442, plus the exp_probs_b
+ * variant, src/qwen_deepseek.rs:773-831). The rest is build-defined. */
+typedef enum moe_route {
+    MOE_ROUTE_SOFTMAX_TOPK = 0,
+    MOE_ROUTE_GROUP_LIMITED = 1   /* keep topk_groups of n_groups by best member, then top-k */
+} moe_route;
+
+/* One MoE layer: the tensors dispatch_qwen3_moe_ffn looks up by name
+ * (src/qwen_deepseek.rs:860-932) plus the recipe's MoeDispatchSpec fields
+ * (src/qwen_deepseek.rs:81-87). */
+typedef struct moe_layer_desc {
+    int32_t hidden;          /* H = norm_ffn_in.len() */
+    int32_t num_experts;     /* E */
+    int32_t top_k;           /* k */
+    int32_t expert_ffn_dim;  /* I (validated against the expert tensors) */
+    int32_t use_shared_expert;
+    int32_t route_mode;      /* moe_route */
+    int32_t normalize;       /* 1 = renormalise chosen weights (reference behaviour) */
+    int32_t n_groups;        /* MOE_ROUTE_GROUP_LIMITED only */
+    int32_t topk_groups;
+    float   routed_scale;    /* multiplies weights when normalize == 0 (1.0 = raw softmax) */
+    moe_tensor router;       /* blk.L.ffn_gate_inp.weight   [H, E] f32 */
+    moe_tensor exp_probs_b;  /* blk.L.exp_probs_b.bias      [E] f32, optional (selection only) */
+    moe_tensor logit_bias;   /* build-defined [E] f32, optional: added to the logits */
+    moe_tensor gate_exps;    /* blk.L.ffn_gate_exps.weight  [H, I, E] */
+    moe_tensor up_exps;      /* blk.L.ffn_up_exps.weight    [H, I, E] */
+    moe_tensor down_exps;    /* blk.L.ffn_down_exps.weight  [I, H, E] */
+    moe_tensor gate_shexp;   /* blk.L.ffn_gate_shexp.weight [H, S], optional */
+    moe_tensor up_shexp;     /* blk.L.ffn_up_shexp.weight   [H, S], optional */
+    moe_tensor down_shexp;   /* blk.L.ffn_down_shexp.weight [S, H], optional */
+} moe_layer_desc;
+
+typedef struct moe_device_spec {
+    int32_t device;            /* CUDA ordinal */
+    int32_t max_tokens;        /* largest T one forward may take (sizes the scratch) */
+    int32_t max_layers;        /* layer slots in the device store */
+    int32_t flags;             /* reserved, 0 */
+    uint64_t reserve_bytes;    /* HBM left free for other users of the device */
+} moe_device_spec;
+
+/* Memory the admission check compares against. The real inspector reads
+ * cudaMemGetInfo on spec->device; tests pass a fixed one, as the reference's
+ * MockMemoryInspector does (src/memory.rs:1519-1547). */
+typedef struct moe_mem_inspector {
+    uint64_t free_bytes;
+    uint64_t total_bytes;
+} moe_mem_inspector;
+
+/* Device footprint, the HBM counterpart of MemoryFootprint (src/memory.rs:792-829). */
+typedef struct moe_footprint {
+    uint64_t weight_bytes;          /* device-layout bytes of all layers */
+    uint64_t scratch_bytes;         /* per-forward working set for max_tokens */
+    uint64_t total_required_bytes;  /* weight + scratch */
+    uint64_t budget_bytes;          /* free - reserve */
+    uint64_t prefill_arena_bytes;   /* optional tensor-core prefill workspace (0 if downgraded) */
+    int32_t  prefill_enabled;       /* 0 when the optional arena did not fit */
+    int32_t  _pad;
+} moe_footprint;
+
+/* Residency counters, the device counterpart of RepackSummary (src/weights.rs:34-49). */
+typedef struct moe_residency {
+    int32_t layers_resident;
+    int32_t upload_count;
+    uint64_t resident_bytes;        /* device bytes held by layer weights */
+    uint64_t gguf_bytes;            /* GGUF bytes those uploads consumed */
+    uint64_t scratch_bytes;
+} moe_residency;
+
+typedef struct moe_ctx moe_ctx;
+
+/* Pointer kinds for moe_forward. */
+#define MOE_PTR_HOST 0    /* host buffers; the call copies in/out and returns when done */
+#define MOE_PTR_DEVICE 1  /* device buffers on spec->device; asynchronous on the context stream */
+
+/* Creates a context on one device. Replaces the model-scoped state that
+ * LockedModelWeights::open_with_admission sets up (src/weights.rs:626-638). */
+int moe_ctx_create(const moe_device_spec *spec, moe_ctx **out);
+
+/* Frees every device buffer; like Drop for LockedModelWeights (src/weights.rs:1146-1171). */
+int moe_ctx_destroy(moe_ctx *ctx);
+
+/* Runs subsequent work on a caller-provided cudaStream_t (NULL = the context's own). */
+int moe_ctx_set_stream(moe_ctx *ctx, void *cuda_stream);
+
+/* Checks that n layers plus the forward scratch fit in device memory, with the
+ * fail-closed and optional-arena-downgrade rules of
+ * check_footprint_against_inspector (src/memory.rs:1576-1605).
+ * inspector == NULL reads cudaMemGetInfo. Never allocates. */
+int moe_admission_check(const moe_device_spec *spec, const moe_layer_desc *layers, int32_t n_layers,
+                        const moe_mem_inspector *inspector, moe_footprint *out);
+
+/* Validates one layer's tensors and uploads them once into device-resident,
+ * expert-major, 128-byte-aligned layouts (the device side of
+ * prepare_repacked_weights, src/weights.rs:776-868, which leaves the 3-D expert
+ * stacks as mmap views, src/weights.rs:89-92). Re-uploading a layer replaces it. */
+int moe_layer_upload(moe_ctx *ctx, int32_t layer, const moe_layer_desc *desc);
+
+/* The batched MoE block: T tokens of x [T x H] f32 -> out [T x H] f32, with
+ * the chosen experts sel_idx [T x k] and weights sel_w [T x k] in rank order.
+ * Row t of the result equals dispatch_qwen3_moe_ffn(out_t, x_t, layer, ...)
+ * (src/qwen_deepseek.rs:847-951) for that token. sel_idx / sel_w may be NULL. */
+int moe_forward(moe_ctx *ctx, int32_t layer, int32_t T, const float *x, float *out,
+                int32_t *sel_idx, float *sel_w, int32_t ptr_kind);
+
+int moe_residency_summary(const moe_ctx *ctx, moe_residency *out);
+
+/* ---- per-kernel timing (the device counterpart of PassTiming, src/engine.rs:136) ---- */
+
+typedef struct moe_kernel_time {
+    char name[32];       /* kernel of the forward sequence ("router", "gate_up", ...) */
+    double total_ms;     /* summed CUDA-event durations on the context stream */
+    int64_t launches;
+} moe_kernel_time;
+
+/* While enabled, every forward records a CUDA event after each of its kernels
+ * on the context stream (no host synchronisation). */
+int moe_ctx_set_profiling(moe_ctx *ctx, int32_t enabled);
+
+/* Synchronises the context stream, folds the recorded events into per-kernel
+ * totals and clears them. Returns up to cap entries; *n_kernels gets the number
+ * of distinct kernels, *n_forwards the forwards timed since the last read. */
+int moe_profile_read(moe_ctx *ctx, moe_kernel_time *out, int32_t cap, int32_t *n_kernels, int32_t *n_forwards);
+
+/* Message of the last failure on ctx (or of the last context-free failure when
+ * ctx == NULL). Valid until the next call on the same context. */
+const char *moe_last_error_message(const moe_ctx *ctx);
+
+/* ---- parity probes (test support; same device code as the forward path) ---- */
+
+/* Copies the dispatch permutation of the last forward on ctx to host memory:
+ * offsets [E+1] (slot range of each expert) and perm_token [T*k] (token of
+ * each slot, experts ascending, tokens ascending inside an expert). */
+int moe_debug_permutation(moe_ctx *ctx, int32_t *offsets, int32_t *perm_token, int32_t *T_out);
+
+/* Quantises rows x [n x cols] f32 with the forward path's activation
+ * quantiser and returns the int32 sum of each 32-value block against GGUF
+ * rows w (host bytes, quant Q8_0 or Q4_K, n rows): isum [n x cols/32].
+ * xq [n x cols] and xd [n x cols/32] receive the quantised activations. */
+int moe_debug_block_dots(int32_t device, int32_t quant, const void *w, const float *x, int32_t n,
+                         int32_t cols, int32_t *isum, int8_t *xq, float *xd);
+
+/* ---- host utilities (no device work) ---- */
+
+/* GGUF row bytes for cols values of quant (0 if cols is not a whole number of blocks). */
+uint64_t moe_row_bytes(int32_t quant, int32_t cols);
+
+/* The repository's quantiser: f32 rows -> GGUF Q8_0 / Q4_K bytes. */
+int moe_quantize_rows(int32_t quant, const float *src, int64_t rows, int32_t cols, void *dst,
+                      int32_t n_threads);
+
+/* Seeded N(0, sigma^2) values: element i of (seed, stream) is a fixed function
+ * of the three numbers (counter-based splitmix64 + Box-Muller). */
+int moe_gen_normal(uint64_t seed, uint64_t stream, uint64_t n, float sigma, float *dst,
+                   int32_t n_threads);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,770 @@
+// api.cpp -- the C ABI of include/jeromoe.h: contexts, HBM admission, layer
+// upload into the device layout, and the batched forward.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <memory>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/jeromoe.h"
+#include "layout.h"
+#include "moe_device.h"
+
+using namespace jmoe;
+
+namespace {
+
+thread_local std::string g_last_error;
+
+constexpr int kMaxExperts = 256;
+constexpr int kMaxTopK = 16;
+constexpr int kMaxGroups = 32;
+
+struct LayerStore {
+    bool present = false;
+    int H = 0, E = 0, k = 0, I = 0, S = 0;
+    int route_mode = 0, normalize = 1, n_groups = 0, topk_groups = 0;
+    float routed_scale = 1.0f;
+    void *block = nullptr;          // one cudaMalloc for the whole layer
+    size_t block_bytes = 0, gguf_bytes = 0;
+    const float *router = nullptr, *logit_bias = nullptr, *sel_bias = nullptr;
+    LayerDev dev{};
+};
+
+struct Scratch {
+    void *block = nullptr;
+    size_t bytes = 0;
+    // capacities this block was carved for
+    int Tm = 0, H = 0, E = 0, k = 0, W = 0;
+    bool af = false;
+    float *x = nullptr, *out = nullptr;
+    int8_t *xq = nullptr;
+    float *xd = nullptr, *xs = nullptr, *logits = nullptr, *sel_w = nullptr;
+    int32_t *sel_idx = nullptr;
+    uint32_t *mask = nullptr;
+    int32_t *wprefix = nullptr, *offsets = nullptr, *perm_token = nullptr, *n_active = nullptr;
+    Problem *problems = nullptr;
+    int8_t *aq = nullptr;
+    float *ad = nullptr, *as = nullptr, *af_buf = nullptr, *y = nullptr;
+};
+
+}  // namespace
+
+namespace {
+
+// CUDA events recorded after each kernel of a forward while profiling is on;
+// folded into per-kernel totals by moe_profile_read.
+struct Profiler {
+    bool on = false;
+    cudaStream_t stream = nullptr;
+    std::vector<cudaEvent_t> pool;
+    size_t used = 0;
+    std::vector<std::pair<const char *, cudaEvent_t>> marks;   // name == nullptr: forward begins
+    int forwards = 0;
+    std::vector<std::pair<std::string, std::pair<double, int64_t>>> totals;
+
+    static void mark_cb(void *user, const char *kernel)
+    {
+        Profiler *p = static_cast<Profiler *>(user);
+        if (p->used == p->pool.size()) {
+            cudaEvent_t ev;
+            if (cudaEventCreate(&ev) != cudaSuccess) return;
+            p->pool.push_back(ev);
+        }
+        cudaEvent_t ev = p->pool[p->used++];
+        if (cudaEventRecord(ev, p->stream) != cudaSuccess) return;
+        p->marks.emplace_back(kernel, ev);
+        if (!kernel) p->forwards++;
+    }
+
+    void add(const char *name, double ms)
+    {
+        for (auto &t : totals)
+            if (t.first == name) { t.second.first += ms; t.second.second++; return; }
+        totals.push_back({name, {ms, 1}});
+    }
+
+    void release()
+    {
+        for (auto ev : pool) cudaEventDestroy(ev);
+        pool.clear();
+        marks.clear();
+        used = 0;
+    }
+};
+
+}  // namespace
+
+struct moe_ctx {
+    moe_device_spec spec{};
+    cudaStream_t own_stream = nullptr;
+    cudaStream_t stream = nullptr;
+    std::vector<LayerStore> layers;
+    Scratch scratch;
+    int upload_count = 0;
+    std::string last_error;
+    // last forward, for moe_debug_permutation
+    int last_layer = -1, last_T = 0;
+    Profiler prof;
+};
+
+namespace {
+
+int fail(moe_ctx *ctx, int code, const char *fmt, ...)
+{
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    if (ctx) ctx->last_error = buf;
+    g_last_error = buf;
+    return code;
+}
+
+int cuda_fail(moe_ctx *ctx, cudaError_t e, const char *what)
+{
+    return fail(ctx, MOE_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
+}
+
+#define CUDA_TRY(ctx, call, what)                            \
+    do {                                                     \
+        cudaError_t e_ = (call);                             \
+        if (e_ != cudaSuccess) return cuda_fail(ctx, e_, what); \
+    } while (0)
+
+// ------------------------------------------------------------ validation
+
+struct MatSpec {
+    int type = 0, rows = 0, cols = 0, experts = 0;
+    const uint8_t *data = nullptr;
+    bool present = false;
+};
+
+const char *quant_name(int q)
+{
+    switch (q) {
+    case MOE_QUANT_F32: return "F32";
+    case MOE_QUANT_Q8_0: return "Q8_0";
+    case MOE_QUANT_Q4_K: return "Q4_K";
+    default: return "unsupported";
+    }
+}
+
+// A GGUF tensor [in, out(, E)] -> rows = out, cols = in.
+int check_tensor(moe_ctx *ctx, const moe_tensor &t, const char *name, int want_dims, int cols, int experts,
+                 MatSpec *out)
+{
+    out->present = t.data != nullptr;
+    if (!out->present) return MOE_OK;
+    if (t.quant != MOE_QUANT_F32 && t.quant != MOE_QUANT_Q8_0 && t.quant != MOE_QUANT_Q4_K)
+        return fail(ctx, MOE_ERR_CAPABILITY_MISMATCH, "unsupported weight quantization %d for tensor '%s'",
+                    t.quant, name);
+    if (t.n_dims != want_dims)
+        return fail(ctx, MOE_ERR_TENSOR_BOUNDS, "tensor '%s' has %d dims, expected %d", name, t.n_dims, want_dims);
+    if (t.shape[0] != cols)
+        return fail(ctx, MOE_ERR_TENSOR_BOUNDS, "tensor '%s' input dim %lld != %d", name, (long long)t.shape[0], cols);
+    if (t.shape[1] <= 0 || t.shape[1] > (1 << 20))
+        return fail(ctx, MOE_ERR_TENSOR_BOUNDS, "tensor '%s' output dim %lld out of range", name,
+                    (long long)t.shape[1]);
+    if (want_dims == 3 && t.shape[2] != experts)
+        return fail(ctx, MOE_ERR_TENSOR_BOUNDS, "tensor '%s' holds %lld experts, expected %d", name,
+                    (long long)t.shape[2], experts);
+    size_t rb = gguf_row_bytes(t.quant, cols);
+    if (!rb)
+        return fail(ctx, MOE_ERR_CAPABILITY_MISMATCH, "tensor '%s': %d columns are not whole %s blocks", name, cols,
+                    quant_name(t.quant));
+    size_t need = rb * (size_t)t.shape[1] * (want_dims == 3 ? (size_t)experts : 1);
+    if (t.nbytes != need)
+        return fail(ctx, MOE_ERR_TENSOR_BOUNDS, "tensor '%s': %llu bytes, shape needs %llu", name,
+                    (unsigned long long)t.nbytes, (unsigned long long)need);
+    out->type = t.quant;
+    out->rows = (int)t.shape[1];
+    out->cols = cols;
+    out->experts = want_dims == 3 ? experts : 1;
+    out->data = static_cast<const uint8_t *>(t.data);
+    return MOE_OK;
+}
+
+struct Validated {
+    int H, E, k, I, S;
+    MatSpec gate, up, down, sg, su, sd;
+    const float *router, *logit_bias, *sel_bias;
+};
+
+int validate_desc(moe_ctx *ctx, const moe_layer_desc *d, Validated *v)
+{
+    if (!d) return fail(ctx, MOE_ERR_INVALID_ARGS, "null layer descriptor");
+    const int H = d->hidden;
+    if (H <= 0) return fail(ctx, MOE_ERR_INVALID_ARGS, "hidden must be positive");
+    if (!d->router.data)
+        return fail(ctx, MOE_ERR_CAPABILITY_MISMATCH,
+                    "layer has no router tensor; the dense fallback stays on the host path");
+    if (d->router.quant != MOE_QUANT_F32)
+        return fail(ctx, MOE_ERR_CAPABILITY_MISMATCH, "router must be F32");
+    if (d->router.n_dims != 2 || d->router.shape[0] != H)
+        return fail(ctx, MOE_ERR_TENSOR_BOUNDS, "router shape must be [hidden, experts]");
+    int E = (int)std::min<int64_t>(d->router.shape[1], d->num_experts);
+    if (E <= 0 || d->top_k <= 0)
+        return fail(ctx, MOE_ERR_CAPABILITY_MISMATCH, "num_experts and top_k must be positive");
+    if ((uint64_t)d->router.nbytes != (uint64_t)d->router.shape[1] * H * 4)
+        return fail(ctx, MOE_ERR_TENSOR_BOUNDS, "router byte length does not match its shape");
+    if (E > kMaxExperts)
+        return fail(ctx, MOE_ERR_CAPABILITY_MISMATCH, "%d experts exceed the supported %d", E, kMaxExperts);
+    if (d->top_k > kMaxTopK || d->top_k > E)
+        return fail(ctx, MOE_ERR_CAPABILITY_MISMATCH, "top_k %d unsupported (max %d, experts %d)", d->top_k,
+                    kMaxTopK, E);
+    if (d->route_mode == MOE_ROUTE_GROUP_LIMITED) {
+        if (d->n_groups <= 1 || d->n_groups > kMaxGroups || E % d->n_groups || d->topk_groups <= 0 ||
+            d->topk_groups >= d->n_groups)
+            return fail(ctx, MOE_ERR_CAPABILITY_MISMATCH, "bad group-limited routing (%d groups, keep %d, %d experts)",
+                        d->n_groups, d->topk_groups, E);
+        if (d->top_k > d->topk_groups * (E / d->n_groups))
+            return fail(ctx, MOE_ERR_CAPABILITY_MISMATCH, "top_k exceeds the experts of the kept groups");
+    } else if (d->route_mode != MOE_ROUTE_SOFTMAX_TOPK) {
+        return fail(ctx, MOE_ERR_INVALID_ARGS, "unknown route_mode %d", d->route_mode);
+    }
+    for (const moe_tensor *b : {&d->exp_probs_b, &d->logit_bias}) {
+        if (b->data && (b->quant != MOE_QUANT_F32 || b->nbytes < (uint64_t)E * 4))
+            return fail(ctx, MOE_ERR_TENSOR_BOUNDS, "router bias must be F32 with at least %d values", E);
+    }
+    int rc;
+    if ((rc = check_tensor(ctx, d->gate_exps, "ffn_gate_exps", 3, H, E, &v->gate))) return rc;
+    if ((rc = check_tensor(ctx, d->up_exps, "ffn_up_exps", 3, H, E, &v->up))) return rc;
+    if (!v->gate.present || !v->up.present || !d->down_exps.data)
+        return fail(ctx, MOE_ERR_CAPABILITY_MISMATCH,
+                    "layer lacks stacked expert tensors; the dense fallback stays on the host path");
+    const int I = v->gate.rows;
+    if (v->up.rows != I) return fail(ctx, MOE_ERR_TENSOR_BOUNDS, "gate/up expert widths differ");
+    if ((rc = check_tensor(ctx, d->down_exps, "ffn_down_exps", 3, I, E, &v->down))) return rc;
+    if (v->down.rows != H) return fail(ctx, MOE_ERR_TENSOR_BOUNDS, "down expert output dim != hidden");
+    if (v->gate.type != v->up.type)
+        return fail(ctx, MOE_ERR_CAPABILITY_MISMATCH, "gate and up experts must share a quantization");
+    if ((v->gate.type == MOE_QUANT_F32) != (v->down.type == MOE_QUANT_F32))
+        return fail(ctx, MOE_ERR_CAPABILITY_MISMATCH, "F32 experts must be F32 in all three matrices");
+    if (v->gate.type != MOE_QUANT_F32 && (I % 32))
+        return fail(ctx, MOE_ERR_CAPABILITY_MISMATCH, "expert width %d is not a multiple of 32", I);
+    int S = 0;
+    v->sg = v->su = v->sd = MatSpec{};
+    if (d->use_shared_expert && d->gate_shexp.data && d->up_shexp.data && d->down_shexp.data) {
+        if ((rc = check_tensor(ctx, d->gate_shexp, "ffn_gate_shexp", 2, H, 1, &v->sg))) return rc;
+        if ((rc = check_tensor(ctx, d->up_shexp, "ffn_up_shexp", 2, H, 1, &v->su))) return rc;
+        S = v->sg.rows;
+        if (v->su.rows != S) return fail(ctx, MOE_ERR_TENSOR_BOUNDS, "shared gate/up widths differ");
+        if ((rc = check_tensor(ctx, d->down_shexp, "ffn_down_shexp", 2, S, 1, &v->sd))) return rc;
+        if (v->sd.rows != H) return fail(ctx, MOE_ERR_TENSOR_BOUNDS, "shared down output dim != hidden");
+        if (v->sg.type != v->su.type)
+            return fail(ctx, MOE_ERR_CAPABILITY_MISMATCH, "shared gate and up must share a quantization");
+        if ((v->sg.type == MOE_QUANT_F32) != (v->sd.type == MOE_QUANT_F32))
+            return fail(ctx, MOE_ERR_CAPABILITY_MISMATCH, "F32 shared expert must be F32 in all three matrices");
+        if (v->sg.type != MOE_QUANT_F32 && (S % 32))
+            return fail(ctx, MOE_ERR_CAPABILITY_MISMATCH, "shared width %d is not a multiple of 32", S);
+    }
+    v->H = H; v->E = E; v->k = d->top_k; v->I = I; v->S = S;
+    v->router = static_cast<const float *>(d->router.data);
+    v->logit_bias = static_cast<const float *>(d->logit_bias.data);
+    v->sel_bias = static_cast<const float *>(d->exp_probs_b.data);
+    return MOE_OK;
+}
+
+// --------------------------------------------------------- device sizing
+
+size_t layer_device_bytes(const Validated &v)
+{
+    size_t b = align_up((size_t)v.E * v.H * 4, 256) + 2 * align_up((size_t)v.E * 4, 256);
+    auto mat = [&](const MatSpec &m) {
+        if (!m.present) return (size_t)0;
+        MatrixPlan p = plan_matrix(m.type, m.rows, m.cols, m.experts);
+        return align_up(p.qs_bytes, 256) + align_up(p.meta_bytes, 256);
+    };
+    return b + mat(v.gate) + mat(v.up) + mat(v.down) + mat(v.sg) + mat(v.su) + mat(v.sd);
+}
+
+struct ScratchDims {
+    int Tm, H, E, k, W;
+    bool af;
+};
+
+// Carves the scratch block (or only measures it when base == nullptr).
+size_t carve_scratch(const ScratchDims &d, uint8_t *base, Scratch *s)
+{
+    size_t off = 0;
+    auto take = [&](size_t bytes) -> uint8_t * {
+        uint8_t *p = base ? base + off : nullptr;
+        off += align_up(bytes ? bytes : 1, 256);
+        return p;
+    };
+    const size_t Tm = (size_t)std::max(d.Tm, 1), H = d.H, E = d.E, k = d.k, W = std::max(d.W, 32);
+    const size_t mw = (Tm + 31) / 32, slots = Tm * k + Tm;
+    const size_t maxp = std::min(E, Tm * k) + 1;
+    Scratch t;
+    t.x = (float *)take(Tm * H * 4);
+    t.out = (float *)take(Tm * H * 4);
+    t.xq = (int8_t *)take(Tm * H);
+    t.xd = (float *)take(Tm * (H / 32 + 1) * 4);
+    t.xs = (float *)take(Tm * (H / 32 + 1) * 4);
+    t.logits = (float *)take(Tm * E * 4);
+    t.sel_idx = (int32_t *)take(Tm * k * 4);
+    t.sel_w = (float *)take(Tm * k * 4);
+    t.mask = (uint32_t *)take(E * mw * 4);
+    t.wprefix = (int32_t *)take(E * mw * 4);
+    t.offsets = (int32_t *)take((E + 1) * 4);
+    t.perm_token = (int32_t *)take(slots * 4);
+    t.problems = (Problem *)take(maxp * sizeof(Problem));
+    t.n_active = (int32_t *)take(4);
+    t.aq = (int8_t *)take(slots * W);
+    t.ad = (float *)take(slots * (W / 32) * 4);
+    t.as = (float *)take(slots * (W / 32) * 4);
+    t.af_buf = d.af ? (float *)take(slots * W * 4) : nullptr;
+    t.y = (float *)take(slots * H * 4);
+    if (s && base) {
+        void *blk = s->block;
+        *s = t;
+        s->block = blk;
+        s->Tm = d.Tm; s->H = d.H; s->E = d.E; s->k = d.k; s->W = d.W; s->af = d.af;
+        s->bytes = off;
+    }
+    return off;
+}
+
+ScratchDims scratch_dims(int Tm, const Validated &v)
+{
+    ScratchDims d;
+    d.Tm = Tm; d.H = v.H; d.E = v.E; d.k = v.k;
+    d.W = std::max(v.I, v.S);
+    d.af = v.down.type == MOE_QUANT_F32 || (v.S && v.sd.type == MOE_QUANT_F32);
+    return d;
+}
+
+// Buffers are used as dense arrays with the layer's own dims (and the
+// scratch's W as the row stride of the SwiGLU buffers), so a block carved for
+// dims that are all at least as large serves the layer.
+bool covers(const Scratch &s, const ScratchDims &d)
+{
+    return s.block && s.Tm >= d.Tm && s.H >= d.H && s.E >= d.E && s.k >= d.k && s.W >= d.W && (s.af || !d.af);
+}
+
+ScratchDims merge(const Scratch &s, const ScratchDims &d)
+{
+    if (!s.block) return d;
+    ScratchDims m = d;
+    m.Tm = std::max(s.Tm, d.Tm);
+    m.H = std::max(s.H, d.H);
+    m.E = std::max(s.E, d.E);
+    m.k = std::max(s.k, d.k);
+    m.W = std::max(s.W, d.W);
+    m.af = s.af || d.af;
+    return m;
+}
+
+DevMatrix to_dev(const MatrixPlan &p, const uint8_t *qs, const uint8_t *meta)
+{
+    DevMatrix m;
+    m.type = p.type; m.rows = p.rows; m.cols = p.cols; m.n_experts = p.n_experts;
+    m.qs = qs; m.meta = meta;
+    m.qs_estride = p.qs_estride; m.meta_estride = p.meta_estride;
+    m.qs_rstride = p.qs_rstride; m.meta_rstride = p.meta_rstride;
+    return m;
+}
+
+void free_layer(LayerStore &L)
+{
+    if (L.block) cudaFree(L.block);
+    L = LayerStore{};
+}
+
+}  // namespace
+
+// ================================================================= C ABI
+
+extern "C" {
+
+int moe_ctx_create(const moe_device_spec *spec, moe_ctx **out)
+{
+    if (!spec || !out) return fail(nullptr, MOE_ERR_INVALID_ARGS, "null argument");
+    *out = nullptr;
+    if (spec->max_tokens <= 0 || spec->max_layers <= 0 || spec->max_layers > 4096)
+        return fail(nullptr, MOE_ERR_INVALID_ARGS, "max_tokens and max_layers must be positive");
+    int ndev = 0;
+    cudaError_t e = cudaGetDeviceCount(&ndev);
+    if (e != cudaSuccess || ndev == 0)
+        return fail(nullptr, MOE_ERR_RESOURCE_EXHAUSTED, "no CUDA device available (%s)", cudaGetErrorName(e));
+    if (spec->device < 0 || spec->device >= ndev)
+        return fail(nullptr, MOE_ERR_INVALID_ARGS, "device %d out of range (%d devices)", spec->device, ndev);
+    if ((e = cudaSetDevice(spec->device)) != cudaSuccess) return cuda_fail(nullptr, e, "cudaSetDevice");
+    std::unique_ptr<moe_ctx> ctx(new moe_ctx());
+    ctx->spec = *spec;
+    ctx->layers.resize(spec->max_layers);
+    if ((e = cudaStreamCreateWithFlags(&ctx->own_stream, cudaStreamNonBlocking)) != cudaSuccess)
+        return cuda_fail(nullptr, e, "cudaStreamCreate");
+    ctx->stream = ctx->own_stream;
+    *out = ctx.release();
+    return MOE_OK;
+}
+
+int moe_ctx_destroy(moe_ctx *ctx)
+{
+    if (!ctx) return MOE_OK;
+    cudaSetDevice(ctx->spec.device);
+    cudaStreamSynchronize(ctx->stream);
+    for (auto &L : ctx->layers) free_layer(L);
+    if (ctx->scratch.block) cudaFree(ctx->scratch.block);
+    ctx->prof.release();
+    if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
+    delete ctx;
+    return MOE_OK;
+}
+
+int moe_ctx_set_stream(moe_ctx *ctx, void *stream)
+{
+    if (!ctx) return fail(nullptr, MOE_ERR_INVALID_ARGS, "null context");
+    ctx->stream = stream ? static_cast<cudaStream_t>(stream) : ctx->own_stream;
+    return MOE_OK;
+}
+
+int moe_admission_check(const moe_device_spec *spec, const moe_layer_desc *layers, int32_t n_layers,
+                        const moe_mem_inspector *inspector, moe_footprint *out)
+{
+    if (!spec || !out || n_layers < 0 || (n_layers > 0 && !layers))
+        return fail(nullptr, MOE_ERR_INVALID_ARGS, "null argument");
+    memset(out, 0, sizeof *out);
+    uint64_t weights = 0, scratch = 0;
+    ScratchDims acc{};
+    bool have = false;
+    for (int i = 0; i < n_layers; i++) {
+        Validated v;
+        int rc = validate_desc(nullptr, &layers[i], &v);
+        if (rc) return rc;
+        weights += layer_device_bytes(v);
+        ScratchDims d = scratch_dims(std::min(spec->max_tokens, 64), v);
+        if (!have) { acc = d; have = true; }
+        else {
+            acc.H = std::max(acc.H, d.H); acc.E = std::max(acc.E, d.E); acc.k = std::max(acc.k, d.k);
+            acc.W = std::max(acc.W, d.W); acc.af = acc.af || d.af;
+        }
+    }
+    uint64_t prefill = 0;
+    if (have) {
+        scratch = carve_scratch(acc, nullptr, nullptr);
+        if (spec->max_tokens > 64) {
+            ScratchDims full = acc;
+            full.Tm = spec->max_tokens;
+            prefill = carve_scratch(full, nullptr, nullptr) - scratch;
+        }
+    }
+    uint64_t free_b = 0, total_b = 0;
+    if (inspector) {
+        free_b = inspector->free_bytes;
+        total_b = inspector->total_bytes;
+    } else {
+        size_t f = 0, t = 0;
+        cudaError_t e = cudaSetDevice(spec->device);
+        if (e == cudaSuccess) e = cudaMemGetInfo(&f, &t);
+        if (e != cudaSuccess) return cuda_fail(nullptr, e, "cudaMemGetInfo");
+        free_b = f; total_b = t;
+    }
+    (void)total_b;
+    const uint64_t budget = free_b > spec->reserve_bytes ? free_b - spec->reserve_bytes : 0;
+    out->weight_bytes = weights;
+    out->scratch_bytes = scratch;
+    out->total_required_bytes = weights + scratch;
+    out->budget_bytes = budget;
+    if (weights + scratch > budget)
+        return fail(nullptr, MOE_ERR_INSUFFICIENT_MEMORY,
+                    "device footprint %llu bytes (weights %llu + scratch %llu) exceeds budget %llu bytes",
+                    (unsigned long long)(weights + scratch), (unsigned long long)weights,
+                    (unsigned long long)scratch, (unsigned long long)budget);
+    // optional prefill arena: dropped, not fatal, when it does not fit
+    if (weights + scratch + prefill <= budget) {
+        out->prefill_arena_bytes = prefill;
+        out->prefill_enabled = 1;
+    } else {
+        out->prefill_arena_bytes = 0;
+        out->prefill_enabled = 0;
+    }
+    return MOE_OK;
+}
+
+int moe_layer_upload(moe_ctx *ctx, int32_t layer, const moe_layer_desc *desc)
+{
+    if (!ctx) return fail(nullptr, MOE_ERR_INVALID_ARGS, "null context");
+    if (layer < 0 || layer >= (int)ctx->layers.size())
+        return fail(ctx, MOE_ERR_INVALID_ARGS, "layer %d outside 0..%d", layer, (int)ctx->layers.size() - 1);
+    Validated v;
+    int rc = validate_desc(ctx, desc, &v);
+    if (rc) return rc;
+    CUDA_TRY(ctx, cudaSetDevice(ctx->spec.device), "cudaSetDevice");
+
+    // admission against free HBM before allocating anything
+    const size_t wbytes = layer_device_bytes(v);
+    ScratchDims sd = merge(ctx->scratch, scratch_dims(ctx->spec.max_tokens, v));
+    const size_t sbytes_new = covers(ctx->scratch, sd) ? 0 : carve_scratch(sd, nullptr, nullptr);
+    size_t freeb = 0, totalb = 0;
+    CUDA_TRY(ctx, cudaMemGetInfo(&freeb, &totalb), "cudaMemGetInfo");
+    const size_t reclaim = ctx->layers[layer].block_bytes + (sbytes_new ? ctx->scratch.bytes : 0);
+    const size_t avail = freeb + reclaim > ctx->spec.reserve_bytes ? freeb + reclaim - ctx->spec.reserve_bytes : 0;
+    if (wbytes + sbytes_new > avail)
+        return fail(ctx, MOE_ERR_INSUFFICIENT_MEMORY, "layer %d needs %zu bytes (+%zu scratch), %zu available",
+                    layer, wbytes, sbytes_new, avail);
+
+    // host staging in device layout
+    std::vector<uint8_t> host(wbytes, 0);
+    size_t off = 0;
+    auto take = [&](size_t bytes) { size_t o = off; off += align_up(bytes, 256); return o; };
+    const size_t o_router = take((size_t)v.E * v.H * 4);
+    const size_t o_lb = take((size_t)v.E * 4), o_sb = take((size_t)v.E * 4);
+    memcpy(host.data() + o_router, v.router, (size_t)v.E * v.H * 4);
+    if (v.logit_bias) memcpy(host.data() + o_lb, v.logit_bias, (size_t)v.E * 4);
+    if (v.sel_bias) memcpy(host.data() + o_sb, v.sel_bias, (size_t)v.E * 4);
+    struct Placed { MatrixPlan plan; size_t qs, meta; bool present; };
+    auto place = [&](const MatSpec &m) {
+        Placed p{};
+        p.present = m.present;
+        if (!m.present) return p;
+        p.plan = plan_matrix(m.type, m.rows, m.cols, m.experts);
+        p.qs = take(p.plan.qs_bytes);
+        p.meta = take(p.plan.meta_bytes);
+        repack_rows(p.plan, m.data, host.data() + p.qs, p.plan.meta_bytes ? host.data() + p.meta : nullptr);
+        return p;
+    };
+    Placed pg = place(v.gate), pu = place(v.up), pd = place(v.down);
+    Placed psg = place(v.sg), psu = place(v.su), psd = place(v.sd);
+
+    // device buffers: release the old layer and grow the scratch if needed
+    CUDA_TRY(ctx, cudaStreamSynchronize(ctx->stream), "cudaStreamSynchronize");
+    free_layer(ctx->layers[layer]);
+    if (sbytes_new) {
+        if (ctx->scratch.block) cudaFree(ctx->scratch.block);
+        ctx->scratch = Scratch{};
+        void *blk = nullptr;
+        CUDA_TRY(ctx, cudaMalloc(&blk, sbytes_new), "cudaMalloc(scratch)");
+        ctx->scratch.block = blk;
+        carve_scratch(sd, static_cast<uint8_t *>(blk), &ctx->scratch);
+    }
+    LayerStore &L = ctx->layers[layer];
+    void *blk = nullptr;
+    CUDA_TRY(ctx, cudaMalloc(&blk, wbytes), "cudaMalloc(layer)");
+    cudaError_t e = cudaMemcpy(blk, host.data(), wbytes, cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) {
+        cudaFree(blk);
+        return cuda_fail(ctx, e, "cudaMemcpy(layer)");
+    }
+    uint8_t *base = static_cast<uint8_t *>(blk);
+    L.present = true;
+    L.block = blk;
+    L.block_bytes = wbytes;
+    L.H = v.H; L.E = v.E; L.k = v.k; L.I = v.I; L.S = v.S;
+    L.route_mode = desc->route_mode;
+    L.normalize = desc->normalize;
+    L.n_groups = desc->n_groups;
+    L.topk_groups = desc->topk_groups;
+    L.routed_scale = desc->routed_scale;
+    L.router = reinterpret_cast<const float *>(base + o_router);
+    L.logit_bias = v.logit_bias ? reinterpret_cast<const float *>(base + o_lb) : nullptr;
+    L.sel_bias = v.sel_bias ? reinterpret_cast<const float *>(base + o_sb) : nullptr;
+    auto dev = [&](const Placed &p) {
+        if (!p.present) return DevMatrix{};
+        return to_dev(p.plan, base + p.qs, p.plan.meta_bytes ? base + p.meta : nullptr);
+    };
+    L.dev.gate = dev(pg); L.dev.up = dev(pu); L.dev.down = dev(pd);
+    L.dev.sh_gate = dev(psg); L.dev.sh_up = dev(psu); L.dev.sh_down = dev(psd);
+    L.gguf_bytes = (size_t)v.E * v.H * 4;
+    for (const MatSpec *m : {&v.gate, &v.up, &v.down, &v.sg, &v.su, &v.sd})
+        if (m->present) L.gguf_bytes += gguf_row_bytes(m->type, m->cols) * m->rows * m->experts;
+    ctx->upload_count++;
+    return MOE_OK;
+}
+
+int moe_forward(moe_ctx *ctx, int32_t layer, int32_t T, const float *x, float *out, int32_t *sel_idx,
+                float *sel_w, int32_t ptr_kind)
+{
+    if (!ctx) return fail(nullptr, MOE_ERR_INVALID_ARGS, "null context");
+    if (layer < 0 || layer >= (int)ctx->layers.size())
+        return fail(ctx, MOE_ERR_INVALID_ARGS, "layer %d outside 0..%d", layer, (int)ctx->layers.size() - 1);
+    LayerStore &L = ctx->layers[layer];
+    if (!L.present) return fail(ctx, MOE_ERR_NOT_UPLOADED, "layer %d was never uploaded", layer);
+    if (T < 0) return fail(ctx, MOE_ERR_INVALID_ARGS, "negative token count");
+    if (T > ctx->spec.max_tokens)
+        return fail(ctx, MOE_ERR_CONTEXT_LENGTH, "T=%d exceeds max_tokens=%d", T, ctx->spec.max_tokens);
+    if (ptr_kind != MOE_PTR_HOST && ptr_kind != MOE_PTR_DEVICE)
+        return fail(ctx, MOE_ERR_INVALID_ARGS, "unknown pointer kind %d", ptr_kind);
+    if (T == 0) return MOE_OK;
+    if (!x || !out) return fail(ctx, MOE_ERR_INVALID_ARGS, "null x or out");
+    if (ptr_kind == MOE_PTR_DEVICE && (((uintptr_t)x | (uintptr_t)out) & 15))
+        return fail(ctx, MOE_ERR_INVALID_ARGS, "device x and out must be 16-byte aligned");
+    CUDA_TRY(ctx, cudaSetDevice(ctx->spec.device), "cudaSetDevice");
+    Scratch &s = ctx->scratch;
+    cudaStream_t st = ctx->stream;
+
+    FwdParams p{};
+    p.T = T; p.H = L.H; p.E = L.E; p.k = L.k; p.I = L.I; p.S = L.S;
+    p.route_mode = L.route_mode; p.normalize = L.normalize;
+    p.n_groups = L.n_groups; p.topk_groups = L.topk_groups; p.routed_scale = L.routed_scale;
+    p.mask_words = (T + 31) / 32;
+    p.quant_x = L.dev.gate.type != FMT_F32 || (L.S && L.dev.sh_gate.type != FMT_F32);
+    p.max_problems = std::min(L.E, T * L.k) + (L.S ? 1 : 0);
+    p.router = L.router; p.logit_bias = L.logit_bias; p.sel_bias = L.sel_bias;
+    p.x = ptr_kind == MOE_PTR_DEVICE ? x : s.x;
+    p.out = ptr_kind == MOE_PTR_DEVICE ? out : s.out;
+    p.xq = s.xq; p.xd = s.xd; p.xs = s.xs; p.logits = s.logits;
+    p.sel_idx = (ptr_kind == MOE_PTR_DEVICE && sel_idx) ? sel_idx : s.sel_idx;
+    p.sel_w = (ptr_kind == MOE_PTR_DEVICE && sel_w) ? sel_w : s.sel_w;
+    p.mask = s.mask; p.wprefix = s.wprefix; p.offsets = s.offsets; p.perm_token = s.perm_token;
+    p.problems = s.problems; p.n_active = s.n_active;
+    p.aq = s.aq; p.ad = s.ad; p.as = s.as; p.af = s.af_buf; p.W = s.W; p.y = s.y;
+
+    if (ptr_kind == MOE_PTR_HOST)
+        CUDA_TRY(ctx, cudaMemcpyAsync(s.x, x, (size_t)T * L.H * 4, cudaMemcpyHostToDevice, st), "copy x");
+    Marker mk{nullptr, nullptr};
+    if (ctx->prof.on) {
+        ctx->prof.stream = st;
+        mk = Marker{&Profiler::mark_cb, &ctx->prof};
+    }
+    int err = launch_forward(p, L.dev, st, mk);
+    if (err != cudaSuccess) return cuda_fail(ctx, (cudaError_t)err, "forward launch");
+    ctx->last_layer = layer;
+    ctx->last_T = T;
+    if (ptr_kind == MOE_PTR_HOST) {
+        CUDA_TRY(ctx, cudaMemcpyAsync(out, s.out, (size_t)T * L.H * 4, cudaMemcpyDeviceToHost, st), "copy out");
+        if (sel_idx)
+            CUDA_TRY(ctx, cudaMemcpyAsync(sel_idx, s.sel_idx, (size_t)T * L.k * 4, cudaMemcpyDeviceToHost, st),
+                     "copy sel_idx");
+        if (sel_w)
+            CUDA_TRY(ctx, cudaMemcpyAsync(sel_w, s.sel_w, (size_t)T * L.k * 4, cudaMemcpyDeviceToHost, st),
+                     "copy sel_w");
+        CUDA_TRY(ctx, cudaStreamSynchronize(st), "forward");
+    }
+    return MOE_OK;
+}
+
+int moe_residency_summary(const moe_ctx *ctx, moe_residency *out)
+{
+    if (!ctx || !out) return fail(nullptr, MOE_ERR_INVALID_ARGS, "null argument");
+    memset(out, 0, sizeof *out);
+    for (const auto &L : ctx->layers) {
+        if (!L.present) continue;
+        out->layers_resident++;
+        out->resident_bytes += L.block_bytes;
+        out->gguf_bytes += L.gguf_bytes;
+    }
+    out->upload_count = ctx->upload_count;
+    out->scratch_bytes = ctx->scratch.bytes;
+    return MOE_OK;
+}
+
+int moe_ctx_set_profiling(moe_ctx *ctx, int32_t enabled)
+{
+    if (!ctx) return fail(nullptr, MOE_ERR_INVALID_ARGS, "null context");
+    ctx->prof.on = enabled != 0;
+    return MOE_OK;
+}
+
+int moe_profile_read(moe_ctx *ctx, moe_kernel_time *out, int32_t cap, int32_t *n_kernels, int32_t *n_forwards)
+{
+    if (!ctx || (cap > 0 && !out)) return fail(nullptr, MOE_ERR_INVALID_ARGS, "null argument");
+    CUDA_TRY(ctx, cudaSetDevice(ctx->spec.device), "cudaSetDevice");
+    Profiler &pf = ctx->prof;
+    if (!pf.marks.empty()) CUDA_TRY(ctx, cudaStreamSynchronize(pf.stream), "profile sync");
+    pf.totals.clear();
+    cudaEvent_t prev = nullptr;
+    for (auto &m : pf.marks) {
+        if (m.first && prev) {
+            float ms = 0.0f;
+            CUDA_TRY(ctx, cudaEventElapsedTime(&ms, prev, m.second), "cudaEventElapsedTime");
+            pf.add(m.first, ms);
+        }
+        prev = m.second;
+    }
+    const int n = (int)pf.totals.size();
+    for (int i = 0; i < n && i < cap; i++) {
+        memset(&out[i], 0, sizeof out[i]);
+        snprintf(out[i].name, sizeof out[i].name, "%s", pf.totals[i].first.c_str());
+        out[i].total_ms = pf.totals[i].second.first;
+        out[i].launches = pf.totals[i].second.second;
+    }
+    if (n_kernels) *n_kernels = n;
+    if (n_forwards) *n_forwards = pf.forwards;
+    pf.marks.clear();
+    pf.used = 0;
+    pf.forwards = 0;
+    return MOE_OK;
+}
+
+const char *moe_last_error_message(const moe_ctx *ctx)
+{
+    if (ctx) return ctx->last_error.c_str();
+    return g_last_error.c_str();
+}
+
+int moe_debug_permutation(moe_ctx *ctx, int32_t *offsets, int32_t *perm_token, int32_t *T_out)
+{
+    if (!ctx || !offsets || !perm_token) return fail(nullptr, MOE_ERR_INVALID_ARGS, "null argument");
+    if (ctx->last_layer < 0) return fail(ctx, MOE_ERR_INVALID_ARGS, "no forward has run on this context");
+    const LayerStore &L = ctx->layers[ctx->last_layer];
+    CUDA_TRY(ctx, cudaSetDevice(ctx->spec.device), "cudaSetDevice");
+    CUDA_TRY(ctx, cudaStreamSynchronize(ctx->stream), "sync");
+    CUDA_TRY(ctx, cudaMemcpy(offsets, ctx->scratch.offsets, (size_t)(L.E + 1) * 4, cudaMemcpyDeviceToHost),
+             "copy offsets");
+    CUDA_TRY(ctx, cudaMemcpy(perm_token, ctx->scratch.perm_token, (size_t)ctx->last_T * L.k * 4,
+                             cudaMemcpyDeviceToHost),
+             "copy perm");
+    if (T_out) *T_out = ctx->last_T;
+    return MOE_OK;
+}
+
+int moe_debug_block_dots(int32_t device, int32_t quant, const void *w, const float *x, int32_t n, int32_t cols,
+                         int32_t *isum, int8_t *xq, float *xd)
+{
+    if (!w || !x || !isum || n <= 0) return fail(nullptr, MOE_ERR_INVALID_ARGS, "null argument");
+    if (quant != MOE_QUANT_Q8_0 && quant != MOE_QUANT_Q4_K)
+        return fail(nullptr, MOE_ERR_CAPABILITY_MISMATCH, "block dots need Q8_0 or Q4_K");
+    if (!gguf_row_bytes(quant, cols)) return fail(nullptr, MOE_ERR_TENSOR_BOUNDS, "cols not whole blocks");
+    cudaError_t e = cudaSetDevice(device);
+    if (e != cudaSuccess) return cuda_fail(nullptr, e, "cudaSetDevice");
+    MatrixPlan plan = plan_matrix(quant, n, cols, 1);
+    std::vector<uint8_t> hq(plan.qs_bytes), hm(plan.meta_bytes);
+    repack_rows(plan, static_cast<const uint8_t *>(w), hq.data(), hm.data());
+    const size_t nb = (size_t)n * (cols / 32);
+    uint8_t *dq = nullptr, *dm = nullptr, *dxq = nullptr;
+    float *dx = nullptr, *dxd = nullptr, *dxs = nullptr;
+    int32_t *dis = nullptr;
+    int rc = MOE_OK;
+    do {
+        if ((e = cudaMalloc(&dq, plan.qs_bytes)) || (e = cudaMalloc(&dm, plan.meta_bytes)) ||
+            (e = cudaMalloc(&dxq, (size_t)n * cols)) || (e = cudaMalloc(&dx, (size_t)n * cols * 4)) ||
+            (e = cudaMalloc(&dxd, nb * 4)) || (e = cudaMalloc(&dxs, nb * 4)) || (e = cudaMalloc(&dis, nb * 4))) {
+            rc = cuda_fail(nullptr, e, "cudaMalloc(probe)");
+            break;
+        }
+        if ((e = cudaMemcpy(dq, hq.data(), plan.qs_bytes, cudaMemcpyHostToDevice)) ||
+            (e = cudaMemcpy(dm, hm.data(), plan.meta_bytes, cudaMemcpyHostToDevice)) ||
+            (e = cudaMemcpy(dx, x, (size_t)n * cols * 4, cudaMemcpyHostToDevice))) {
+            rc = cuda_fail(nullptr, e, "cudaMemcpy(probe)");
+            break;
+        }
+        DevMatrix m = to_dev(plan, dq, dm);
+        if ((e = (cudaError_t)launch_quantize_rows(dx, n, cols, (int8_t *)dxq, dxd, dxs, nullptr)) ||
+            (e = (cudaError_t)launch_block_dots(m, (const int8_t *)dxq, n, dis, nullptr)) ||
+            (e = cudaDeviceSynchronize())) {
+            rc = cuda_fail(nullptr, e, "probe kernels");
+            break;
+        }
+        if ((e = cudaMemcpy(isum, dis, nb * 4, cudaMemcpyDeviceToHost)) ||
+            (xq && (e = cudaMemcpy(xq, dxq, (size_t)n * cols, cudaMemcpyDeviceToHost))) ||
+            (xd && (e = cudaMemcpy(xd, dxd, nb * 4, cudaMemcpyDeviceToHost)))) {
+            rc = cuda_fail(nullptr, e, "cudaMemcpy(probe out)");
+            break;
+        }
+    } while (0);
+    cudaFree(dq); cudaFree(dm); cudaFree(dxq); cudaFree(dx); cudaFree(dxd); cudaFree(dxs); cudaFree(dis);
+    return rc;
+}
+
+uint64_t moe_row_bytes(int32_t quant, int32_t cols) { return gguf_row_bytes(quant, cols); }
+
+}  // extern "C"

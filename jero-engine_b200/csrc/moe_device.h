@@ -1,0 +1,99 @@
+// moe_device.h -- device-side data layout and launch interface of the MoE path.
+//
+// Weights live in HBM in an expert-major structure-of-arrays layout derived
+// from the GGUF blocks at upload time (a byte permutation of the same values,
+// no requantisation):
+//   Q8_0  qs   [E][rows][cols]        int8 quants
+//         meta [E][rows][cols/32]     f16 block scale d
+//   Q4_K  qs   [E][rows][cols/2]      16 bytes per 32-value sub-block j: byte b holds
+//                                     value 32j+b (low nibble) and 32j+16+b (high nibble)
+//         meta [E][rows][cols/256][16] f16 d, f16 dmin, 12 bytes of packed 6-bit scales/mins
+//   F32   qs   [E][rows][cols]        f32
+// Every expert slab starts on a 128-byte boundary.
+#pragma once
+
+#include <stddef.h>
+#include <stdint.h>
+
+namespace jmoe {
+
+enum Fmt : int { FMT_F32 = 0, FMT_Q8_0 = 8, FMT_Q4_K = 12 };
+
+struct DevMatrix {
+    int type;                // Fmt
+    int rows;                // output features
+    int cols;                // input features
+    int n_experts;
+    const uint8_t *qs;
+    const uint8_t *meta;
+    size_t qs_estride;       // bytes per expert slab (multiple of 128)
+    size_t meta_estride;
+    size_t qs_rstride;       // bytes per row
+    size_t meta_rstride;
+};
+
+// One group of slots that share a weight set: a routed expert, or the shared
+// expert (is_shared = 1, all T tokens in order).
+struct Problem {
+    int expert;
+    int slot0;
+    int count;
+    int is_shared;
+};
+
+struct FwdParams {
+    int T, H, E, k, I, S;        // S = 0: no shared expert
+    int route_mode, normalize, n_groups, topk_groups;
+    float routed_scale;
+    int mask_words;              // ceil(T/32)
+    int quant_x;                 // x needs int8 blocks (some gate/up matrix is quantised)
+    int max_problems;            // grid.y of the expert kernels
+
+    const float *x;              // [T][H]
+    const float *router;         // [E][H]
+    const float *logit_bias;     // [E] or null
+    const float *sel_bias;       // [E] or null
+
+    int8_t *xq;                  // [T][H]
+    float *xd;                   // [T][H/32] block scale
+    float *xs;                   // [T][H/32] block scale * block sum of quants
+    float *logits;               // [T][E]
+    int32_t *sel_idx;            // [T][k]
+    float *sel_w;                // [T][k]
+    uint32_t *mask;              // [E][mask_words]: bit t of expert e = token t chose e
+    int32_t *wprefix;            // [E][mask_words]: set bits of expert e before word w
+    int32_t *offsets;            // [E+1]
+    int32_t *perm_token;         // [T*k + T]
+    Problem *problems;           // [max_problems]
+    int32_t *n_active;           // [1]
+
+    int8_t *aq;                  // [slots][W] quantised SwiGLU output, W = max(I, S)
+    float *ad;                   // [slots][W/32]
+    float *as;                   // [slots][W/32]
+    float *af;                   // [slots][W] f32 SwiGLU output (F32 down matrices)
+    int W;
+    float *y;                    // [slots][H] expert outputs
+    float *out;                  // [T][H]
+};
+
+struct LayerDev {
+    DevMatrix gate, up, down;
+    DevMatrix sh_gate, sh_up, sh_down;   // rows == 0: absent
+};
+
+// Called after each kernel of the forward sequence is enqueued (profiling).
+struct Marker {
+    void (*fn)(void *user, const char *kernel);
+    void *user;
+    void mark(const char *k) const { if (fn) fn(user, k); }
+};
+
+// Launch sequence of one forward on stream; returns cudaError_t as int.
+int launch_forward(const FwdParams &p, const LayerDev &L, void *stream, const Marker &mk);
+
+// Integer block sums for the parity probe (same device code as the forward path).
+int launch_block_dots(const DevMatrix &m, const int8_t *xq, int n, int32_t *isum, void *stream);
+int launch_quantize_rows(const float *x, int n, int cols, int8_t *xq, float *xd, float *xs,
+                         void *stream);
+
+}  // namespace jmoe

@@ -1,0 +1,401 @@
+"""Python binding of libjeromoe.so (include/jeromoe.h) over ctypes.
+
+The library is the product; this module only marshals arguments. Every call
+goes to the CUDA path, and a missing or unloadable library raises at import
+(there is no CPU fallback).
+
+Names follow the reference: tensors are addressed by their GGUF names
+(blk.{L}.ffn_gate_inp.weight, blk.{L}.ffn_{gate,up,down}_exps.weight, ...) with
+GGUF shapes [in, out(, experts)], and failures raise MoeError subclasses named
+after the K3Error variants of jero-core that the status codes map to.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+from dataclasses import dataclass, field
+from typing import Dict, Optional, Sequence
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libjeromoe.so")
+
+# ---------------------------------------------------------------- constants
+MOE_OK = 0
+MOE_ERR_INVALID_ARGS = 2
+MOE_ERR_CAPABILITY_MISMATCH = 10
+MOE_ERR_INSUFFICIENT_MEMORY = 11
+MOE_ERR_RESOURCE_EXHAUSTED = 12
+MOE_ERR_TENSOR_BOUNDS = 14
+MOE_ERR_CONTEXT_LENGTH = 15
+MOE_ERR_NOT_UPLOADED = 16
+MOE_ERR_CUDA = 20
+MOE_ERR_NCCL = 21
+MOE_ERR_TIMEOUT = 22
+
+F32, Q8_0, Q4_K = 0, 8, 12
+QUANT_NAMES = {F32: "F32", Q8_0: "Q8_0", Q4_K: "Q4_K"}
+ROUTE_SOFTMAX_TOPK, ROUTE_GROUP_LIMITED = 0, 1
+PTR_HOST, PTR_DEVICE = 0, 1
+
+
+class MoeError(RuntimeError):
+    code = -1
+
+    def __init__(self, code, msg):
+        super().__init__(f"[{code}] {msg}")
+        self.code = code
+        self.msg = msg
+
+
+class InvalidArguments(MoeError): pass
+class CapabilityMismatch(MoeError): pass
+class InsufficientLockableMemory(MoeError): pass
+class ResourceExhausted(MoeError): pass
+class TensorBoundsError(MoeError): pass
+class ContextLengthExceeded(MoeError): pass
+class NotUploaded(MoeError): pass
+class CudaError(MoeError): pass
+class NcclError(MoeError): pass
+class DeviceTimeout(MoeError): pass
+
+
+_ERRORS = {
+    MOE_ERR_INVALID_ARGS: InvalidArguments,
+    MOE_ERR_CAPABILITY_MISMATCH: CapabilityMismatch,
+    MOE_ERR_INSUFFICIENT_MEMORY: InsufficientLockableMemory,
+    MOE_ERR_RESOURCE_EXHAUSTED: ResourceExhausted,
+    MOE_ERR_TENSOR_BOUNDS: TensorBoundsError,
+    MOE_ERR_CONTEXT_LENGTH: ContextLengthExceeded,
+    MOE_ERR_NOT_UPLOADED: NotUploaded,
+    MOE_ERR_CUDA: CudaError,
+    MOE_ERR_NCCL: NcclError,
+    MOE_ERR_TIMEOUT: DeviceTimeout,
+}
+
+# ------------------------------------------------------------------- structs
+
+
+class moe_tensor(C.Structure):
+    _fields_ = [("data", C.c_void_p), ("nbytes", C.c_uint64), ("quant", C.c_int32),
+                ("n_dims", C.c_int32), ("shape", C.c_int64 * 4)]
+
+
+class moe_layer_desc(C.Structure):
+    _fields_ = [("hidden", C.c_int32), ("num_experts", C.c_int32), ("top_k", C.c_int32),
+                ("expert_ffn_dim", C.c_int32), ("use_shared_expert", C.c_int32),
+                ("route_mode", C.c_int32), ("normalize", C.c_int32), ("n_groups", C.c_int32),
+                ("topk_groups", C.c_int32), ("routed_scale", C.c_float),
+                ("router", moe_tensor), ("exp_probs_b", moe_tensor), ("logit_bias", moe_tensor),
+                ("gate_exps", moe_tensor), ("up_exps", moe_tensor), ("down_exps", moe_tensor),
+                ("gate_shexp", moe_tensor), ("up_shexp", moe_tensor), ("down_shexp", moe_tensor)]
+
+
+class moe_device_spec(C.Structure):
+    _fields_ = [("device", C.c_int32), ("max_tokens", C.c_int32), ("max_layers", C.c_int32),
+                ("flags", C.c_int32), ("reserve_bytes", C.c_uint64)]
+
+
+class moe_mem_inspector(C.Structure):
+    _fields_ = [("free_bytes", C.c_uint64), ("total_bytes", C.c_uint64)]
+
+
+class moe_footprint(C.Structure):
+    _fields_ = [("weight_bytes", C.c_uint64), ("scratch_bytes", C.c_uint64),
+                ("total_required_bytes", C.c_uint64), ("budget_bytes", C.c_uint64),
+                ("prefill_arena_bytes", C.c_uint64), ("prefill_enabled", C.c_int32),
+                ("_pad", C.c_int32)]
+
+
+class moe_residency(C.Structure):
+    _fields_ = [("layers_resident", C.c_int32), ("upload_count", C.c_int32),
+                ("resident_bytes", C.c_uint64), ("gguf_bytes", C.c_uint64),
+                ("scratch_bytes", C.c_uint64)]
+
+
+class moe_kernel_time(C.Structure):
+    _fields_ = [("name", C.c_char * 32), ("total_ms", C.c_double), ("launches", C.c_int64)]
+
+
+# ------------------------------------------------------------------- library
+
+EXPORTS = {
+    "moe_ctx_create": (C.c_int, [C.POINTER(moe_device_spec), C.POINTER(C.c_void_p)]),
+    "moe_ctx_destroy": (C.c_int, [C.c_void_p]),
+    "moe_ctx_set_stream": (C.c_int, [C.c_void_p, C.c_void_p]),
+    "moe_admission_check": (C.c_int, [C.POINTER(moe_device_spec), C.POINTER(moe_layer_desc), C.c_int32,
+                                      C.POINTER(moe_mem_inspector), C.POINTER(moe_footprint)]),
+    "moe_layer_upload": (C.c_int, [C.c_void_p, C.c_int32, C.POINTER(moe_layer_desc)]),
+    "moe_forward": (C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.c_void_p, C.c_void_p, C.c_void_p,
+                              C.c_void_p, C.c_int32]),
+    "moe_residency_summary": (C.c_int, [C.c_void_p, C.POINTER(moe_residency)]),
+    "moe_ctx_set_profiling": (C.c_int, [C.c_void_p, C.c_int32]),
+    "moe_profile_read": (C.c_int, [C.c_void_p, C.POINTER(moe_kernel_time), C.c_int32, C.POINTER(C.c_int32),
+                                   C.POINTER(C.c_int32)]),
+    "moe_last_error_message": (C.c_char_p, [C.c_void_p]),
+    "moe_debug_permutation": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.POINTER(C.c_int32)]),
+    "moe_debug_block_dots": (C.c_int, [C.c_int32, C.c_int32, C.c_void_p, C.c_void_p, C.c_int32, C.c_int32,
+                                       C.c_void_p, C.c_void_p, C.c_void_p]),
+    "moe_row_bytes": (C.c_uint64, [C.c_int32, C.c_int32]),
+    "moe_quantize_rows": (C.c_int, [C.c_int32, C.c_void_p, C.c_int64, C.c_int32, C.c_void_p, C.c_int32]),
+    "moe_gen_normal": (C.c_int, [C.c_uint64, C.c_uint64, C.c_uint64, C.c_float, C.c_void_p, C.c_int32]),
+}
+
+
+def _load():
+    if not os.path.exists(LIB_PATH):
+        raise ImportError(f"{LIB_PATH} is not built; run `python jero-engine_b200/build.py`")
+    lib = C.CDLL(LIB_PATH)
+    for name, (res, args) in EXPORTS.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    return lib
+
+
+lib = _load()
+
+
+def _check(rc, ctx=None):
+    if rc != MOE_OK:
+        msg = lib.moe_last_error_message(ctx)
+        raise _ERRORS.get(rc, MoeError)(rc, msg.decode() if msg else "")
+
+
+def _ptr(a: Optional[np.ndarray]):
+    if a is None:
+        return None
+    assert a.flags["C_CONTIGUOUS"], "arrays passed to libjeromoe must be C-contiguous"
+    return a.ctypes.data
+
+
+def threads_default():
+    return max(1, min(32, os.cpu_count() or 1))
+
+
+# --------------------------------------------------------------- host utils
+
+
+def row_bytes(quant: int, cols: int) -> int:
+    return int(lib.moe_row_bytes(quant, cols))
+
+
+def quantize_rows(quant: int, src: np.ndarray, n_threads: int = 0) -> np.ndarray:
+    """f32 [rows, cols] -> GGUF bytes [rows, row_bytes] with the repository quantiser."""
+    src = np.ascontiguousarray(src, dtype=np.float32)
+    rows, cols = src.reshape(-1, src.shape[-1]).shape
+    rb = row_bytes(quant, cols)
+    if rb == 0:
+        raise CapabilityMismatch(MOE_ERR_CAPABILITY_MISMATCH, f"{cols} columns are not whole {QUANT_NAMES.get(quant)} blocks")
+    out = np.empty((rows, rb), dtype=np.uint8)
+    _check(lib.moe_quantize_rows(quant, _ptr(src), rows, cols, _ptr(out), n_threads or threads_default()))
+    return out
+
+
+def gen_normal(seed: int, stream: int, n: int, sigma: float, n_threads: int = 0) -> np.ndarray:
+    out = np.empty(n, dtype=np.float32)
+    _check(lib.moe_gen_normal(seed, stream, n, sigma, _ptr(out), n_threads or threads_default()))
+    return out
+
+
+# ------------------------------------------------------------------ tensors
+
+
+@dataclass
+class Tensor:
+    """A GGUF tensor: raw bytes + quant + GGUF shape (jero_core::TensorView)."""
+    quant: int
+    shape: Sequence[int]
+    data: np.ndarray  # uint8 (or float32 for F32) C-contiguous
+
+    def to_c(self) -> moe_tensor:
+        t = moe_tensor()
+        raw = self.data
+        t.data = raw.ctypes.data
+        t.nbytes = raw.nbytes
+        t.quant = self.quant
+        t.n_dims = len(self.shape)
+        for i, s in enumerate(self.shape):
+            t.shape[i] = int(s)
+        return t
+
+
+def f32_tensor(values: np.ndarray, shape: Sequence[int]) -> Tensor:
+    return Tensor(F32, list(shape), np.ascontiguousarray(values, dtype=np.float32))
+
+
+class ModelWeights:
+    """Name -> Tensor map, the role of jero_core::ModelWeights in the reference."""
+
+    def __init__(self, tensors: Optional[Dict[str, Tensor]] = None):
+        self.tensors: Dict[str, Tensor] = dict(tensors or {})
+
+    def contains_tensor(self, name: str) -> bool:
+        return name in self.tensors
+
+    def tensor(self, name: str) -> Tensor:
+        if name not in self.tensors:
+            raise TensorBoundsError(MOE_ERR_TENSOR_BOUNDS, f"tensor '{name}' not present")
+        return self.tensors[name]
+
+    def tensor_count(self) -> int:
+        return len(self.tensors)
+
+    def total_weight_bytes(self) -> int:
+        return sum(t.data.nbytes for t in self.tensors.values())
+
+    def insert(self, name: str, t: Tensor):
+        self.tensors[name] = t
+
+
+@dataclass
+class RouteSpec:
+    mode: int = ROUTE_SOFTMAX_TOPK
+    normalize: bool = True
+    n_groups: int = 0
+    topk_groups: int = 0
+    routed_scale: float = 1.0
+
+
+def layer_desc(weights: ModelWeights, layer: int, num_experts: int, top_k: int, expert_ffn_dim: int,
+               use_shared_expert: bool, route: Optional[RouteSpec] = None, hidden: Optional[int] = None):
+    """Builds moe_layer_desc from the GGUF tensor names dispatch_qwen3_moe_ffn reads
+    (src/qwen_deepseek.rs:860-932). Returns (desc, keepalive)."""
+    route = route or RouteSpec()
+    d = moe_layer_desc()
+    router_name = f"blk.{layer}.ffn_gate_inp.weight"
+    d.hidden = hidden if hidden is not None else (
+        weights.tensor(router_name).shape[0] if weights.contains_tensor(router_name) else 0)
+    d.num_experts = num_experts
+    d.top_k = top_k
+    d.expert_ffn_dim = expert_ffn_dim
+    d.use_shared_expert = int(bool(use_shared_expert))
+    d.route_mode = route.mode
+    d.normalize = int(bool(route.normalize))
+    d.n_groups = route.n_groups
+    d.topk_groups = route.topk_groups
+    d.routed_scale = route.routed_scale
+    names = {
+        "router": router_name,
+        "exp_probs_b": f"blk.{layer}.exp_probs_b.bias",
+        "logit_bias": f"blk.{layer}.ffn_gate_inp.logit_bias",
+        "gate_exps": f"blk.{layer}.ffn_gate_exps.weight",
+        "up_exps": f"blk.{layer}.ffn_up_exps.weight",
+        "down_exps": f"blk.{layer}.ffn_down_exps.weight",
+        "gate_shexp": f"blk.{layer}.ffn_gate_shexp.weight",
+        "up_shexp": f"blk.{layer}.ffn_up_shexp.weight",
+        "down_shexp": f"blk.{layer}.ffn_down_shexp.weight",
+    }
+    keep = []
+    for field_name, tname in names.items():
+        if weights.contains_tensor(tname):
+            t = weights.tensor(tname)
+            keep.append(t)
+            setattr(d, field_name, t.to_c())
+    return d, keep
+
+
+# ------------------------------------------------------------------ context
+
+
+class Context:
+    """One device context (moe_ctx): device-resident layers + forward scratch."""
+
+    def __init__(self, device: int = 0, max_tokens: int = 64, max_layers: int = 1, reserve_bytes: int = 0):
+        spec = moe_device_spec(device, max_tokens, max_layers, 0, reserve_bytes)
+        h = C.c_void_p()
+        _check(lib.moe_ctx_create(C.byref(spec), C.byref(h)))
+        self.h = h
+        self.device = device
+        self.max_tokens = max_tokens
+        self.layers = {}
+
+    def close(self):
+        if self.h:
+            lib.moe_ctx_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *a):
+        self.close()
+
+    def set_stream(self, stream_ptr: int):
+        _check(lib.moe_ctx_set_stream(self.h, C.c_void_p(stream_ptr)), self.h)
+
+    def upload(self, layer: int, desc: moe_layer_desc, meta=None):
+        _check(lib.moe_layer_upload(self.h, layer, C.byref(desc)), self.h)
+        self.layers[layer] = meta or {"H": desc.hidden, "k": desc.top_k, "E": desc.num_experts}
+
+    def forward(self, layer: int, x: np.ndarray, want_selection: bool = True):
+        """Host arrays in and out: x [T, H] f32 -> (out [T, H], sel_idx [T, k], sel_w [T, k])."""
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        T, H = x.shape
+        k = self.layers[layer]["k"]
+        out = np.empty((T, H), dtype=np.float32)
+        si = np.empty((T, k), dtype=np.int32) if want_selection else None
+        sw = np.empty((T, k), dtype=np.float32) if want_selection else None
+        _check(lib.moe_forward(self.h, layer, T, _ptr(x), _ptr(out), _ptr(si), _ptr(sw), PTR_HOST), self.h)
+        return out, si, sw
+
+    def forward_ptrs(self, layer: int, T: int, x_ptr: int, out_ptr: int, sel_idx_ptr: int = 0, sel_w_ptr: int = 0,
+                     ptr_kind: int = PTR_DEVICE):
+        _check(lib.moe_forward(self.h, layer, T, C.c_void_p(x_ptr), C.c_void_p(out_ptr),
+                               C.c_void_p(sel_idx_ptr or None), C.c_void_p(sel_w_ptr or None), ptr_kind), self.h)
+
+    def set_profiling(self, on: bool):
+        _check(lib.moe_ctx_set_profiling(self.h, int(bool(on))), self.h)
+
+    def profile_read(self):
+        """{kernel: (total_ms, launches)}, forwards timed since the last read."""
+        cap = 32
+        arr = (moe_kernel_time * cap)()
+        nk, nf = C.c_int32(), C.c_int32()
+        _check(lib.moe_profile_read(self.h, arr, cap, C.byref(nk), C.byref(nf)), self.h)
+        return {arr[i].name.decode(): (arr[i].total_ms, arr[i].launches) for i in range(min(nk.value, cap))}, nf.value
+
+    def residency(self) -> moe_residency:
+        r = moe_residency()
+        _check(lib.moe_residency_summary(self.h, C.byref(r)), self.h)
+        return r
+
+    def debug_permutation(self, E: int, k: int):
+        T = C.c_int32()
+        offs = np.empty(E + 1, dtype=np.int32)
+        perm = np.empty(self.max_tokens * k, dtype=np.int32)
+        _check(lib.moe_debug_permutation(self.h, _ptr(offs), _ptr(perm), C.byref(T)), self.h)
+        return offs, perm[: T.value * k]
+
+
+def admission_check(device: int, max_tokens: int, descs: Sequence[moe_layer_desc],
+                    free_bytes: Optional[int] = None, total_bytes: Optional[int] = None,
+                    reserve_bytes: int = 0) -> moe_footprint:
+    spec = moe_device_spec(device, max_tokens, max(1, len(descs)), 0, reserve_bytes)
+    arr = (moe_layer_desc * max(1, len(descs)))(*descs)
+    fp = moe_footprint()
+    insp = None
+    if free_bytes is not None:
+        insp = C.byref(moe_mem_inspector(free_bytes, total_bytes or free_bytes))
+    _check(lib.moe_admission_check(C.byref(spec), arr, len(descs), insp, C.byref(fp)))
+    return fp
+
+
+def debug_block_dots(device: int, quant: int, w_rows: np.ndarray, x: np.ndarray):
+    """Integer block sums of GGUF rows w against the activation quantiser of the
+    forward path: returns (isum [n, cols/32], xq [n, cols], xd [n, cols/32])."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    n, cols = x.shape
+    w_rows = np.ascontiguousarray(w_rows, dtype=np.uint8)
+    isum = np.empty((n, cols // 32), dtype=np.int32)
+    xq = np.empty((n, cols), dtype=np.int8)
+    xd = np.empty((n, cols // 32), dtype=np.float32)
+    _check(lib.moe_debug_block_dots(device, quant, _ptr(w_rows), _ptr(x), n, cols, _ptr(isum), _ptr(xq), _ptr(xd)))
+    return isum, xq, xd

@@ -1,0 +1,292 @@
+"""Parity of the CUDA path (through the C ABI) with the CPU oracle.
+
+Gates: router top-k indices and the dispatch permutation bit-exact; integer
+block sums of the quantised dots bit-exact; selection weights within 1e-5
+relative (the softmax sum is reduced in a different order); layer outputs
+within 1e-2 max relative error per token row, max|y - y_ref| / max|y_ref|.
+"""
+import numpy as np
+import pytest
+
+import jeromoe as jm
+import oracle as orc
+import synth
+from kat_util import (SEEDED_CASES, check_dispatch_expect, kat_weights, load_kats, load_seeded,
+                      row_rel_err, seeded_case)
+
+pytestmark = pytest.mark.gpu
+
+OUT_TOL = 1e-2
+W_RTOL = 1e-5
+KATS = load_kats()
+
+
+def gpu_layer(weights, E, k, I, use_shared, route, hidden, max_tokens, layer=0):
+    ctx = jm.Context(0, max_tokens, layer + 1)
+    d, keep = jm.layer_desc(weights, layer, E, k, I, use_shared, route, hidden)
+    ctx.upload(layer, d)
+    return ctx
+
+
+def oracle_layer(weights, cfg):
+    return orc.Layer(weights, 0, cfg.E, cfg.k, cfg.S > 0, cfg.route, hidden=cfg.H)
+
+
+def assert_parity(out, si, sw, ref_out, ref_si, ref_sw, tol=OUT_TOL):
+    np.testing.assert_array_equal(si, ref_si)
+    np.testing.assert_allclose(sw, ref_sw, rtol=W_RTOL, atol=1e-7)
+    err = row_rel_err(out, ref_out)
+    assert np.all(np.isfinite(out))
+    assert err.max() <= tol, f"max row rel err {err.max():.3e}"
+    return err.max()
+
+
+# ------------------------------------------------------------ reference KATs
+
+@pytest.mark.parametrize("case", KATS["dispatch"], ids=lambda c: c["name"])
+def test_gpu_reference_dispatch_kats(case):
+    w = kat_weights(case)
+    with gpu_layer(w, case["num_experts"], case["top_k"], case["expert_ffn_dim"], case["use_shared_expert"],
+                   None, case["hidden"], 4) as ctx:
+        x = np.array([case["x"]], dtype=np.float32)
+        out, si, sw = ctx.forward(0, x)
+    check_dispatch_expect(case, out[0], si[0], sw[0])
+    L = orc.Layer(w, 0, case["num_experts"], case["top_k"], case["use_shared_expert"], hidden=case["hidden"])
+    ro, rsi, rsw = L.forward(x)
+    assert_parity(out, si, sw, ro, rsi, rsw, tol=1e-5)
+
+
+@pytest.mark.parametrize("case", KATS["routing"], ids=lambda c: c["name"])
+def test_gpu_reference_select_top_k(case):
+    """Router logits equal to the KAT logits: hidden 1, x = [1], router row e = logit e."""
+    logits = np.array(case["logits"], dtype=np.float32)
+    E = len(logits)
+    w = jm.ModelWeights({
+        "blk.0.ffn_gate_inp.weight": jm.f32_tensor(logits, [1, E]),
+        "blk.0.ffn_gate_exps.weight": jm.f32_tensor(np.full(4 * E, 0.1), [1, 4, E]),
+        "blk.0.ffn_up_exps.weight": jm.f32_tensor(np.full(4 * E, 0.2), [1, 4, E]),
+        "blk.0.ffn_down_exps.weight": jm.f32_tensor(np.full(4 * E, 0.3), [4, 1, E]),
+    })
+    x = np.ones((1, 1), dtype=np.float32)
+    with gpu_layer(w, E, case["top_k"], 4, False, None, 1, 1) as ctx:
+        _, si, sw = ctx.forward(0, x)
+    assert si[0].tolist() == case["normalize"]["indices"]
+    np.testing.assert_allclose(sw[0], case["normalize"]["weights"], atol=case["normalize"]["tol"])
+    with gpu_layer(w, E, case["top_k"], 4, False, jm.RouteSpec(normalize=False), 1, 1) as ctx:
+        _, si2, sw2 = ctx.forward(0, x)
+    assert si2[0].tolist() == case["normalize"]["indices"]
+    assert float(sw2[0].sum()) < case["raw"]["weight_sum_lt"]
+
+
+# ------------------------------------------------------- committed fixtures
+
+@pytest.mark.parametrize("name", list(SEEDED_CASES))
+def test_gpu_matches_committed_fixture(name):
+    g = load_seeded()
+    cfg, T = seeded_case(name)
+    w = synth.build_weights(cfg)
+    x = synth.gen_x(cfg, T)
+    with gpu_layer(w, cfg.E, cfg.k, cfg.I, cfg.S > 0, cfg.route, cfg.H, T) as ctx:
+        out, si, sw = ctx.forward(0, x)
+        offs, perm = ctx.debug_permutation(cfg.E, cfg.k)
+    assert_parity(out, si, sw, g[f"{name}/out"], g[f"{name}/sel_idx"], g[f"{name}/sel_w"])
+    np.testing.assert_array_equal(offs, g[f"{name}/offsets"])
+    np.testing.assert_array_equal(perm, g[f"{name}/perm_token"])
+
+
+# ------------------------------------------------------- integer block sums
+
+@pytest.mark.parametrize("quant", [jm.Q8_0, jm.Q4_K])
+def test_gpu_block_sums_bit_exact(quant):
+    n, cols = 24, 2048
+    wf = jm.gen_normal(11, 1, n * cols, 0.02).reshape(n, cols)
+    wq = jm.quantize_rows(quant, wf)
+    x = jm.gen_normal(11, 2, n * cols, 1.0).reshape(n, cols)
+    x[3, :64] = 0.0                      # an all-zero block
+    x[5, 100] = 1e30                     # a block dominated by one value
+    isum, xq, xd = jm.debug_block_dots(0, quant, wq, x)
+    for r in range(n):
+        oq, od = orc.quantize_act(x[r])
+        np.testing.assert_array_equal(xq[r], oq)
+        np.testing.assert_array_equal(xd[r], od)
+        ref, _ = orc.block_dots(quant, wq[r], oq, cols)
+        np.testing.assert_array_equal(isum[r], ref)
+
+
+# ------------------------------------------------------- full-size configs
+
+def _full_size_parity(cid, T, sample=16, seed=0):
+    cfg = synth.CONFIGS[cid]
+    w = synth.build_weights(cfg)
+    x = synth.gen_x(cfg, T)
+    with gpu_layer(w, cfg.E, cfg.k, cfg.I, cfg.S > 0, cfg.route, cfg.H, T) as ctx:
+        out, si, sw = ctx.forward(0, x)
+        offs, perm = ctx.debug_permutation(cfg.E, cfg.k)
+    L = oracle_layer(w, cfg)
+    # routing of every token, bit-exact
+    router = w.tensor("blk.0.ffn_gate_inp.weight").data.reshape(cfg.E, cfg.H)
+    ref_si = np.empty_like(si)
+    ref_sw = np.empty_like(sw)
+    for t in range(T):
+        idx, wt = L.select(orc.router_logits(router, x[t]))
+        ref_si[t, : len(idx)] = idx
+        ref_sw[t, : len(idx)] = wt
+    np.testing.assert_array_equal(si, ref_si)
+    np.testing.assert_allclose(sw, ref_sw, rtol=W_RTOL, atol=1e-7)
+    # the dispatch permutation, bit-exact
+    ro, rp = orc.permutation(ref_si, cfg.E)
+    np.testing.assert_array_equal(offs, ro)
+    np.testing.assert_array_equal(perm, rp)
+    # output rows: all of them for small T, a seeded sample otherwise
+    rows = np.arange(T) if T <= sample else np.sort(np.random.default_rng(seed).choice(T, sample, replace=False))
+    r_out, r_si, r_sw = L.forward(x[rows], 8)
+    return assert_parity(out[rows], si[rows], sw[rows], r_out, r_si, r_sw)
+
+
+@pytest.mark.parametrize("T", [1, 2, 4, 8, 16, 32, 64])
+def test_gpu_cfg2_decode_sweep(T):
+    _full_size_parity(2, T, sample=64)
+
+
+def test_gpu_cfg1_q8_0():
+    _full_size_parity(1, 32, sample=32)
+
+
+def test_gpu_cfg3_deepseek_lite_shared():
+    _full_size_parity(3, 2048)
+
+
+@pytest.mark.parametrize("T", [512, 4096])
+def test_gpu_cfg4_skewed(T):
+    _full_size_parity(4, T)
+
+
+def test_gpu_cfg5_group_limited():
+    _full_size_parity(5, 8192, sample=12)
+
+
+# ------------------------------------------------------------- edge cases
+
+def _small_cfg(**kw):
+    return synth.CONFIGS[2].scaled(E=32, I=256, H=512, **kw)
+
+
+def test_gpu_edge_token_counts_and_errors():
+    cfg = _small_cfg()
+    w = synth.build_weights(cfg)
+    L = oracle_layer(w, cfg)
+    with gpu_layer(w, cfg.E, cfg.k, cfg.I, False, cfg.route, cfg.H, 70) as ctx:
+        for T in (0, 1, 31, 33, 70):
+            x = synth.gen_x(cfg, max(T, 1))[:T]
+            out, si, sw = ctx.forward(0, x)
+            assert out.shape == (T, cfg.H)
+            if T:
+                assert_parity(out, si, sw, *L.forward(x, 4))
+        with pytest.raises(jm.ContextLengthExceeded):
+            ctx.forward(0, synth.gen_x(cfg, 71))
+        with pytest.raises(jm.InvalidArguments):
+            ctx.forward(3, synth.gen_x(cfg, 1))
+        r = ctx.residency()
+        assert r.layers_resident == 1 and r.upload_count == 1 and r.resident_bytes > 0
+    ctx = jm.Context(0, 8, 2)
+    with pytest.raises(jm.NotUploaded):
+        ctx.forward(1, synth.gen_x(cfg, 1))
+    ctx.close()
+
+
+def test_gpu_skewed_routing_many_tokens_per_expert():
+    """Every token picks the same experts (large logit bias): one problem holds
+    all T tokens, several token tiles per CTA."""
+    cfg = _small_cfg(logit_bias_sigma=0.0)
+    w = synth.build_weights(cfg)
+    bias = np.zeros(cfg.E, dtype=np.float32)
+    bias[[3, 7, 11, 12, 20, 25, 30, 31]] = 50.0
+    w.insert("blk.0.ffn_gate_inp.logit_bias", jm.f32_tensor(bias, [cfg.E]))
+    x = synth.gen_x(cfg, 100)
+    with gpu_layer(w, cfg.E, cfg.k, cfg.I, False, cfg.route, cfg.H, 100) as ctx:
+        out, si, sw = ctx.forward(0, x)
+        offs, perm = ctx.debug_permutation(cfg.E, cfg.k)
+    assert sorted(set(si.reshape(-1).tolist())) == [3, 7, 11, 12, 20, 25, 30, 31]
+    assert_parity(out, si, sw, *oracle_layer(w, cfg).forward(x, 4))
+    ro, rp = orc.permutation(si, cfg.E)
+    np.testing.assert_array_equal(offs, ro)
+    np.testing.assert_array_equal(perm, rp)
+
+
+def test_gpu_ties_signed_zero_and_non_finite_logits():
+    """Identical router rows tie -> lower index; zero rows give +0.0 logits
+    that tie with each other; an infinite or NaN logit ranks as -inf with
+    probability 0 (select_top_k_experts, src/gemma.rs:371-417)."""
+    cfg = _small_cfg()
+    w = synth.build_weights(cfg)
+    router = w.tensor("blk.0.ffn_gate_inp.weight").data.reshape(cfg.E, cfg.H).copy()
+    router[9] = router[4]            # exact tie between experts 4 and 9
+    router[14] = 0.0                 # logit +0.0
+    router[15] = -0.0                # the fma chain starts at +0.0, so this logit is +0.0 too
+    router[16, 0] = np.inf           # +inf or NaN logit
+    router[17, :] = np.nan
+    w.insert("blk.0.ffn_gate_inp.weight", jm.f32_tensor(router.reshape(-1), [cfg.H, cfg.E]))
+    x = synth.gen_x(cfg, 40)
+    with gpu_layer(w, cfg.E, cfg.k, cfg.I, False, cfg.route, cfg.H, 40) as ctx:
+        out, si, sw = ctx.forward(0, x)
+    ro, rsi, rsw = oracle_layer(w, cfg).forward(x, 4)
+    assert_parity(out, si, sw, ro, rsi, rsw)
+    pos4 = np.argwhere(si == 4)
+    for t, r in pos4:
+        if 9 in si[t]:
+            assert r < list(si[t]).index(9)
+
+
+def test_gpu_sel_bias_and_group_modes_small():
+    cfg = synth.CONFIGS[5].scaled(E=64, I=256, S=256, H=512)
+    w = synth.build_weights(cfg)
+    bias = jm.gen_normal(99, 1, cfg.E, 0.05)
+    w.insert("blk.0.exp_probs_b.bias", jm.f32_tensor(bias, [cfg.E]))
+    x = synth.gen_x(cfg, 50)
+    for route in (cfg.route, jm.RouteSpec(), jm.RouteSpec(normalize=False, routed_scale=2.5)):
+        c2 = cfg.scaled(n_groups=route.n_groups, topk_groups=route.topk_groups, normalize=route.normalize,
+                        routed_scale=route.routed_scale)
+        with gpu_layer(w, c2.E, c2.k, c2.I, True, route, c2.H, 50) as ctx:
+            out, si, sw = ctx.forward(0, x)
+        assert_parity(out, si, sw, *oracle_layer(w, c2).forward(x, 4))
+
+
+def test_gpu_device_pointers_and_determinism():
+    import torch
+    cfg = _small_cfg()
+    w = synth.build_weights(cfg)
+    x = synth.gen_x(cfg, 20)
+    with gpu_layer(w, cfg.E, cfg.k, cfg.I, False, cfg.route, cfg.H, 20) as ctx:
+        out_h, si_h, sw_h = ctx.forward(0, x)
+        out_h2, _, _ = ctx.forward(0, x)
+        np.testing.assert_array_equal(out_h, out_h2)
+        xd = torch.from_numpy(x).cuda()
+        od = torch.empty_like(xd)
+        sid = torch.empty((20, cfg.k), dtype=torch.int32, device="cuda")
+        swd = torch.empty((20, cfg.k), dtype=torch.float32, device="cuda")
+        stream = torch.cuda.current_stream()
+        ctx.set_stream(stream.cuda_stream)
+        ctx.forward_ptrs(0, 20, xd.data_ptr(), od.data_ptr(), sid.data_ptr(), swd.data_ptr())
+        torch.cuda.synchronize()
+    np.testing.assert_array_equal(od.cpu().numpy(), out_h)
+    np.testing.assert_array_equal(sid.cpu().numpy(), si_h)
+    np.testing.assert_array_equal(swd.cpu().numpy(), sw_h)
+
+
+def test_gpu_reupload_replaces_layer():
+    cfg = _small_cfg()
+    w1 = synth.build_weights(cfg)
+    w2 = synth.build_weights(cfg.scaled(seed=77))
+    x = synth.gen_x(cfg, 5)
+    ctx = jm.Context(0, 5, 1)
+    d1, k1 = synth.desc_for(cfg, w1)
+    ctx.upload(0, d1)
+    a = ctx.forward(0, x)[0]
+    d2, k2 = synth.desc_for(cfg, w2)
+    ctx.upload(0, d2)
+    b = ctx.forward(0, x)[0]
+    assert ctx.residency().upload_count == 2 and ctx.residency().layers_resident == 1
+    ctx.close()
+    assert not np.allclose(a, b)
+    ref = oracle_layer(w2, cfg).forward(x, 2)[0]
+    assert row_rel_err(b, ref).max() <= OUT_TOL
