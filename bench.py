@@ -80,6 +80,16 @@ class ClockSampler:
         except Exception:
             self.proc = None
 
+    def wait_first(self, timeout=5.0):
+        """Blocks until nvidia-smi has written its first sample (it needs a few
+        hundred ms to start), so the samples cover the timed region."""
+        t0 = time.time()
+        while self.proc and time.time() - t0 < timeout:
+            self.f.flush()
+            if os.path.getsize(self.path) > 0:
+                return
+            time.sleep(0.05)
+
     def stop(self):
         if not self.proc:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
@@ -199,7 +209,9 @@ def run_ours(args):
     ctx = jm.Context(local_rank, max([T] + sweep_T), 1)
     d, keep = synth.desc_for(cfg, weights)
     ctx.upload(0, d)
-    stream = torch.cuda.current_stream()
+    # one dedicated stream for the library, the flush and the timing events
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
     ctx.set_stream(stream.cuda_stream)
     flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device="cuda")
     x_dev = torch.from_numpy(x_host).cuda()
@@ -233,15 +245,19 @@ def run_ours(args):
             ctx.set_profiling(False)
         return [a.elapsed_time(b) for a, b in evs], prof
 
+    sampler = ClockSampler(local_rank)
+    sampler.start()
     for i in range(args.warmup):
         flush.fill_(i & 0xFF)
         step(T)
     torch.cuda.synchronize()
     sel = si_dev[:T].cpu().numpy()
     kb = kernel_bytes(cfg, weights, sel, T)
-
-    sampler = ClockSampler(local_rank)
-    sampler.start()
+    sampler.wait_first()
+    # keep the GPU busy until the timed region starts so the samples see it under load
+    for i in range(max(args.warmup, 20)):
+        flush.fill_(i & 0xFF)
+        step(T)
     step_ms, (prof, n_fwd) = timed(T, args.steps, True)
     clocks = sampler.stop()
     total_ms = sum(step_ms)

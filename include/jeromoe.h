@@ -168,6 +168,11 @@ int moe_forward(moe_ctx *ctx, int32_t layer, int32_t T, const float *x, float *o
 
 int moe_residency_summary(const moe_ctx *ctx, moe_residency *out);
 
+/* Reads and clears the device status word of ctx (synchronises the context
+ * stream). *status != 0 (and MOE_ERR_TIMEOUT) when a bounded wait inside a
+ * kernel gave up since the last check; host-pointer forwards check it themselves. */
+int moe_device_status(moe_ctx *ctx, int32_t *status);
+
 /* ---- per-kernel timing (the device counterpart of PassTiming, src/engine.rs:136) ---- */
 
 typedef struct moe_kernel_time {

@@ -51,6 +51,7 @@ struct Scratch {
     Problem *problems = nullptr;
     int8_t *aq = nullptr;
     float *ad = nullptr, *as = nullptr, *af_buf = nullptr, *y = nullptr;
+    int *err = nullptr;
 };
 
 }  // namespace
@@ -110,6 +111,8 @@ struct moe_ctx {
     std::string last_error;
     // last forward, for moe_debug_permutation
     int last_layer = -1, last_T = 0;
+    int num_sms = 148;
+    int *status_host = nullptr;   // pinned word for the device status flag
     Profiler prof;
 };
 
@@ -322,6 +325,7 @@ size_t carve_scratch(const ScratchDims &d, uint8_t *base, Scratch *s)
     t.as = (float *)take(slots * (W / 32) * 4);
     t.af_buf = d.af ? (float *)take(slots * W * 4) : nullptr;
     t.y = (float *)take(slots * H * 4);
+    t.err = (int *)take(4);
     if (s && base) {
         void *blk = s->block;
         *s = t;
@@ -403,6 +407,11 @@ int moe_ctx_create(const moe_device_spec *spec, moe_ctx **out)
     if ((e = cudaStreamCreateWithFlags(&ctx->own_stream, cudaStreamNonBlocking)) != cudaSuccess)
         return cuda_fail(nullptr, e, "cudaStreamCreate");
     ctx->stream = ctx->own_stream;
+    if ((e = cudaDeviceGetAttribute(&ctx->num_sms, cudaDevAttrMultiProcessorCount, spec->device)) != cudaSuccess)
+        return cuda_fail(nullptr, e, "cudaDeviceGetAttribute");
+    if ((e = cudaMallocHost(&ctx->status_host, sizeof(int))) != cudaSuccess)
+        return cuda_fail(nullptr, e, "cudaMallocHost");
+    *ctx->status_host = 0;
     *out = ctx.release();
     return MOE_OK;
 }
@@ -415,6 +424,7 @@ int moe_ctx_destroy(moe_ctx *ctx)
     for (auto &L : ctx->layers) free_layer(L);
     if (ctx->scratch.block) cudaFree(ctx->scratch.block);
     ctx->prof.release();
+    if (ctx->status_host) cudaFreeHost(ctx->status_host);
     if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
     delete ctx;
     return MOE_OK;
@@ -545,6 +555,7 @@ int moe_layer_upload(moe_ctx *ctx, int32_t layer, const moe_layer_desc *desc)
         CUDA_TRY(ctx, cudaMalloc(&blk, sbytes_new), "cudaMalloc(scratch)");
         ctx->scratch.block = blk;
         carve_scratch(sd, static_cast<uint8_t *>(blk), &ctx->scratch);
+        CUDA_TRY(ctx, cudaMemset(ctx->scratch.err, 0, sizeof(int)), "cudaMemset(status)");
     }
     LayerStore &L = ctx->layers[layer];
     void *blk = nullptr;
@@ -617,6 +628,7 @@ int moe_forward(moe_ctx *ctx, int32_t layer, int32_t T, const float *x, float *o
     p.mask = s.mask; p.wprefix = s.wprefix; p.offsets = s.offsets; p.perm_token = s.perm_token;
     p.problems = s.problems; p.n_active = s.n_active;
     p.aq = s.aq; p.ad = s.ad; p.as = s.as; p.af = s.af_buf; p.W = s.W; p.y = s.y;
+    p.err = s.err;
 
     if (ptr_kind == MOE_PTR_HOST)
         CUDA_TRY(ctx, cudaMemcpyAsync(s.x, x, (size_t)T * L.H * 4, cudaMemcpyHostToDevice, st), "copy x");
@@ -625,7 +637,7 @@ int moe_forward(moe_ctx *ctx, int32_t layer, int32_t T, const float *x, float *o
         ctx->prof.stream = st;
         mk = Marker{&Profiler::mark_cb, &ctx->prof};
     }
-    int err = launch_forward(p, L.dev, st, mk);
+    int err = launch_forward(p, L.dev, st, mk, ctx->num_sms);
     if (err != cudaSuccess) return cuda_fail(ctx, (cudaError_t)err, "forward launch");
     ctx->last_layer = layer;
     ctx->last_T = T;
@@ -637,7 +649,32 @@ int moe_forward(moe_ctx *ctx, int32_t layer, int32_t T, const float *x, float *o
         if (sel_w)
             CUDA_TRY(ctx, cudaMemcpyAsync(sel_w, s.sel_w, (size_t)T * L.k * 4, cudaMemcpyDeviceToHost, st),
                      "copy sel_w");
+        CUDA_TRY(ctx, cudaMemcpyAsync(ctx->status_host, s.err, sizeof(int), cudaMemcpyDeviceToHost, st),
+                 "copy status");
         CUDA_TRY(ctx, cudaStreamSynchronize(st), "forward");
+        if (*ctx->status_host) {
+            cudaMemsetAsync(s.err, 0, sizeof(int), st);
+            return fail(ctx, MOE_ERR_TIMEOUT, "a bounded device wait ran out in layer %d (status %d)", layer,
+                        *ctx->status_host);
+        }
+    }
+    return MOE_OK;
+}
+
+int moe_device_status(moe_ctx *ctx, int32_t *status)
+{
+    if (!ctx || !status) return fail(nullptr, MOE_ERR_INVALID_ARGS, "null argument");
+    *status = 0;
+    if (!ctx->scratch.err) return MOE_OK;
+    CUDA_TRY(ctx, cudaSetDevice(ctx->spec.device), "cudaSetDevice");
+    CUDA_TRY(ctx, cudaMemcpyAsync(ctx->status_host, ctx->scratch.err, sizeof(int), cudaMemcpyDeviceToHost,
+                                  ctx->stream),
+             "copy status");
+    CUDA_TRY(ctx, cudaStreamSynchronize(ctx->stream), "status sync");
+    *status = *ctx->status_host;
+    if (*status) {
+        CUDA_TRY(ctx, cudaMemsetAsync(ctx->scratch.err, 0, sizeof(int), ctx->stream), "clear status");
+        return fail(ctx, MOE_ERR_TIMEOUT, "a bounded device wait ran out (status %d)", *status);
     }
     return MOE_OK;
 }

@@ -1,0 +1,48 @@
+// forward.cu -- the launch sequence of one batched MoE forward:
+// memset(mask) -> router -> topk -> scan -> gate_up -> down -> combine.
+// Each kernel reads its work from device-side counters written by the one
+// before it, so the sequence needs no host round trip.
+#include <cuda_runtime.h>
+
+#include "kernels.h"
+#include "moe_device.h"
+
+namespace jmoe {
+
+int launch_forward(const FwdParams &p, const LayerDev &L, void *stream, const Marker &mk, int num_sms)
+{
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    cudaError_t err;
+    if (p.T == 0) return cudaSuccess;
+    mk.mark(nullptr);
+    if ((err = cudaMemsetAsync(p.mask, 0, sizeof(uint32_t) * (size_t)p.E * p.mask_words, st)) != cudaSuccess)
+        return err;
+    if ((err = launch_router(p, st)) != cudaSuccess) return err;
+    mk.mark("router");
+    if ((err = launch_topk(p, st)) != cudaSuccess) return err;
+    mk.mark("topk");
+    if ((err = launch_scan(p, st)) != cudaSuccess) return err;
+    mk.mark("scan");
+
+    const bool has_sh = p.S > 0;
+    // one launch covers routed and shared problems when they share a format
+    const bool same_gu = has_sh && L.sh_gate.type == L.gate.type;
+    const bool same_d = has_sh && L.sh_down.type == L.down.type;
+    if ((err = launch_gate_up(p, L, same_gu ? 2 : 0, num_sms, st)) != cudaSuccess) return err;
+    mk.mark("gate_up");
+    if (has_sh && !same_gu) {
+        if ((err = launch_gate_up(p, L, 1, num_sms, st)) != cudaSuccess) return err;
+        mk.mark("gate_up_shared");
+    }
+    if ((err = launch_down(p, L, same_d ? 2 : 0, num_sms, st)) != cudaSuccess) return err;
+    mk.mark("down");
+    if (has_sh && !same_d) {
+        if ((err = launch_down(p, L, 1, num_sms, st)) != cudaSuccess) return err;
+        mk.mark("down_shared");
+    }
+    if ((err = launch_combine(p, st)) != cudaSuccess) return err;
+    mk.mark("combine");
+    return cudaSuccess;
+}
+
+}  // namespace jmoe

@@ -1,0 +1,29 @@
+// kernels.h -- host-side launchers of the MoE kernels (internal to the library).
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include "moe_device.h"
+
+namespace jmoe {
+
+// Work split of the streaming expert kernels, chosen on the host.
+struct StreamCfg {
+    int stages;        // ring depth
+    int stage_bytes;   // bytes of one ring stage (multiple of 128)
+    int act_k;         // largest activation row (values) staged in shared memory
+    int mode;          // 0: routed problems, 1: the shared expert only, 2: both
+    int down_f32;      // gate_up: store a in f32 (F32 down matrices)
+    int rt_routed;     // row tiles per routed problem
+    int rt_shared;     // row tiles of the shared problem
+    int item_rows;     // rows per work item
+};
+
+cudaError_t launch_router(const FwdParams &p, cudaStream_t st);
+cudaError_t launch_topk(const FwdParams &p, cudaStream_t st);
+cudaError_t launch_scan(const FwdParams &p, cudaStream_t st);
+cudaError_t launch_gate_up(const FwdParams &p, const LayerDev &L, int mode, int num_sms, cudaStream_t st);
+cudaError_t launch_down(const FwdParams &p, const LayerDev &L, int mode, int num_sms, cudaStream_t st);
+cudaError_t launch_combine(const FwdParams &p, cudaStream_t st);
+
+}  // namespace jmoe

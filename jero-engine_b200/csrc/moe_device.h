@@ -74,6 +74,7 @@ struct FwdParams {
     int W;
     float *y;                    // [slots][H] expert outputs
     float *out;                  // [T][H]
+    int *err;                    // device status word: 0 ok, 1 a bounded wait ran out
 };
 
 struct LayerDev {
@@ -89,7 +90,8 @@ struct Marker {
 };
 
 // Launch sequence of one forward on stream; returns cudaError_t as int.
-int launch_forward(const FwdParams &p, const LayerDev &L, void *stream, const Marker &mk);
+// num_sms sizes the grids of the streaming expert kernels.
+int launch_forward(const FwdParams &p, const LayerDev &L, void *stream, const Marker &mk, int num_sms);
 
 // Integer block sums for the parity probe (same device code as the forward path).
 int launch_block_dots(const DevMatrix &m, const int8_t *xq, int n, int32_t *isum, void *stream);

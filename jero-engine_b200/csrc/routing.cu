@@ -1,0 +1,445 @@
+// routing.cu -- router logits, top-k selection and the dispatch permutation.
+#include <cuda_runtime.h>
+#include <math.h>
+#include <stdint.h>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace jmoe {
+namespace {
+
+// Quantises the activation blocks of tokens [t0, t0 + ntok): eight lanes per
+// 32-value block, four blocks per warp pass; tasks are spread over the warps
+// of all CTAs that share this token tile. Same arithmetic as quant_block32.
+__device__ __forceinline__ void quantize_tile(const FwdParams &p, int t0, int ntok, int worker, int n_workers,
+                                              int lane)
+{
+    const int H = p.H, nb = H >> 5, ntask = ntok * nb;
+    const int sub = lane >> 3, l8 = lane & 7;
+    for (int base = worker * 4; base < ntask; base += n_workers * 4) {
+        const int i = base + sub;
+        const bool ok = i < ntask;
+        const int t = t0 + (ok ? i / nb : 0), b = ok ? i % nb : 0;
+        float4 v = ok ? *reinterpret_cast<const float4 *>(p.x + (size_t)t * H + 32 * b + 4 * l8)
+                      : make_float4(0.f, 0.f, 0.f, 0.f);
+        float amax = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+#pragma unroll
+        for (int o = 4; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+        amax = fmaxf(amax, 0.0f);
+        const float id = amax > 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f;
+        auto q8 = [&](float a) {
+            float r = roundf(__fmul_rn(a, id));
+            return (int)fminf(fmaxf(r, -127.0f), 127.0f);
+        };
+        const int q0 = q8(v.x), q1 = q8(v.y), q2 = q8(v.z), q3 = q8(v.w);
+        int qs = q0 + q1 + q2 + q3;
+#pragma unroll
+        for (int o = 4; o > 0; o >>= 1) qs += __shfl_xor_sync(0xffffffffu, qs, o);
+        if (ok) {
+            const uint32_t packed = (uint32_t)(q0 & 0xFF) | ((uint32_t)(q1 & 0xFF) << 8) |
+                                    ((uint32_t)(q2 & 0xFF) << 16) | ((uint32_t)(q3 & 0xFF) << 24);
+            *reinterpret_cast<uint32_t *>(p.xq + (size_t)t * H + 32 * b + 4 * l8) = packed;
+            if (l8 == 0) {
+                const float d = __fdiv_rn(amax, 127.0f);
+                p.xd[(size_t)t * nb + b] = d;
+                p.xs[(size_t)t * nb + b] = d * (float)qs;
+            }
+        }
+    }
+}
+
+// logits[t][e] = router row e . x_t in the canonical order shared with the
+// oracle: element h feeds partial (h/4) mod 32 (one lane each), every partial is
+// an fmaf chain in increasing h, and the partials are combined by the xor
+// butterfly 16, 8, 4, 2, 1; then + logit_bias[e]. Each warp owns EPW experts
+// and TT tokens of the CTA's tile; CTAs also quantise x (p.quant_x).
+template <int TT, int EPW>
+__global__ void __launch_bounds__(128) router_kernel(FwdParams p)
+{
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int e0 = (blockIdx.x * 4 + warp) * EPW;
+    const int t0 = blockIdx.y * TT;
+    const int H = p.H, E = p.E, T = p.T;
+    const int ntok = min(TT, T - t0);
+
+    if (p.quant_x) quantize_tile(p, t0, ntok, blockIdx.x * 4 + warp, gridDim.x * 4, lane);
+    if (e0 >= E) return;
+
+    float acc[TT][EPW];
+#pragma unroll
+    for (int t = 0; t < TT; t++)
+#pragma unroll
+        for (int j = 0; j < EPW; j++) acc[t][j] = 0.0f;
+
+    if ((H & 3) == 0) {
+        const int n4 = H >> 2;
+#pragma unroll 2
+        for (int h4 = lane; h4 < n4; h4 += 32) {
+            float4 w[EPW];
+#pragma unroll
+            for (int j = 0; j < EPW; j++)
+                w[j] = (e0 + j < E) ? __ldg(reinterpret_cast<const float4 *>(p.router + (size_t)(e0 + j) * H) + h4)
+                                    : make_float4(0.f, 0.f, 0.f, 0.f);
+            float4 xv[TT];
+#pragma unroll
+            for (int t = 0; t < TT; t++)
+                xv[t] = (t < ntok) ? __ldg(reinterpret_cast<const float4 *>(p.x + (size_t)(t0 + t) * H) + h4)
+                                   : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+            for (int t = 0; t < TT; t++) {
+#pragma unroll
+                for (int j = 0; j < EPW; j++) {
+                    acc[t][j] = __fmaf_rn(w[j].x, xv[t].x, acc[t][j]);
+                    acc[t][j] = __fmaf_rn(w[j].y, xv[t].y, acc[t][j]);
+                    acc[t][j] = __fmaf_rn(w[j].z, xv[t].z, acc[t][j]);
+                    acc[t][j] = __fmaf_rn(w[j].w, xv[t].w, acc[t][j]);
+                }
+            }
+        }
+    } else {
+        for (int hb = 4 * lane; hb < H; hb += 128) {
+#pragma unroll
+            for (int c = 0; c < 4; c++) {
+                const int h = hb + c;
+                if (h < H) {
+#pragma unroll
+                    for (int t = 0; t < TT; t++) {
+                        if (t < ntok) {
+                            const float xv = p.x[(size_t)(t0 + t) * H + h];
+#pragma unroll
+                            for (int j = 0; j < EPW; j++)
+                                if (e0 + j < E)
+                                    acc[t][j] = __fmaf_rn(p.router[(size_t)(e0 + j) * H + h], xv, acc[t][j]);
+                        }
+                    }
+                }
+            }
+        }
+    }
+
+#pragma unroll
+    for (int t = 0; t < TT; t++) {
+#pragma unroll
+        for (int j = 0; j < EPW; j++) {
+            float v = acc[t][j];
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
+            if (lane == 0 && t < ntok && e0 + j < E) {
+                if (p.logit_bias) v = __fadd_rn(v, p.logit_bias[e0 + j]);
+                p.logits[(size_t)(t0 + t) * E + e0 + j] = v;
+            }
+        }
+    }
+}
+
+// One warp per token: softmax over all E logits, (group-limited) top-k on the
+// total_cmp key with ties to the lower index, the weights, and the token's bit
+// in each chosen expert's mask. Semantics of select_top_k_experts and
+// select_experts_with_optional_bias (src/gemma.rs:362-442,
+// src/qwen_deepseek.rs:773-831); selection list and weights stay in registers.
+__global__ void __launch_bounds__(128) topk_kernel(FwdParams p)
+{
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int t = blockIdx.x * 4 + warp;
+    if (t >= p.T) return;
+    const int E = p.E;
+    float lg[kMaxLaneE];
+    int32_t key[kMaxLaneE];
+    bool cand[kMaxLaneE];
+#pragma unroll
+    for (int i = 0; i < kMaxLaneE; i++) {
+        const int e = lane + 32 * i;
+        const bool valid = e < E;
+        lg[i] = valid ? p.logits[(size_t)t * E + e] : 0.0f;
+        const float s = (valid && p.sel_bias) ? __fadd_rn(lg[i], p.sel_bias[e]) : lg[i];
+        key[i] = valid ? total_key(isfinite(s) ? s : -INFINITY) : INT32_MIN;
+        cand[i] = valid;
+    }
+
+    // softmax of the logits (logit_bias already added) over all E
+    float mx = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < kMaxLaneE; i++)
+        if (lane + 32 * i < E && isfinite(lg[i])) mx = fmaxf(mx, lg[i]);
+    mx = warp_max(mx);
+    float pv[kMaxLaneE];
+    float psum = 0.0f;
+#pragma unroll
+    for (int i = 0; i < kMaxLaneE; i++) {
+        const bool ok = lane + 32 * i < E && isfinite(lg[i]) && isfinite(mx);
+        pv[i] = ok ? expf(__fsub_rn(lg[i], mx)) : 0.0f;
+        psum = __fadd_rn(psum, pv[i]);
+    }
+    psum = warp_sum(psum);
+    const bool sum_ok = psum > 0.0f && isfinite(psum);
+
+    int k = min(p.k, E);
+    if (p.route_mode == 1 && p.n_groups > 0 && p.topk_groups > 0 && p.topk_groups < p.n_groups) {
+        const int G = p.n_groups, gs = E / G;
+        int32_t mykey = INT32_MIN;
+        for (int g = 0; g < G; g++) {
+            int32_t local = INT32_MIN;
+#pragma unroll
+            for (int i = 0; i < kMaxLaneE; i++) {
+                const int e = lane + 32 * i;
+                if (e < E && e / gs == g) local = max(local, key[i]);
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) local = max(local, __shfl_xor_sync(0xffffffffu, local, o));
+            if (lane == g) mykey = local;
+        }
+        uint32_t gmask = 0;
+        for (int r = 0; r < p.topk_groups; r++) {
+            const bool live = lane < G && !((gmask >> lane) & 1u);
+            int32_t bk = live ? mykey : INT32_MIN;
+            int bi = live ? lane : 0x7fffffff;
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                const int32_t ok = __shfl_xor_sync(0xffffffffu, bk, o);
+                const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+                if (oi != 0x7fffffff && (bi == 0x7fffffff || rank_before(ok, oi, bk, bi))) { bk = ok; bi = oi; }
+            }
+            gmask |= 1u << bi;
+        }
+#pragma unroll
+        for (int i = 0; i < kMaxLaneE; i++) {
+            const int e = lane + 32 * i;
+            cand[i] = cand[i] && ((gmask >> (e / gs)) & 1u);
+        }
+        k = min(k, p.topk_groups * gs);
+    }
+
+    int sel[kMaxK];
+    float w[kMaxK];
+    int nsel = 0;
+#pragma unroll
+    for (int r = 0; r < kMaxK; r++) {
+        sel[r] = -1;
+        w[r] = 0.0f;
+        if (r < k) {
+            int32_t bk = INT32_MIN;
+            int bi = 0x7fffffff;
+            float bp = 0.0f;
+#pragma unroll
+            for (int i = 0; i < kMaxLaneE; i++) {
+                const int e = lane + 32 * i;
+                if (cand[i] && (bi == 0x7fffffff || rank_before(key[i], e, bk, bi))) { bk = key[i]; bi = e; bp = pv[i]; }
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                const int32_t ok = __shfl_xor_sync(0xffffffffu, bk, o);
+                const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+                const float op = __shfl_xor_sync(0xffffffffu, bp, o);
+                if (oi != 0x7fffffff && (bi == 0x7fffffff || rank_before(ok, oi, bk, bi))) { bk = ok; bi = oi; bp = op; }
+            }
+            if (bi != 0x7fffffff) {
+                if ((bi & 31) == lane) {
+#pragma unroll
+                    for (int i = 0; i < kMaxLaneE; i++)
+                        if (i == (bi >> 5)) cand[i] = false;
+                }
+                sel[r] = bi;
+                if (p.sel_bias) w[r] = sum_ok ? __fdiv_rn(bp, psum) : 0.0f;
+                else w[r] = sum_ok ? __fdiv_rn(bp, psum) : __fdiv_rn(1.0f, (float)E);
+                nsel = r + 1;
+            }
+        }
+    }
+    if (p.sel_bias || p.normalize) {
+        float ss = 0.0f;
+#pragma unroll
+        for (int r = 0; r < kMaxK; r++)
+            if (r < nsel) ss = __fadd_rn(ss, w[r]);
+        const bool ok = ss > 0.0f && isfinite(ss);
+#pragma unroll
+        for (int r = 0; r < kMaxK; r++)
+            if (r < nsel) w[r] = ok ? __fdiv_rn(w[r], ss) : __fdiv_rn(1.0f, (float)nsel);
+    } else if (p.routed_scale != 1.0f) {
+#pragma unroll
+        for (int r = 0; r < kMaxK; r++) w[r] = __fmul_rn(w[r], p.routed_scale);
+    }
+
+    const int mw = p.mask_words;
+#pragma unroll
+    for (int r = 0; r < kMaxK; r++) {
+        if (r < p.k && lane == r) {
+            p.sel_idx[(size_t)t * p.k + r] = sel[r];
+            p.sel_w[(size_t)t * p.k + r] = sel[r] >= 0 ? w[r] : 0.0f;
+            if (sel[r] >= 0) atomicOr(p.mask + (size_t)sel[r] * mw + (t >> 5), 1u << (t & 31));
+        }
+    }
+}
+
+// Single CTA: per-expert token counts from the bit masks, slot offsets
+// (experts ascending), the list of experts that received tokens, and the
+// slot -> token permutation (tokens ascending inside an expert).
+__global__ void __launch_bounds__(1024) scan_kernel(FwdParams p)
+{
+    extern __shared__ int s_scan[];
+    int *s_count = s_scan;       // [E]
+    int *s_off = s_scan + p.E;   // [E+1]
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
+    const int E = p.E, mw = p.mask_words;
+
+    for (int e = warp; e < E; e += nwarps) {
+        int run = 0;
+        for (int c = 0; c < mw; c += 32) {
+            const int word = c + lane;
+            const uint32_t m = word < mw ? p.mask[(size_t)e * mw + word] : 0u;
+            const int pc = __popc(m);
+            int incl = pc;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int v = __shfl_up_sync(0xffffffffu, incl, o);
+                if (lane >= o) incl += v;
+            }
+            if (word < mw) p.wprefix[(size_t)e * mw + word] = run + incl - pc;
+            run += __shfl_sync(0xffffffffu, incl, 31);
+        }
+        if (lane == 0) s_count[e] = run;
+    }
+    __syncthreads();
+    if (warp == 0) {
+        const int chunk = (E + 31) / 32;
+        const int b = lane * chunk;
+        int local = 0;
+        for (int i = 0; i < chunk; i++)
+            if (b + i < E) local += s_count[b + i];
+        int incl = local;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int v = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += v;
+        }
+        int run = incl - local;
+        for (int i = 0; i < chunk; i++) {
+            if (b + i < E) {
+                s_off[b + i] = run;
+                p.offsets[b + i] = run;
+                run += s_count[b + i];
+            }
+        }
+        if (lane == 31) {
+            s_off[E] = incl;
+            p.offsets[E] = incl;
+        }
+    }
+    __syncthreads();
+    if (warp == 0) {
+        int nact = 0;
+        for (int c = 0; c < E; c += 32) {
+            const int e = c + lane;
+            const bool act = e < E && s_count[e] > 0;
+            const uint32_t bal = __ballot_sync(0xffffffffu, act);
+            const int pos = nact + __popc(bal & ((1u << lane) - 1u));
+            if (act) {
+                Problem pr;
+                pr.expert = e;
+                pr.slot0 = s_off[e];
+                pr.count = s_count[e];
+                pr.is_shared = 0;
+                p.problems[pos] = pr;
+            }
+            nact += __popc(bal);
+        }
+        if (lane == 0) {
+            *p.n_active = nact;
+            if (p.S > 0) {
+                Problem pr;
+                pr.expert = 0;
+                pr.slot0 = p.T * p.k;
+                pr.count = p.T;
+                pr.is_shared = 1;
+                p.problems[p.max_problems - 1] = pr;
+            }
+        }
+    }
+    for (int e = warp; e < E; e += nwarps) {
+        if (s_count[e] == 0) continue;
+        for (int c = 0; c < mw; c += 32) {
+            const int word = c + lane;
+            if (word < mw) {
+                uint32_t m = p.mask[(size_t)e * mw + word];
+                int pos = s_off[e] + p.wprefix[(size_t)e * mw + word];
+                while (m) {
+                    const int bit = __ffs(m) - 1;
+                    p.perm_token[pos++] = word * 32 + bit;
+                    m &= m - 1u;
+                }
+            }
+        }
+    }
+    if (p.S > 0)
+        for (int i = threadIdx.x; i < p.T; i += blockDim.x) p.perm_token[(size_t)p.T * p.k + i] = i;
+}
+
+// ------------------------------------------------------------ parity probes
+
+__global__ void quantize_rows_kernel(const float *x, int n, int cols, int8_t *xq, float *xd, float *xs)
+{
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    const int nb = cols >> 5;
+    if (warp >= n * nb) return;
+    const int r = warp / nb, b = warp % nb;
+    quant_block32(x[(size_t)r * cols + 32 * b + lane], xq + (size_t)r * cols + 32 * b, xd + (size_t)r * nb + b,
+                  xs + (size_t)r * nb + b, lane);
+}
+
+template <int FMT>
+__global__ void block_dots_kernel(DevMatrix m, const int8_t *xq, int n, int32_t *isum)
+{
+    const int nb = m.cols >> 5;
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n * nb) return;
+    const int r = i / nb, u = i % nb;
+    WUnit<FMT> w;
+    w.load(m.qs + (size_t)r * m.qs_rstride, m.meta + (size_t)r * m.meta_rstride, u);
+    isum[i] = w.isum(xq + (size_t)r * m.cols + 32 * u);
+}
+
+}  // namespace
+
+cudaError_t launch_router(const FwdParams &p, cudaStream_t st)
+{
+    if (p.T <= 256) {
+        dim3 grid((p.E + 3) / 4, (p.T + 3) / 4);
+        router_kernel<4, 1><<<grid, 128, 0, st>>>(p);
+    } else {
+        dim3 grid((p.E + 15) / 16, (p.T + 7) / 8);
+        router_kernel<8, 4><<<grid, 128, 0, st>>>(p);
+    }
+    return cudaGetLastError();
+}
+
+cudaError_t launch_topk(const FwdParams &p, cudaStream_t st)
+{
+    topk_kernel<<<(p.T + 3) / 4, 128, 0, st>>>(p);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_scan(const FwdParams &p, cudaStream_t st)
+{
+    scan_kernel<<<1, 1024, sizeof(int) * (2 * (size_t)p.E + 1), st>>>(p);
+    return cudaGetLastError();
+}
+
+int launch_quantize_rows(const float *x, int n, int cols, int8_t *xq, float *xd, float *xs, void *stream)
+{
+    const int warps = n * (cols / 32);
+    quantize_rows_kernel<<<(warps + 7) / 8, 256, 0, static_cast<cudaStream_t>(stream)>>>(x, n, cols, xq, xd, xs);
+    return cudaGetLastError();
+}
+
+int launch_block_dots(const DevMatrix &m, const int8_t *xq, int n, int32_t *isum, void *stream)
+{
+    const int tot = n * (m.cols / 32);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (m.type == FMT_Q4_K)
+        block_dots_kernel<FMT_Q4_K><<<(tot + 255) / 256, 256, 0, st>>>(m, xq, n, isum);
+    else
+        block_dots_kernel<FMT_Q8_0><<<(tot + 255) / 256, 256, 0, st>>>(m, xq, n, isum);
+    return cudaGetLastError();
+}
+
+}  // namespace jmoe

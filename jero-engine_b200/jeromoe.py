@@ -130,6 +130,7 @@ EXPORTS = {
     "moe_forward": (C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.c_void_p, C.c_void_p, C.c_void_p,
                               C.c_void_p, C.c_int32]),
     "moe_residency_summary": (C.c_int, [C.c_void_p, C.POINTER(moe_residency)]),
+    "moe_device_status": (C.c_int, [C.c_void_p, C.POINTER(C.c_int32)]),
     "moe_ctx_set_profiling": (C.c_int, [C.c_void_p, C.c_int32]),
     "moe_profile_read": (C.c_int, [C.c_void_p, C.POINTER(moe_kernel_time), C.c_int32, C.POINTER(C.c_int32),
                                    C.POINTER(C.c_int32)]),
@@ -339,7 +340,7 @@ class Context:
         """Host arrays in and out: x [T, H] f32 -> (out [T, H], sel_idx [T, k], sel_w [T, k])."""
         x = np.ascontiguousarray(x, dtype=np.float32)
         T, H = x.shape
-        k = self.layers[layer]["k"]
+        k = self.layers.get(layer, {"k": 1})["k"]   # unknown layers are rejected by the library
         out = np.empty((T, H), dtype=np.float32)
         si = np.empty((T, k), dtype=np.int32) if want_selection else None
         sw = np.empty((T, k), dtype=np.float32) if want_selection else None
@@ -350,6 +351,11 @@ class Context:
                      ptr_kind: int = PTR_DEVICE):
         _check(lib.moe_forward(self.h, layer, T, C.c_void_p(x_ptr), C.c_void_p(out_ptr),
                                C.c_void_p(sel_idx_ptr or None), C.c_void_p(sel_w_ptr or None), ptr_kind), self.h)
+
+    def device_status(self) -> int:
+        st = C.c_int32()
+        _check(lib.moe_device_status(self.h, C.byref(st)), self.h)
+        return st.value
 
     def set_profiling(self, on: bool):
         _check(lib.moe_ctx_set_profiling(self.h, int(bool(on))), self.h)

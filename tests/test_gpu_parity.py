@@ -264,10 +264,12 @@ def test_gpu_device_pointers_and_determinism():
         od = torch.empty_like(xd)
         sid = torch.empty((20, cfg.k), dtype=torch.int32, device="cuda")
         swd = torch.empty((20, cfg.k), dtype=torch.float32, device="cuda")
-        stream = torch.cuda.current_stream()
+        stream = torch.cuda.Stream()
+        stream.wait_stream(torch.cuda.current_stream())
         ctx.set_stream(stream.cuda_stream)
         ctx.forward_ptrs(0, 20, xd.data_ptr(), od.data_ptr(), sid.data_ptr(), swd.data_ptr())
         torch.cuda.synchronize()
+        ctx.set_stream(0)
     np.testing.assert_array_equal(od.cpu().numpy(), out_h)
     np.testing.assert_array_equal(sid.cpu().numpy(), si_h)
     np.testing.assert_array_equal(swd.cpu().numpy(), sw_h)
