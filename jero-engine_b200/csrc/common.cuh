@@ -1,5 +1,5 @@
 // common.cuh -- device helpers shared by the MoE kernels: ranking keys, warp
-// reductions, the activation block quantiser and the quantised weight units.
+// reductions, the activation block quantiser and the quantised block dots.
 #pragma once
 
 #include <cuda_fp16.h>
@@ -68,91 +68,80 @@ __device__ __forceinline__ void quant_block32(float v, int8_t *q_out, float *d_o
     }
 }
 
-__device__ __forceinline__ int byte_of(uint32_t a, uint32_t b, uint32_t c, int i)
+// dp4a with unsigned bytes in a and signed bytes in b.
+__device__ __forceinline__ int dp4a_us(uint32_t a, int b, int c)
 {
-    uint32_t w = i < 4 ? a : (i < 8 ? b : c);
-    return (int)((w >> (8 * (i & 3))) & 0xFFu);
+    int d;
+    asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
 }
 
-// One 32-value block of a quantised row (a Q8_0 block or a Q4_K sub-block)
-// in the device layout, held in registers and dotted against many tokens.
-// load() reads from global or shared memory through a generic pointer.
-template <int FMT>
-struct WUnit;
+// Exact int -> float for |v| < 2^22 with an integer add and a float add
+// (keeps the conversion off the slow pipe).
+__device__ __forceinline__ float i2f_small(int v)
+{
+    return __int_as_float(v + 0x4B400000) - 12582912.0f;
+}
 
-template <>
-struct WUnit<FMT_Q4_K> {
-    uint4 q;
-    float dsc, dmn;
-    __device__ __forceinline__ void load(const uint8_t *qs_row, const uint8_t *meta_row, int u)
-    {
-        q = *reinterpret_cast<const uint4 *>(qs_row + 16 * (size_t)u);
-        const uint4 m = *reinterpret_cast<const uint4 *>(meta_row + 16 * (size_t)(u >> 3));
-        const float d = __half2float(__ushort_as_half((unsigned short)(m.x & 0xFFFFu)));
-        const float dmin = __half2float(__ushort_as_half((unsigned short)(m.x >> 16)));
-        const int j = u & 7;
-        int sc, mn;
-        if (j < 4) {
-            sc = byte_of(m.y, m.z, m.w, j) & 63;
-            mn = byte_of(m.y, m.z, m.w, j + 4) & 63;
-        } else {
-            sc = (byte_of(m.y, m.z, m.w, j + 4) & 0x0F) | ((byte_of(m.y, m.z, m.w, j - 4) >> 6) << 4);
-            mn = (byte_of(m.y, m.z, m.w, j + 4) >> 4) | ((byte_of(m.y, m.z, m.w, j) >> 6) << 4);
-        }
-        dsc = d * (float)sc;
-        dmn = dmin * (float)mn;
-    }
-    __device__ __forceinline__ int isum(const int8_t *xq) const
-    {
-        const int4 a = *reinterpret_cast<const int4 *>(xq);
-        const int4 b = *reinterpret_cast<const int4 *>(xq + 16);
-        const uint32_t m4 = 0x0F0F0F0Fu;
-        int s = __dp4a((int)(q.x & m4), a.x, 0);
-        s = __dp4a((int)(q.y & m4), a.y, s);
-        s = __dp4a((int)(q.z & m4), a.z, s);
-        s = __dp4a((int)(q.w & m4), a.w, s);
-        s = __dp4a((int)((q.x >> 4) & m4), b.x, s);
-        s = __dp4a((int)((q.y >> 4) & m4), b.y, s);
-        s = __dp4a((int)((q.z >> 4) & m4), b.z, s);
-        s = __dp4a((int)((q.w >> 4) & m4), b.w, s);
-        return s;
-    }
-    __device__ __forceinline__ float dot(const int8_t *xq, float xd, float xs) const
-    {
-        return xd * (dsc * (float)isum(xq)) - xs * dmn;
-    }
+// ---- Q4_K sub-block (32 values, 16 bytes of nibbles in the device layout:
+// byte b = value b (low nibble) | value 16 + b (high nibble)) ----
+
+// Nibbles of one sub-block prepared once for many tokens: lo holds values
+// 0..15 as bytes, hi16 values 16..31 times 16 (the high nibble left in place).
+struct Q4Nib {
+    uint32_t lo[4], hi16[4];
 };
 
-template <>
-struct WUnit<FMT_Q8_0> {
-    uint4 q0, q1;
-    float d;
-    __device__ __forceinline__ void load(const uint8_t *qs_row, const uint8_t *meta_row, int u)
-    {
-        const uint4 *src = reinterpret_cast<const uint4 *>(qs_row + 32 * (size_t)u);
-        q0 = src[0];
-        q1 = src[1];
-        d = __half2float(__ushort_as_half(reinterpret_cast<const unsigned short *>(meta_row)[u]));
-    }
-    __device__ __forceinline__ int isum(const int8_t *xq) const
-    {
-        const int4 a = *reinterpret_cast<const int4 *>(xq);
-        const int4 b = *reinterpret_cast<const int4 *>(xq + 16);
-        int s = __dp4a((int)q0.x, a.x, 0);
-        s = __dp4a((int)q0.y, a.y, s);
-        s = __dp4a((int)q0.z, a.z, s);
-        s = __dp4a((int)q0.w, a.w, s);
-        s = __dp4a((int)q1.x, b.x, s);
-        s = __dp4a((int)q1.y, b.y, s);
-        s = __dp4a((int)q1.z, b.z, s);
-        s = __dp4a((int)q1.w, b.w, s);
-        return s;
-    }
-    __device__ __forceinline__ float dot(const int8_t *xq, float xd, float xs) const
-    {
-        return (d * xd) * (float)isum(xq);
-    }
-};
+__device__ __forceinline__ Q4Nib q4_nibbles(uint4 q)
+{
+    Q4Nib n;
+    n.lo[0] = q.x & 0x0F0F0F0Fu; n.hi16[0] = q.x & 0xF0F0F0F0u;
+    n.lo[1] = q.y & 0x0F0F0F0Fu; n.hi16[1] = q.y & 0xF0F0F0F0u;
+    n.lo[2] = q.z & 0x0F0F0F0Fu; n.hi16[2] = q.z & 0xF0F0F0F0u;
+    n.lo[3] = q.w & 0x0F0F0F0Fu; n.hi16[3] = q.w & 0xF0F0F0F0u;
+    return n;
+}
+
+// 16 * sum(q * x) over the sub-block; a holds x[0..15], b holds x[16..31].
+__device__ __forceinline__ int q4_isum16(const Q4Nib &n, int4 a, int4 b)
+{
+    int lo = dp4a_us(n.lo[0], a.x, 0);
+    int hi = dp4a_us(n.hi16[0], b.x, 0);
+    lo = dp4a_us(n.lo[1], a.y, lo);
+    hi = dp4a_us(n.hi16[1], b.y, hi);
+    lo = dp4a_us(n.lo[2], a.z, lo);
+    hi = dp4a_us(n.hi16[2], b.z, hi);
+    lo = dp4a_us(n.lo[3], a.w, lo);
+    hi = dp4a_us(n.hi16[3], b.w, hi);
+    return lo * 16 + hi;
+}
+
+// Q4_K scale and min of sub-block j from the device meta (16 bytes per
+// super-block: f16 d, f16 dmin, then eight 12-bit fields sc_j | m_j << 6 at
+// bit 12j of the remaining 96 bits). Returns (d*sc_j/16, dmin*m_j).
+__device__ __forceinline__ float2 q4_scales(uint4 m, int j)
+{
+    const int bit = 12 * j, wi = bit >> 5, sh = bit & 31;
+    const uint32_t lo = wi == 0 ? m.y : (wi == 1 ? m.z : m.w);
+    const uint32_t hi = wi == 0 ? m.z : (wi == 1 ? m.w : 0u);
+    const uint32_t f = __funnelshift_r(lo, hi, sh) & 0xFFFu;
+    const float2 dd = __half22float2(*reinterpret_cast<const __half2 *>(&m.x));
+    return make_float2(dd.x * (float)(f & 63u) * 0.0625f, dd.y * (float)(f >> 6));
+}
+
+// ---- Q8_0 block (32 signed bytes, f16 scale) ----
+__device__ __forceinline__ int q8_isum(uint4 q0, uint4 q1, int4 a, int4 b)
+{
+    int s0 = __dp4a((int)q0.x, a.x, 0);
+    int s1 = __dp4a((int)q1.x, b.x, 0);
+    s0 = __dp4a((int)q0.y, a.y, s0);
+    s1 = __dp4a((int)q1.y, b.y, s1);
+    s0 = __dp4a((int)q0.z, a.z, s0);
+    s1 = __dp4a((int)q1.z, b.z, s1);
+    s0 = __dp4a((int)q0.w, a.w, s0);
+    s1 = __dp4a((int)q1.w, b.w, s1);
+    return s0 + s1;
+}
 
 // SiLU(g) * u with silu(g) = g / (1 + exp(-g)), each operation rounded (the oracle's form).
 __device__ __forceinline__ float swiglu(float g, float u)

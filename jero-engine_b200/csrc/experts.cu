@@ -2,11 +2,17 @@
 //
 // Quantised experts run as weight-streaming kernels: the HBM traffic of a
 // decode-sized MoE layer is the weight rows of the routed experts, read once.
-// Each CTA owns a contiguous range of work items (problem, 32- or 64-row tile);
-// a producer warp streams the tiles' weight chunks into a shared-memory ring
-// with bulk async copies (cp.async.bulk, completion on mbarriers) while eight
-// consumer warps dot them against the problem's int8 activation blocks, which
-// sit in shared memory. The copy stream does not stop between work items.
+// A work item is (problem, 32-row tile); each CTA owns a contiguous range of
+// items. A producer warp streams each item's rows, one K-slice at a time, into
+// a shared-memory ring with bulk async copies (cp.async.bulk, one per row and
+// matrix, completing on an mbarrier), while eight consumer warps dot them
+// against the problem's int8 activation blocks held in shared memory. The copy
+// stream does not stop between items.
+//
+// Consumer mapping: warp w owns rows 4w..4w+3 of the tile, 8 lanes per row;
+// lane l8 takes the 32-value units l8, l8+8, ... of the slice, so a lane always
+// sees the same Q4_K sub-block index (l8) and the 8 lanes of a row read 128
+// contiguous bytes. Activation loads are broadcast to the 4 rows of a warp.
 #include <cuda_runtime.h>
 #include <math.h>
 #include <stdint.h>
@@ -21,9 +27,8 @@ namespace {
 constexpr int kConsumerWarps = 8;
 constexpr int kConsumers = kConsumerWarps * 32;
 constexpr int kStreamThreads = kConsumers + 32;
-constexpr int kGuChunkRows = 8, kGuItemRows = 32;    // gate/up: one warp per row, 32 lanes
-constexpr int kDnChunkRows = 16, kDnItemRows = 64;   // down: two rows per warp, 16 lanes each
-constexpr long long kWaitCycles = 4000000000LL;      // ~2 s: a wait that long means a fault
+constexpr int kRows = 32;                           // rows per work item and per chunk
+constexpr long long kWaitCycles = 4000000000LL;     // ~2 s: a wait that long means a fault
 constexpr int kRingBudget = 80 * 1024;
 constexpr int kErrTimeout = 1;
 
@@ -64,28 +69,32 @@ __device__ __forceinline__ Item item_at(const FwdParams &p, const StreamCfg &c, 
     return x;
 }
 
+// Shared memory: ring [stages][stage_bytes] | xq int4 [kTT][2][act_k/32] |
+// xds float2 [kTT][act_k/32] | g, u [kTT][32] f32 | full[stages], empty[stages] | abort.
 struct Smem {
     uint8_t *ring;
-    int8_t *xq;
-    float *xd, *xs, *g, *u;
+    int4 *xq;
+    float2 *xds;
+    float *g, *u;
     uint64_t *full, *empty;
     volatile int *abort_flag;
 };
 
 __host__ __device__ inline size_t smem_bytes(const StreamCfg &c)
 {
-    return (size_t)c.stages * c.stage_bytes + (size_t)kTT * c.act_k + 2 * (size_t)kTT * (c.act_k / 32) * 4 +
-           2 * (size_t)kTT * 32 * 4 + 16 * (size_t)c.stages + 16;
+    const size_t nu = (size_t)c.act_k / 32;
+    return (size_t)c.stages * c.stage_bytes + (size_t)kTT * nu * 32 + (size_t)kTT * nu * 8 + 2 * (size_t)kTT * 32 * 4 +
+           16 * (size_t)c.stages + 16;
 }
 
 __device__ __forceinline__ Smem carve(uint8_t *base, const StreamCfg &c)
 {
+    const int nu = c.act_k / 32;
     Smem s;
     s.ring = base;
-    s.xq = reinterpret_cast<int8_t *>(base + (size_t)c.stages * c.stage_bytes);
-    s.xd = reinterpret_cast<float *>(s.xq + (size_t)kTT * c.act_k);
-    s.xs = s.xd + kTT * (c.act_k / 32);
-    s.g = s.xs + kTT * (c.act_k / 32);
+    s.xq = reinterpret_cast<int4 *>(base + (size_t)c.stages * c.stage_bytes);
+    s.xds = reinterpret_cast<float2 *>(s.xq + (size_t)kTT * 2 * nu);
+    s.g = reinterpret_cast<float *>(s.xds + (size_t)kTT * nu);
     s.u = s.g + kTT * 32;
     s.full = reinterpret_cast<uint64_t *>(s.u + kTT * 32);
     s.empty = s.full + c.stages;
@@ -117,73 +126,225 @@ __device__ __forceinline__ void drain(const Smem &s, int stages, uint32_t g)
     }
 }
 
-// Activation blocks of nt rows into shared memory: q [kTT][K] int8 and the
-// per-block scale d and d*sum(q). Rows come from perm (token ids) or are
-// consecutive slots starting at row0.
-__device__ __forceinline__ void stage_act(const Smem &s, const int8_t *gq, const float *gd, const float *gs,
+// Stages the activation blocks of nt rows: xq as [t][half][unit] 16-byte
+// halves (so eight lanes reading eight consecutive units touch 128 contiguous
+// bytes) and (d, d*sum q) pairs as [t][unit]. Rows are token ids from perm,
+// or consecutive slots from row0 when perm is null.
+__device__ __forceinline__ void stage_act(const Smem &s, int nu_s, const int8_t *gq, const float *gd, const float *gs,
                                           size_t q_stride, size_t d_stride, const int32_t *perm, int row0, int nt,
                                           int K)
 {
-    const int nv = K >> 4, nb = K >> 5;
-    for (int v = threadIdx.x; v < nt * nv; v += kConsumers) {
-        const int i = v / nv, c = v % nv;
+    const int nu = K >> 5;
+    for (int v = threadIdx.x; v < nt * nu * 2; v += kConsumers) {
+        const int i = v / (2 * nu), rem = v % (2 * nu), u = rem >> 1, h = rem & 1;
         const size_t row = perm ? (size_t)perm[row0 + i] : (size_t)(row0 + i);
-        reinterpret_cast<uint4 *>(s.xq + (size_t)i * K)[c] = __ldg(reinterpret_cast<const uint4 *>(gq + row * q_stride) + c);
+        s.xq[((size_t)i * 2 + h) * nu_s + u] = __ldg(reinterpret_cast<const int4 *>(gq + row * q_stride) + 2 * u + h);
     }
-    for (int v = threadIdx.x; v < nt * nb; v += kConsumers) {
-        const int i = v / nb, c = v % nb;
+    for (int v = threadIdx.x; v < nt * nu; v += kConsumers) {
+        const int i = v / nu, u = v % nu;
         const size_t row = perm ? (size_t)perm[row0 + i] : (size_t)(row0 + i);
-        s.xd[i * nb + c] = __ldg(gd + row * d_stride + c);
-        s.xs[i * nb + c] = __ldg(gs + row * d_stride + c);
+        s.xds[(size_t)i * nu_s + u] = make_float2(__ldg(gd + row * d_stride + u), __ldg(gs + row * d_stride + u));
     }
 }
 
-// ---------------------------------------------------------------- gate/up
+// Producer: per chunk (item, token tile, K-slice) lane 0 arms the stage's
+// mbarrier with the byte count, then lane r copies row r of every matrix.
+struct SliceSrc {
+    const uint8_t *qs, *meta;   // expert slab bases
+    size_t qs_rs, meta_rs;      // global row strides
+};
 
-template <int FMT>
-__global__ void __launch_bounds__(kStreamThreads, 2) gate_up_stream_kernel(FwdParams p, LayerDev L, StreamCfg c)
+__device__ __forceinline__ void produce_chunk(const Smem &s, const StreamCfg &c, int st, const SliceSrc *src, int nmat,
+                                              int r0, int nrow, int sl, int ks_cur, int fmt, int lane)
+{
+    // bytes of one row's slice
+    const uint32_t qsz = fmt == FMT_Q4_K ? (uint32_t)ks_cur / 2 : (uint32_t)ks_cur;
+    const uint32_t msz = fmt == FMT_Q4_K ? (uint32_t)(ks_cur / 256) * 16 : (uint32_t)(((ks_cur / 32) * 2 + 15) & ~15);
+    const size_t qoff = fmt == FMT_Q4_K ? (size_t)sl * c.ks / 2 : (size_t)sl * c.ks;
+    const size_t moff = fmt == FMT_Q4_K ? (size_t)sl * (c.ks / 256) * 16 : (size_t)sl * (c.ks / 32) * 2;
+    if (lane == 0) mbar_arrive_expect_tx(&s.full[st], (uint32_t)nmat * nrow * (qsz + msz));
+    __syncwarp();
+    if (lane < nrow) {
+        uint8_t *stage = s.ring + (size_t)st * c.stage_bytes;
+        for (int m = 0; m < nmat; m++) {
+            uint8_t *dq = stage + (size_t)m * kRows * (c.qs_row + c.meta_row);
+            uint8_t *dm = dq + (size_t)kRows * c.qs_row;
+            const size_t row = (size_t)r0 + lane;
+            bulk_g2s(dq + (size_t)lane * c.qs_row, src[m].qs + row * src[m].qs_rs + qoff, qsz, &s.full[st]);
+            bulk_g2s(dm + (size_t)lane * c.meta_row, src[m].meta + row * src[m].meta_rs + moff, msz, &s.full[st]);
+        }
+    }
+}
+
+// Dots of one chunk: NMAT matrices (gate/up or down), NT tokens. acc[m][t]
+// accumulates the lane's partial sums over the units it owns.
+template <int FMT, int NMAT, int NT>
+__device__ __forceinline__ void consume_chunk(const Smem &s, const StreamCfg &c, const uint8_t *stage, int rw, int l8,
+                                              int nu_slice, int ubase, int nu_s, float (&acc)[NMAT][NT])
+{
+    const uint8_t *q[NMAT], *mt[NMAT];
+#pragma unroll
+    for (int m = 0; m < NMAT; m++) {
+        q[m] = stage + (size_t)m * kRows * (c.qs_row + c.meta_row) + (size_t)rw * c.qs_row;
+        mt[m] = stage + (size_t)m * kRows * (c.qs_row + c.meta_row) + (size_t)kRows * c.qs_row + (size_t)rw * c.meta_row;
+    }
+    for (int u = l8; u < nu_slice; u += 8) {
+        const int ug = ubase + u;
+        if (FMT == FMT_Q4_K) {
+            Q4Nib nb[NMAT];
+            float2 sc[NMAT];
+#pragma unroll
+            for (int m = 0; m < NMAT; m++) {
+                nb[m] = q4_nibbles(*reinterpret_cast<const uint4 *>(q[m] + 16 * u));
+                sc[m] = q4_scales(*reinterpret_cast<const uint4 *>(mt[m] + 16 * (u >> 3)), l8);
+            }
+#pragma unroll
+            for (int t = 0; t < NT; t++) {
+                const int4 a = s.xq[((size_t)t * 2) * nu_s + ug];
+                const int4 b = s.xq[((size_t)t * 2 + 1) * nu_s + ug];
+                const float2 ds = s.xds[(size_t)t * nu_s + ug];
+#pragma unroll
+                for (int m = 0; m < NMAT; m++) {
+                    const float f = i2f_small(q4_isum16(nb[m], a, b));
+                    acc[m][t] = fmaf(f, ds.x * sc[m].x, acc[m][t]);
+                    acc[m][t] = fmaf(-ds.y, sc[m].y, acc[m][t]);
+                }
+            }
+        } else {
+            uint4 q0[NMAT], q1[NMAT];
+            float d[NMAT];
+#pragma unroll
+            for (int m = 0; m < NMAT; m++) {
+                q0[m] = *reinterpret_cast<const uint4 *>(q[m] + 32 * u);
+                q1[m] = *reinterpret_cast<const uint4 *>(q[m] + 32 * u + 16);
+                d[m] = __half2float(*reinterpret_cast<const __half *>(mt[m] + 2 * u));
+            }
+#pragma unroll
+            for (int t = 0; t < NT; t++) {
+                const int4 a = s.xq[((size_t)t * 2) * nu_s + ug];
+                const int4 b = s.xq[((size_t)t * 2 + 1) * nu_s + ug];
+                const float xd = s.xds[(size_t)t * nu_s + ug].x;
+#pragma unroll
+                for (int m = 0; m < NMAT; m++)
+                    acc[m][t] = fmaf(i2f_small(q8_isum(q0[m], q1[m], a, b)), d[m] * xd, acc[m][t]);
+            }
+        }
+    }
+}
+
+// Consumer side of one (item, token tile) with NT tokens: all K-slices of the
+// 32-row tile, then the 8-lane reduction. Returns false when a wait gave up.
+template <int FMT, int NMAT, int NT>
+__device__ __forceinline__ bool consume_tile(const Smem &s, const StreamCfg &c, uint32_t &g, int K, int nu_s,
+                                             int *err, float (&out)[NMAT][NT], int rw,
+                                             int l8)
+{
+    float acc[NMAT][NT];
+#pragma unroll
+    for (int m = 0; m < NMAT; m++)
+#pragma unroll
+        for (int t = 0; t < NT; t++) acc[m][t] = 0.0f;
+    const int ns = (K + c.ks - 1) / c.ks;
+    for (int sl = 0; sl < ns; sl++) {
+        const int st = g % c.stages;
+        if (!wait_bar(&s.full[st], (g / c.stages) & 1, s.abort_flag, err)) return false;
+        const int ks_cur = min(c.ks, K - sl * c.ks);
+        consume_chunk<FMT, NMAT, NT>(s, c, s.ring + (size_t)st * c.stage_bytes, rw, l8, ks_cur >> 5, sl * (c.ks >> 5),
+                                     nu_s, acc);
+        __syncwarp();
+        if ((threadIdx.x & 31) == 0) mbar_arrive(&s.empty[st]);
+        g++;
+    }
+#pragma unroll
+    for (int m = 0; m < NMAT; m++)
+#pragma unroll
+        for (int t = 0; t < NT; t++) {
+            float v = acc[m][t];
+            v += __shfl_xor_sync(0xffffffffu, v, 4);
+            v += __shfl_xor_sync(0xffffffffu, v, 2);
+            v += __shfl_xor_sync(0xffffffffu, v, 1);
+            out[m][t] = v;
+        }
+    return true;
+}
+
+// Gate/up epilogue for NT tokens: the row-group leaders publish g and u.
+template <int NT>
+__device__ __forceinline__ void publish_gu(const Smem &s, const float (&o)[2][NT], int nt, int row, int l8)
+{
+    if (l8 == 0) {
+#pragma unroll
+        for (int t = 0; t < NT; t++)
+            if (t < nt) {
+                s.g[t * 32 + row] = o[0][t];
+                s.u[t * 32 + row] = o[1][t];
+            }
+    }
+}
+
+template <int NT>
+__device__ __forceinline__ void publish_y(const FwdParams &p, const float (&o)[1][NT], int nt, size_t slot0, int row,
+                                          int l8)
+{
+    if (l8 == 0) {
+#pragma unroll
+        for (int t = 0; t < NT; t++)
+            if (t < nt) p.y[(slot0 + t) * p.H + row] = o[0][t];
+    }
+}
+
+// ---------------------------------------------------------- the kernels
+
+// NMAT == 2: gate and up (rows of I or S, K = H), epilogue a = silu(g) * u
+// quantised per 32 rows. NMAT == 1: down (rows of H, K = I or S), y written.
+template <int FMT, int NMAT>
+__global__ void __launch_bounds__(kStreamThreads, 2) expert_stream_kernel(FwdParams p, LayerDev L, StreamCfg c)
 {
     extern __shared__ __align__(128) uint8_t smem_raw[];
     const Smem s = carve(smem_raw, c);
-    const int S = c.stages;
-    init_ring(s, S);
+    init_ring(s, c.stages);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int nr = c.mode == 1 ? 0 : *p.n_active;
     const int total = nr * c.rt_routed + ((c.mode != 0 && p.S > 0) ? c.rt_shared : 0);
     const int it0 = (int)((long long)blockIdx.x * total / gridDim.x);
     const int it1 = (int)((long long)(blockIdx.x + 1) * total / gridDim.x);
-    constexpr int CR = kGuChunkRows, IR = kGuItemRows;
 
-    if (warp == kConsumerWarps) {   // producer
-        if (lane != 0) return;
+    if (warp == kConsumerWarps) {   // producer warp
         uint32_t g = 0;
         for (int it = it0; it < it1; it++) {
             const Item x = item_at(p, c, nr, it);
-            const DevMatrix &G = x.shared ? L.sh_gate : L.gate;
-            const DevMatrix &U = x.shared ? L.sh_up : L.up;
-            const size_t qsr = G.qs_rstride, mr = G.meta_rstride;
-            const uint8_t *gq = G.qs + (size_t)x.pr.expert * G.qs_estride;
-            const uint8_t *gm = G.meta + (size_t)x.pr.expert * G.meta_estride;
-            const uint8_t *uq = U.qs + (size_t)x.pr.expert * U.qs_estride;
-            const uint8_t *um = U.meta + (size_t)x.pr.expert * U.meta_estride;
-            const int r0 = x.rt * IR, nrow = min(IR, G.rows - r0), nch = (nrow + CR - 1) / CR;
-            const int tiles = (x.pr.count + kTT - 1) / kTT;
+            SliceSrc src[NMAT];
+            int K, rows;
+            if (NMAT == 2) {
+                const DevMatrix &G = x.shared ? L.sh_gate : L.gate;
+                const DevMatrix &U = x.shared ? L.sh_up : L.up;
+                src[0] = {G.qs + (size_t)x.pr.expert * G.qs_estride, G.meta + (size_t)x.pr.expert * G.meta_estride,
+                          G.qs_rstride, G.meta_rstride};
+                src[NMAT - 1] = {U.qs + (size_t)x.pr.expert * U.qs_estride,
+                                 U.meta + (size_t)x.pr.expert * U.meta_estride, U.qs_rstride, U.meta_rstride};
+                K = G.cols;
+                rows = G.rows;
+            } else {
+                const DevMatrix &D = x.shared ? L.sh_down : L.down;
+                src[0] = {D.qs + (size_t)x.pr.expert * D.qs_estride, D.meta + (size_t)x.pr.expert * D.meta_estride,
+                          D.qs_rstride, D.meta_rstride};
+                K = D.cols;
+                rows = D.rows;
+            }
+            const int r0 = x.rt * kRows, nrow = min(kRows, rows - r0);
+            const int tiles = (x.pr.count + kTT - 1) / kTT, ns = (K + c.ks - 1) / c.ks;
             for (int tt = 0; tt < tiles; tt++) {
-                for (int ch = 0; ch < nch; ch++) {
-                    const int st = g % S;
-                    const uint32_t use = g / S;
-                    if (use > 0 && !wait_bar(&s.empty[st], (use - 1) & 1, s.abort_flag, p.err)) {
-                        drain(s, S, g);
+                for (int sl = 0; sl < ns; sl++) {
+                    const int st = g % c.stages;
+                    const uint32_t use = g / c.stages;
+                    int ok = 1;
+                    if (use > 0 && lane == 0) ok = wait_bar(&s.empty[st], (use - 1) & 1, s.abort_flag, p.err);
+                    ok = __shfl_sync(0xffffffffu, ok, 0);
+                    if (!ok) {
+                        if (lane == 0) drain(s, c.stages, g);
                         return;
                     }
-                    const size_t rr = (size_t)r0 + ch * CR;
-                    const uint32_t qb = (uint32_t)(CR * qsr), mb = (uint32_t)(CR * mr);
-                    uint8_t *dst = s.ring + (size_t)st * c.stage_bytes;
-                    mbar_arrive_expect_tx(&s.full[st], 2 * (qb + mb));
-                    bulk_g2s(dst, gq + rr * qsr, qb, &s.full[st]);
-                    bulk_g2s(dst + qb, gm + rr * mr, mb, &s.full[st]);
-                    bulk_g2s(dst + qb + mb, uq + rr * qsr, qb, &s.full[st]);
-                    bulk_g2s(dst + 2 * qb + mb, um + rr * mr, mb, &s.full[st]);
+                    produce_chunk(s, c, st, src, NMAT, r0, nrow, sl, min(c.ks, K - sl * c.ks), FMT, lane);
                     g++;
                 }
             }
@@ -194,181 +355,73 @@ __global__ void __launch_bounds__(kStreamThreads, 2) gate_up_stream_kernel(FwdPa
     // consumers
     uint32_t g = 0;
     int staged_slot = -1, staged_tile = -1;
-    const int H = p.H;
+    const int rw = warp * 4 + (lane >> 3), l8 = lane & 7;
+    const int nu_s = c.act_k >> 5;
     for (int it = it0; it < it1; it++) {
         const Item x = item_at(p, c, nr, it);
-        const DevMatrix &G = x.shared ? L.sh_gate : L.gate;
-        const int K = G.cols, NU = K >> 5;
-        const size_t qsr = G.qs_rstride, mr = G.meta_rstride;
-        const int r0 = x.rt * IR, nrow = min(IR, G.rows - r0), nch = (nrow + CR - 1) / CR;
-        const int tiles = (x.pr.count + kTT - 1) / kTT;
-        const int down_f32 = c.down_f32;
-        for (int tt = 0; tt < tiles; tt++) {
-            const int t0 = tt * kTT, nt = min(kTT, x.pr.count - t0);
-            if (staged_slot != x.pr.slot0 || staged_tile != tt) {
-                named_bar(1, kConsumers);
-                stage_act(s, p.xq, p.xd, p.xs, (size_t)H, (size_t)(H >> 5), p.perm_token, x.pr.slot0 + t0, nt, K);
-                named_bar(1, kConsumers);
-                staged_slot = x.pr.slot0;
-                staged_tile = tt;
-            }
-            for (int ch = 0; ch < nch; ch++) {
-                const int st = g % S;
-                if (!wait_bar(&s.full[st], (g / S) & 1, s.abort_flag, p.err)) return;
-                const uint8_t *base = s.ring + (size_t)st * c.stage_bytes;
-                const int rl = ch * CR + warp;
-                float ag[kTT], au[kTT];
-#pragma unroll
-                for (int t = 0; t < kTT; t++) { ag[t] = 0.0f; au[t] = 0.0f; }
-                if (rl < nrow) {
-                    const size_t qb = CR * qsr, mb = CR * mr;
-                    const uint8_t *gqr = base + warp * qsr, *gmr = base + qb + warp * mr;
-                    const uint8_t *uqr = base + qb + mb + warp * qsr, *umr = base + 2 * qb + mb + warp * mr;
-                    for (int u = lane; u < NU; u += 32) {
-                        WUnit<FMT> wg, wu;
-                        wg.load(gqr, gmr, u);
-                        wu.load(uqr, umr, u);
-#pragma unroll
-                        for (int t = 0; t < kTT; t++) {
-                            if (t < nt) {
-                                const int8_t *xq = s.xq + (size_t)t * K + 32 * u;
-                                const float xd = s.xd[t * NU + u], xs = s.xs[t * NU + u];
-                                ag[t] += wg.dot(xq, xd, xs);
-                                au[t] += wu.dot(xq, xd, xs);
-                            }
-                        }
-                    }
-                }
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&s.empty[st]);
-                g++;
-#pragma unroll
-                for (int t = 0; t < kTT; t++) {
-                    float a = ag[t], b = au[t];
-#pragma unroll
-                    for (int o = 16; o > 0; o >>= 1) {
-                        a += __shfl_xor_sync(0xffffffffu, a, o);
-                        b += __shfl_xor_sync(0xffffffffu, b, o);
-                    }
-                    if (lane == 0 && t < nt && rl < nrow) {
-                        s.g[t * 32 + rl] = a;
-                        s.u[t * 32 + rl] = b;
-                    }
-                }
-            }
-            named_bar(1, kConsumers);
-            if (warp < nt) {
-                const size_t slot = (size_t)x.pr.slot0 + t0 + warp;
-                const float a = lane < nrow ? swiglu(s.g[warp * 32 + lane], s.u[warp * 32 + lane]) : 0.0f;
-                if (down_f32) {
-                    if (lane < nrow) p.af[slot * p.W + r0 + lane] = a;
-                } else {
-                    quant_block32(a, p.aq + slot * p.W + r0, p.ad + slot * (p.W >> 5) + (r0 >> 5),
-                                  p.as + slot * (p.W >> 5) + (r0 >> 5), lane);
-                }
-            }
-            named_bar(1, kConsumers);
-        }
-    }
-}
-
-// ------------------------------------------------------------------- down
-
-template <int FMT>
-__global__ void __launch_bounds__(kStreamThreads, 2) down_stream_kernel(FwdParams p, LayerDev L, StreamCfg c)
-{
-    extern __shared__ __align__(128) uint8_t smem_raw[];
-    const Smem s = carve(smem_raw, c);
-    const int S = c.stages;
-    init_ring(s, S);
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int nr = c.mode == 1 ? 0 : *p.n_active;
-    const int total = nr * c.rt_routed + ((c.mode != 0 && p.S > 0) ? c.rt_shared : 0);
-    const int it0 = (int)((long long)blockIdx.x * total / gridDim.x);
-    const int it1 = (int)((long long)(blockIdx.x + 1) * total / gridDim.x);
-    constexpr int CR = kDnChunkRows, IR = kDnItemRows;
-
-    if (warp == kConsumerWarps) {
-        if (lane != 0) return;
-        uint32_t g = 0;
-        for (int it = it0; it < it1; it++) {
-            const Item x = item_at(p, c, nr, it);
+        int K, rows;
+        if (NMAT == 2) {
+            const DevMatrix &G = x.shared ? L.sh_gate : L.gate;
+            K = G.cols;
+            rows = G.rows;
+        } else {
             const DevMatrix &D = x.shared ? L.sh_down : L.down;
-            const size_t qsr = D.qs_rstride, mr = D.meta_rstride;
-            const uint8_t *dq = D.qs + (size_t)x.pr.expert * D.qs_estride;
-            const uint8_t *dm = D.meta + (size_t)x.pr.expert * D.meta_estride;
-            const int r0 = x.rt * IR, nrow = min(IR, D.rows - r0), nch = (nrow + CR - 1) / CR;
-            const int tiles = (x.pr.count + kTT - 1) / kTT;
-            for (int tt = 0; tt < tiles; tt++) {
-                for (int ch = 0; ch < nch; ch++) {
-                    const int st = g % S;
-                    const uint32_t use = g / S;
-                    if (use > 0 && !wait_bar(&s.empty[st], (use - 1) & 1, s.abort_flag, p.err)) {
-                        drain(s, S, g);
-                        return;
-                    }
-                    const size_t rr = (size_t)r0 + ch * CR;
-                    const uint32_t qb = (uint32_t)(CR * qsr), mb = (uint32_t)(CR * mr);
-                    uint8_t *dst = s.ring + (size_t)st * c.stage_bytes;
-                    mbar_arrive_expect_tx(&s.full[st], qb + mb);
-                    bulk_g2s(dst, dq + rr * qsr, qb, &s.full[st]);
-                    bulk_g2s(dst + qb, dm + rr * mr, mb, &s.full[st]);
-                    g++;
-                }
-            }
+            K = D.cols;
+            rows = D.rows;
         }
-        return;
-    }
-
-    uint32_t g = 0;
-    int staged_slot = -1, staged_tile = -1;
-    const int half = lane >> 4, hl = lane & 15;
-    for (int it = it0; it < it1; it++) {
-        const Item x = item_at(p, c, nr, it);
-        const DevMatrix &D = x.shared ? L.sh_down : L.down;
-        const int K = D.cols, NU = K >> 5;
-        const size_t qsr = D.qs_rstride, mr = D.meta_rstride;
-        const int r0 = x.rt * IR, nrow = min(IR, D.rows - r0), nch = (nrow + CR - 1) / CR;
+        const int r0 = x.rt * kRows, nrow = min(kRows, rows - r0);
         const int tiles = (x.pr.count + kTT - 1) / kTT;
         for (int tt = 0; tt < tiles; tt++) {
             const int t0 = tt * kTT, nt = min(kTT, x.pr.count - t0);
             if (staged_slot != x.pr.slot0 || staged_tile != tt) {
                 named_bar(1, kConsumers);
-                stage_act(s, p.aq, p.ad, p.as, (size_t)p.W, (size_t)(p.W >> 5), nullptr, x.pr.slot0 + t0, nt, K);
+                if (NMAT == 2)
+                    stage_act(s, nu_s, p.xq, p.xd, p.xs, (size_t)p.H, (size_t)(p.H >> 5), p.perm_token,
+                              x.pr.slot0 + t0, nt, K);
+                else
+                    stage_act(s, nu_s, p.aq, p.ad, p.as, (size_t)p.W, (size_t)(p.W >> 5), nullptr, x.pr.slot0 + t0, nt,
+                              K);
                 named_bar(1, kConsumers);
                 staged_slot = x.pr.slot0;
                 staged_tile = tt;
             }
-            for (int ch = 0; ch < nch; ch++) {
-                const int st = g % S;
-                if (!wait_bar(&s.full[st], (g / S) & 1, s.abort_flag, p.err)) return;
-                const uint8_t *base = s.ring + (size_t)st * c.stage_bytes;
-                const int rw = 2 * warp + half;        // row within the chunk
-                const int rl = ch * CR + rw;           // row within the item
-                float acc[kTT];
-#pragma unroll
-                for (int t = 0; t < kTT; t++) acc[t] = 0.0f;
-                if (rl < nrow) {
-                    const uint8_t *qr = base + rw * qsr, *mrow = base + CR * qsr + rw * mr;
-                    for (int u = hl; u < NU; u += 16) {
-                        WUnit<FMT> w;
-                        w.load(qr, mrow, u);
-#pragma unroll
-                        for (int t = 0; t < kTT; t++)
-                            if (t < nt) acc[t] += w.dot(s.xq + (size_t)t * K + 32 * u, s.xd[t * NU + u], s.xs[t * NU + u]);
+            const bool row_ok = rw < nrow;
+            bool ok = true;
+            const size_t slot0 = (size_t)x.pr.slot0 + t0;
+#define JMOE_TILE(NTV)                                                                                   \
+    {                                                                                                    \
+        float o[NMAT][NTV];                                                                              \
+        ok = consume_tile<FMT, NMAT, NTV>(s, c, g, K, nu_s, p.err, o, rw, l8);                           \
+        if (ok && row_ok) {                                                                              \
+            if constexpr (NMAT == 2) publish_gu<NTV>(s, o, nt, rw, l8);                                  \
+            else publish_y<NTV>(p, o, nt, slot0, r0 + rw, l8);                                           \
+        }                                                                                                \
+    }
+            switch (nt) {
+            case 1: JMOE_TILE(1) break;
+            case 2: JMOE_TILE(2) break;
+            case 3: JMOE_TILE(3) break;
+            case 4: JMOE_TILE(4) break;
+            case 5: JMOE_TILE(5) break;
+            case 6: JMOE_TILE(6) break;
+            case 7: JMOE_TILE(7) break;
+            default: JMOE_TILE(8) break;
+            }
+#undef JMOE_TILE
+            if (!ok) return;
+            if (NMAT == 2) {
+                named_bar(1, kConsumers);
+                if (warp < nt) {
+                    const size_t slot = slot0 + warp;
+                    const float a = lane < nrow ? swiglu(s.g[warp * 32 + lane], s.u[warp * 32 + lane]) : 0.0f;
+                    if (c.down_f32) {
+                        if (lane < nrow) p.af[slot * p.W + r0 + lane] = a;
+                    } else {
+                        quant_block32(a, p.aq + slot * p.W + r0, p.ad + slot * (p.W >> 5) + (r0 >> 5),
+                                      p.as + slot * (p.W >> 5) + (r0 >> 5), lane);
                     }
                 }
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&s.empty[st]);
-                g++;
-#pragma unroll
-                for (int t = 0; t < kTT; t++) {
-                    float v = acc[t];
-#pragma unroll
-                    for (int o = 8; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-                    if (hl == 0 && t < nt && rl < nrow)
-                        p.y[((size_t)x.pr.slot0 + t0 + t) * p.H + r0 + rl] = v;
-                }
+                named_bar(1, kConsumers);
             }
         }
     }
@@ -511,10 +564,18 @@ cudaError_t launch_stream(Kern kern, const FwdParams &p, const LayerDev &L, Stre
     return cudaGetLastError();
 }
 
-int ring_stages(int stage_bytes)
+// K-slice, smem row strides, stage size and ring depth for matrices of one
+// format whose largest input dimension is kmax.
+void plan_stream(StreamCfg &c, int fmt, int kmax, int nmat)
 {
-    int s = kRingBudget / stage_bytes;
-    return s < 2 ? 2 : (s > 16 ? 16 : s);
+    const int cap = fmt == FMT_Q4_K ? 1024 : 512;
+    c.ks = kmax < cap ? kmax : cap;
+    c.qs_row = fmt == FMT_Q4_K ? c.ks / 2 : c.ks;
+    c.meta_row = fmt == FMT_Q4_K ? (c.ks / 256) * 16 : (((c.ks / 32) * 2 + 15) & ~15);
+    const size_t stage = (size_t)nmat * kRows * (c.qs_row + c.meta_row);
+    c.stage_bytes = (int)((stage + 127) / 128 * 128);
+    int stg = kRingBudget / c.stage_bytes;
+    c.stages = stg < 2 ? 2 : (stg > 16 ? 16 : stg);
 }
 
 }  // namespace
@@ -531,17 +592,14 @@ cudaError_t launch_gate_up(const FwdParams &p, const LayerDev &L, int mode, int 
     }
     StreamCfg c{};
     c.mode = mode;
-    c.item_rows = kGuItemRows;
-    c.rt_routed = mode == 1 ? 0 : (L.gate.rows + kGuItemRows - 1) / kGuItemRows;
-    c.rt_shared = (mode != 0 && p.S > 0) ? (L.sh_gate.rows + kGuItemRows - 1) / kGuItemRows : 0;
+    c.rt_routed = mode == 1 ? 0 : (L.gate.rows + kRows - 1) / kRows;
+    c.rt_shared = (mode != 0 && p.S > 0) ? (L.sh_gate.rows + kRows - 1) / kRows : 0;
     c.down_f32 = (mode == 1 ? L.sh_down.type : L.down.type) == FMT_F32;
     c.act_k = p.H;
-    size_t per_row = G0.qs_rstride + G0.meta_rstride;
-    c.stage_bytes = (int)(((2 * kGuChunkRows * per_row) + 127) / 128 * 128);
-    c.stages = ring_stages(c.stage_bytes);
+    plan_stream(c, G0.type, p.H, 2);
     const int upper = (mode == 1 ? 0 : (p.max_problems - (p.S > 0 ? 1 : 0)) * c.rt_routed) + c.rt_shared;
-    if (G0.type == FMT_Q4_K) return launch_stream(gate_up_stream_kernel<FMT_Q4_K>, p, L, c, upper, num_sms, st);
-    return launch_stream(gate_up_stream_kernel<FMT_Q8_0>, p, L, c, upper, num_sms, st);
+    if (G0.type == FMT_Q4_K) return launch_stream(expert_stream_kernel<FMT_Q4_K, 2>, p, L, c, upper, num_sms, st);
+    return launch_stream(expert_stream_kernel<FMT_Q8_0, 2>, p, L, c, upper, num_sms, st);
 }
 
 cudaError_t launch_down(const FwdParams &p, const LayerDev &L, int mode, int num_sms, cudaStream_t st)
@@ -554,22 +612,15 @@ cudaError_t launch_down(const FwdParams &p, const LayerDev &L, int mode, int num
     }
     StreamCfg c{};
     c.mode = mode;
-    c.item_rows = kDnItemRows;
-    c.rt_routed = mode == 1 ? 0 : (p.H + kDnItemRows - 1) / kDnItemRows;
-    c.rt_shared = (mode != 0 && p.S > 0) ? (p.H + kDnItemRows - 1) / kDnItemRows : 0;
-    size_t per_row = D0.qs_rstride + D0.meta_rstride;
-    int act = D0.cols;
-    if (mode == 2) {
-        const size_t sh_row = L.sh_down.qs_rstride + L.sh_down.meta_rstride;
-        per_row = per_row > sh_row ? per_row : sh_row;
-        act = act > L.sh_down.cols ? act : L.sh_down.cols;
-    }
-    c.act_k = act;
-    c.stage_bytes = (int)((kDnChunkRows * per_row + 127) / 128 * 128);
-    c.stages = ring_stages(c.stage_bytes);
+    c.rt_routed = mode == 1 ? 0 : (p.H + kRows - 1) / kRows;
+    c.rt_shared = (mode != 0 && p.S > 0) ? (p.H + kRows - 1) / kRows : 0;
+    int kmax = D0.cols;
+    if (mode == 2 && L.sh_down.cols > kmax) kmax = L.sh_down.cols;
+    c.act_k = kmax;
+    plan_stream(c, D0.type, kmax, 1);
     const int upper = (mode == 1 ? 0 : (p.max_problems - (p.S > 0 ? 1 : 0)) * c.rt_routed) + c.rt_shared;
-    if (D0.type == FMT_Q4_K) return launch_stream(down_stream_kernel<FMT_Q4_K>, p, L, c, upper, num_sms, st);
-    return launch_stream(down_stream_kernel<FMT_Q8_0>, p, L, c, upper, num_sms, st);
+    if (D0.type == FMT_Q4_K) return launch_stream(expert_stream_kernel<FMT_Q4_K, 1>, p, L, c, upper, num_sms, st);
+    return launch_stream(expert_stream_kernel<FMT_Q8_0, 1>, p, L, c, upper, num_sms, st);
 }
 
 cudaError_t launch_combine(const FwdParams &p, cudaStream_t st)

@@ -16,7 +16,9 @@ struct StreamCfg {
     int down_f32;      // gate_up: store a in f32 (F32 down matrices)
     int rt_routed;     // row tiles per routed problem
     int rt_shared;     // row tiles of the shared problem
-    int item_rows;     // rows per work item
+    int ks;            // values per K-slice (one ring stage holds 32 rows of one slice)
+    int qs_row;        // shared-memory bytes of one row's slice of quants
+    int meta_row;      // shared-memory bytes of one row's slice of scales (multiple of 16)
 };
 
 cudaError_t launch_router(const FwdParams &p, cudaStream_t st);

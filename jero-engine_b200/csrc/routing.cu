@@ -210,64 +210,53 @@ __global__ void __launch_bounds__(128) topk_kernel(FwdParams p)
         k = min(k, p.topk_groups * gs);
     }
 
-    int sel[kMaxK];
-    float w[kMaxK];
+    // The rank list lives one entry per lane: lane r holds the r-th choice.
+    int my_e = -1;
+    float my_w = 0.0f;
     int nsel = 0;
+#pragma unroll 1
+    for (int r = 0; r < k; r++) {
+        int32_t bk = INT32_MIN;
+        int bi = 0x7fffffff;
+        float bp = 0.0f;
 #pragma unroll
-    for (int r = 0; r < kMaxK; r++) {
-        sel[r] = -1;
-        w[r] = 0.0f;
-        if (r < k) {
-            int32_t bk = INT32_MIN;
-            int bi = 0x7fffffff;
-            float bp = 0.0f;
-#pragma unroll
-            for (int i = 0; i < kMaxLaneE; i++) {
-                const int e = lane + 32 * i;
-                if (cand[i] && (bi == 0x7fffffff || rank_before(key[i], e, bk, bi))) { bk = key[i]; bi = e; bp = pv[i]; }
-            }
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) {
-                const int32_t ok = __shfl_xor_sync(0xffffffffu, bk, o);
-                const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-                const float op = __shfl_xor_sync(0xffffffffu, bp, o);
-                if (oi != 0x7fffffff && (bi == 0x7fffffff || rank_before(ok, oi, bk, bi))) { bk = ok; bi = oi; bp = op; }
-            }
-            if (bi != 0x7fffffff) {
-                if ((bi & 31) == lane) {
-#pragma unroll
-                    for (int i = 0; i < kMaxLaneE; i++)
-                        if (i == (bi >> 5)) cand[i] = false;
-                }
-                sel[r] = bi;
-                if (p.sel_bias) w[r] = sum_ok ? __fdiv_rn(bp, psum) : 0.0f;
-                else w[r] = sum_ok ? __fdiv_rn(bp, psum) : __fdiv_rn(1.0f, (float)E);
-                nsel = r + 1;
-            }
+        for (int i = 0; i < kMaxLaneE; i++) {
+            const int e = lane + 32 * i;
+            if (cand[i] && (bi == 0x7fffffff || rank_before(key[i], e, bk, bi))) { bk = key[i]; bi = e; bp = pv[i]; }
         }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const int32_t ok = __shfl_xor_sync(0xffffffffu, bk, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            const float op = __shfl_xor_sync(0xffffffffu, bp, o);
+            if (oi != 0x7fffffff && (bi == 0x7fffffff || rank_before(ok, oi, bk, bi))) { bk = ok; bi = oi; bp = op; }
+        }
+        if (bi == 0x7fffffff) break;
+        if ((bi & 31) == lane) {
+#pragma unroll
+            for (int i = 0; i < kMaxLaneE; i++)
+                if (i == (bi >> 5)) cand[i] = false;
+        }
+        if (lane == r) {
+            my_e = bi;
+            if (p.sel_bias) my_w = sum_ok ? __fdiv_rn(bp, psum) : 0.0f;
+            else my_w = sum_ok ? __fdiv_rn(bp, psum) : __fdiv_rn(1.0f, (float)E);
+        }
+        nsel = r + 1;
     }
     if (p.sel_bias || p.normalize) {
+        // sum of the chosen weights in rank order, as the reference adds them
         float ss = 0.0f;
-#pragma unroll
-        for (int r = 0; r < kMaxK; r++)
-            if (r < nsel) ss = __fadd_rn(ss, w[r]);
+        for (int r = 0; r < nsel; r++) ss = __fadd_rn(ss, __shfl_sync(0xffffffffu, my_w, r));
         const bool ok = ss > 0.0f && isfinite(ss);
-#pragma unroll
-        for (int r = 0; r < kMaxK; r++)
-            if (r < nsel) w[r] = ok ? __fdiv_rn(w[r], ss) : __fdiv_rn(1.0f, (float)nsel);
+        if (lane < nsel) my_w = ok ? __fdiv_rn(my_w, ss) : __fdiv_rn(1.0f, (float)nsel);
     } else if (p.routed_scale != 1.0f) {
-#pragma unroll
-        for (int r = 0; r < kMaxK; r++) w[r] = __fmul_rn(w[r], p.routed_scale);
+        my_w = __fmul_rn(my_w, p.routed_scale);
     }
-
-    const int mw = p.mask_words;
-#pragma unroll
-    for (int r = 0; r < kMaxK; r++) {
-        if (r < p.k && lane == r) {
-            p.sel_idx[(size_t)t * p.k + r] = sel[r];
-            p.sel_w[(size_t)t * p.k + r] = sel[r] >= 0 ? w[r] : 0.0f;
-            if (sel[r] >= 0) atomicOr(p.mask + (size_t)sel[r] * mw + (t >> 5), 1u << (t & 31));
-        }
+    if (lane < p.k) {
+        p.sel_idx[(size_t)t * p.k + lane] = my_e;
+        p.sel_w[(size_t)t * p.k + lane] = my_e >= 0 ? my_w : 0.0f;
+        if (my_e >= 0) atomicOr(p.mask + (size_t)my_e * p.mask_words + (t >> 5), 1u << (t & 31));
     }
 }
 
@@ -386,6 +375,7 @@ __global__ void quantize_rows_kernel(const float *x, int n, int cols, int8_t *xq
                   xs + (size_t)r * nb + b, lane);
 }
 
+// Integer block sums with the dot routines of the expert kernels.
 template <int FMT>
 __global__ void block_dots_kernel(DevMatrix m, const int8_t *xq, int n, int32_t *isum)
 {
@@ -393,9 +383,15 @@ __global__ void block_dots_kernel(DevMatrix m, const int8_t *xq, int n, int32_t 
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n * nb) return;
     const int r = i / nb, u = i % nb;
-    WUnit<FMT> w;
-    w.load(m.qs + (size_t)r * m.qs_rstride, m.meta + (size_t)r * m.meta_rstride, u);
-    isum[i] = w.isum(xq + (size_t)r * m.cols + 32 * u);
+    const uint8_t *qrow = m.qs + (size_t)r * m.qs_rstride;
+    const int4 *x = reinterpret_cast<const int4 *>(xq + (size_t)r * m.cols + 32 * u);
+    if (FMT == FMT_Q4_K) {
+        const Q4Nib nb4 = q4_nibbles(*reinterpret_cast<const uint4 *>(qrow + 16 * (size_t)u));
+        isum[i] = q4_isum16(nb4, x[0], x[1]) >> 4;   // exact: the sum is a multiple of 16
+    } else {
+        const uint4 *q = reinterpret_cast<const uint4 *>(qrow + 32 * (size_t)u);
+        isum[i] = q8_isum(q[0], q[1], x[0], x[1]);
+    }
 }
 
 }  // namespace
