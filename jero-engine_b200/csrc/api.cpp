@@ -34,6 +34,7 @@ struct LayerStore {
     size_t block_bytes = 0, gguf_bytes = 0;
     const float *router = nullptr, *logit_bias = nullptr, *sel_bias = nullptr;
     LayerDev dev{};
+    LayerMaps maps{};
 };
 
 struct Scratch {
@@ -580,10 +581,29 @@ int moe_layer_upload(moe_ctx *ctx, int32_t layer, const moe_layer_desc *desc)
     L.sel_bias = v.sel_bias ? reinterpret_cast<const float *>(base + o_sb) : nullptr;
     auto dev = [&](const Placed &p) {
         if (!p.present) return DevMatrix{};
-        return to_dev(p.plan, base + p.qs, p.plan.meta_bytes ? base + p.meta : nullptr);
+        DevMatrix m = to_dev(p.plan, base + p.qs, p.plan.meta_bytes ? base + p.meta : nullptr);
+        plan_slices(m);
+        return m;
     };
     L.dev.gate = dev(pg); L.dev.up = dev(pu); L.dev.down = dev(pd);
     L.dev.sh_gate = dev(psg); L.dev.sh_up = dev(psu); L.dev.sh_down = dev(psd);
+    // TMA descriptors: each quantised stack is a dense [E*rows][row bytes] array
+    const std::pair<const DevMatrix *, MatMaps *> mats[] = {
+        {&L.dev.gate, &L.maps.gate}, {&L.dev.up, &L.maps.up}, {&L.dev.down, &L.maps.down},
+        {&L.dev.sh_gate, &L.maps.sh_gate}, {&L.dev.sh_up, &L.maps.sh_up}, {&L.dev.sh_down, &L.maps.sh_down}};
+    for (const auto &mm : mats) {
+        const DevMatrix &m = *mm.first;
+        if (m.rows && m.type != FMT_F32 &&
+            (m.qs_estride != m.qs_rstride * m.rows || m.meta_estride != m.meta_rstride * m.rows)) {
+            free_layer(L);
+            return fail(ctx, MOE_ERR_CAPABILITY_MISMATCH, "expert slabs are not dense (rows %d)", m.rows);
+        }
+        const int r = make_matrix_maps(m, mm.second);
+        if (r != 0) {
+            free_layer(L);
+            return fail(ctx, MOE_ERR_CUDA, "cuTensorMapEncodeTiled failed (CUresult %d)", r);
+        }
+    }
     L.gguf_bytes = (size_t)v.E * v.H * 4;
     for (const MatSpec *m : {&v.gate, &v.up, &v.down, &v.sg, &v.su, &v.sd})
         if (m->present) L.gguf_bytes += gguf_row_bytes(m->type, m->cols) * m->rows * m->experts;
@@ -637,7 +657,7 @@ int moe_forward(moe_ctx *ctx, int32_t layer, int32_t T, const float *x, float *o
         ctx->prof.stream = st;
         mk = Marker{&Profiler::mark_cb, &ctx->prof};
     }
-    int err = launch_forward(p, L.dev, st, mk, ctx->num_sms);
+    int err = launch_forward(p, L.dev, L.maps, st, mk, ctx->num_sms);
     if (err != cudaSuccess) return cuda_fail(ctx, (cudaError_t)err, "forward launch");
     ctx->last_layer = layer;
     ctx->last_T = T;

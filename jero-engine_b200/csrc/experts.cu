@@ -147,32 +147,19 @@ __device__ __forceinline__ void stage_act(const Smem &s, int nu_s, const int8_t 
     }
 }
 
-// Producer: per chunk (item, token tile, K-slice) lane 0 arms the stage's
-// mbarrier with the byte count, then lane r copies row r of every matrix.
-struct SliceSrc {
-    const uint8_t *qs, *meta;   // expert slab bases
-    size_t qs_rs, meta_rs;      // global row strides
-};
-
-__device__ __forceinline__ void produce_chunk(const Smem &s, const StreamCfg &c, int st, const SliceSrc *src, int nmat,
-                                              int r0, int nrow, int sl, int ks_cur, int fmt, int lane)
+// Producer: one chunk (item, token tile, K-slice) = for each matrix two 2-D
+// TMA boxes of 32 rows (quants and scales) landing back to back in the stage.
+// Boxes past the end of a row read zeros and still count full box bytes.
+__device__ __forceinline__ void produce_chunk(const Smem &s, const StreamCfg &c, int st, const MatMaps *const *mm,
+                                              int nmat, int y, int sl)
 {
-    // bytes of one row's slice
-    const uint32_t qsz = fmt == FMT_Q4_K ? (uint32_t)ks_cur / 2 : (uint32_t)ks_cur;
-    const uint32_t msz = fmt == FMT_Q4_K ? (uint32_t)(ks_cur / 256) * 16 : (uint32_t)(((ks_cur / 32) * 2 + 15) & ~15);
-    const size_t qoff = fmt == FMT_Q4_K ? (size_t)sl * c.ks / 2 : (size_t)sl * c.ks;
-    const size_t moff = fmt == FMT_Q4_K ? (size_t)sl * (c.ks / 256) * 16 : (size_t)sl * (c.ks / 32) * 2;
-    if (lane == 0) mbar_arrive_expect_tx(&s.full[st], (uint32_t)nmat * nrow * (qsz + msz));
-    __syncwarp();
-    if (lane < nrow) {
-        uint8_t *stage = s.ring + (size_t)st * c.stage_bytes;
-        for (int m = 0; m < nmat; m++) {
-            uint8_t *dq = stage + (size_t)m * kRows * (c.qs_row + c.meta_row);
-            uint8_t *dm = dq + (size_t)kRows * c.qs_row;
-            const size_t row = (size_t)r0 + lane;
-            bulk_g2s(dq + (size_t)lane * c.qs_row, src[m].qs + row * src[m].qs_rs + qoff, qsz, &s.full[st]);
-            bulk_g2s(dm + (size_t)lane * c.meta_row, src[m].meta + row * src[m].meta_rs + moff, msz, &s.full[st]);
-        }
+    mbar_arrive_expect_tx(&s.full[st], (uint32_t)nmat * kRows * (c.qs_row + c.meta_row));
+    uint8_t *stage = s.ring + (size_t)st * c.stage_bytes;
+    for (int m = 0; m < nmat; m++) {
+        uint8_t *dq = stage + (size_t)m * kRows * (c.qs_row + c.meta_row);
+        uint8_t *dm = dq + (size_t)kRows * c.qs_row;
+        tma_load_2d(dq, &mm[m]->qs, sl * (c.qs_row / 8), y, &s.full[st]);
+        tma_load_2d(dm, &mm[m]->meta, sl * (c.meta_row / 8), y, &s.full[st]);
     }
 }
 
@@ -182,27 +169,30 @@ template <int FMT, int NMAT, int NT>
 __device__ __forceinline__ void consume_chunk(const Smem &s, const StreamCfg &c, const uint8_t *stage, int rw, int l8,
                                               int nu_slice, int ubase, int nu_s, float (&acc)[NMAT][NT])
 {
-    const uint8_t *q[NMAT], *mt[NMAT];
-#pragma unroll
-    for (int m = 0; m < NMAT; m++) {
-        q[m] = stage + (size_t)m * kRows * (c.qs_row + c.meta_row) + (size_t)rw * c.qs_row;
-        mt[m] = stage + (size_t)m * kRows * (c.qs_row + c.meta_row) + (size_t)kRows * c.qs_row + (size_t)rw * c.meta_row;
-    }
+    // 32-bit shared addresses throughout the loop
+    const uint32_t st = smem_addr(stage);
+    const uint32_t mat_stride = (uint32_t)kRows * (c.qs_row + c.meta_row);
+    const uint32_t q0a = st + (uint32_t)rw * c.qs_row;
+    const uint32_t m0a = st + (uint32_t)kRows * c.qs_row + (uint32_t)rw * c.meta_row;
+    const uint32_t xa = smem_addr(s.xq), xda = smem_addr(s.xds);
+    const uint32_t xh_stride = (uint32_t)nu_s * 16;   // bytes between the two halves of a token's blocks
+#pragma unroll 1
     for (int u = l8; u < nu_slice; u += 8) {
-        const int ug = ubase + u;
+        const uint32_t ug = (uint32_t)(ubase + u);
         if (FMT == FMT_Q4_K) {
             Q4Nib nb[NMAT];
             float2 sc[NMAT];
 #pragma unroll
             for (int m = 0; m < NMAT; m++) {
-                nb[m] = q4_nibbles(*reinterpret_cast<const uint4 *>(q[m] + 16 * u));
-                sc[m] = q4_scales(*reinterpret_cast<const uint4 *>(mt[m] + 16 * (u >> 3)), l8);
+                nb[m] = q4_nibbles(lds128(q0a + m * mat_stride + 16 * u));
+                sc[m] = q4_scales(lds128(m0a + m * mat_stride + 16 * (u >> 3)), l8);
             }
 #pragma unroll
             for (int t = 0; t < NT; t++) {
-                const int4 a = s.xq[((size_t)t * 2) * nu_s + ug];
-                const int4 b = s.xq[((size_t)t * 2 + 1) * nu_s + ug];
-                const float2 ds = s.xds[(size_t)t * nu_s + ug];
+                const uint32_t xt = xa + (uint32_t)t * 2 * xh_stride + 16 * ug;
+                const int4 a = lds128i(xt);
+                const int4 b = lds128i(xt + xh_stride);
+                const float2 ds = lds64f(xda + 8 * ((uint32_t)t * nu_s + ug));
 #pragma unroll
                 for (int m = 0; m < NMAT; m++) {
                     const float f = i2f_small(q4_isum16(nb[m], a, b));
@@ -215,15 +205,16 @@ __device__ __forceinline__ void consume_chunk(const Smem &s, const StreamCfg &c,
             float d[NMAT];
 #pragma unroll
             for (int m = 0; m < NMAT; m++) {
-                q0[m] = *reinterpret_cast<const uint4 *>(q[m] + 32 * u);
-                q1[m] = *reinterpret_cast<const uint4 *>(q[m] + 32 * u + 16);
-                d[m] = __half2float(*reinterpret_cast<const __half *>(mt[m] + 2 * u));
+                q0[m] = lds128(q0a + m * mat_stride + 32 * u);
+                q1[m] = lds128(q0a + m * mat_stride + 32 * u + 16);
+                d[m] = __half2float(__ushort_as_half((unsigned short)lds16(m0a + m * mat_stride + 2 * u)));
             }
 #pragma unroll
             for (int t = 0; t < NT; t++) {
-                const int4 a = s.xq[((size_t)t * 2) * nu_s + ug];
-                const int4 b = s.xq[((size_t)t * 2 + 1) * nu_s + ug];
-                const float xd = s.xds[(size_t)t * nu_s + ug].x;
+                const uint32_t xt = xa + (uint32_t)t * 2 * xh_stride + 16 * ug;
+                const int4 a = lds128i(xt);
+                const int4 b = lds128i(xt + xh_stride);
+                const float xd = lds64f(xda + 8 * ((uint32_t)t * nu_s + ug)).x;
 #pragma unroll
                 for (int m = 0; m < NMAT; m++)
                     acc[m][t] = fmaf(i2f_small(q8_isum(q0[m], q1[m], a, b)), d[m] * xd, acc[m][t]);
@@ -298,7 +289,8 @@ __device__ __forceinline__ void publish_y(const FwdParams &p, const float (&o)[1
 // NMAT == 2: gate and up (rows of I or S, K = H), epilogue a = silu(g) * u
 // quantised per 32 rows. NMAT == 1: down (rows of H, K = I or S), y written.
 template <int FMT, int NMAT>
-__global__ void __launch_bounds__(kStreamThreads, 2) expert_stream_kernel(FwdParams p, LayerDev L, StreamCfg c)
+__global__ void __launch_bounds__(kStreamThreads, 2)
+    expert_stream_kernel(FwdParams p, LayerDev L, StreamCfg c, const __grid_constant__ LayerMaps maps)
 {
     extern __shared__ __align__(128) uint8_t smem_raw[];
     const Smem s = carve(smem_raw, c);
@@ -309,42 +301,34 @@ __global__ void __launch_bounds__(kStreamThreads, 2) expert_stream_kernel(FwdPar
     const int it0 = (int)((long long)blockIdx.x * total / gridDim.x);
     const int it1 = (int)((long long)(blockIdx.x + 1) * total / gridDim.x);
 
-    if (warp == kConsumerWarps) {   // producer warp
+    if (warp == kConsumerWarps) {   // producer: one thread issues the TMA boxes
+        if (lane != 0) return;
         uint32_t g = 0;
         for (int it = it0; it < it1; it++) {
             const Item x = item_at(p, c, nr, it);
-            SliceSrc src[NMAT];
+            const MatMaps *mm[NMAT];
             int K, rows;
             if (NMAT == 2) {
-                const DevMatrix &G = x.shared ? L.sh_gate : L.gate;
-                const DevMatrix &U = x.shared ? L.sh_up : L.up;
-                src[0] = {G.qs + (size_t)x.pr.expert * G.qs_estride, G.meta + (size_t)x.pr.expert * G.meta_estride,
-                          G.qs_rstride, G.meta_rstride};
-                src[NMAT - 1] = {U.qs + (size_t)x.pr.expert * U.qs_estride,
-                                 U.meta + (size_t)x.pr.expert * U.meta_estride, U.qs_rstride, U.meta_rstride};
-                K = G.cols;
-                rows = G.rows;
+                mm[0] = x.shared ? &maps.sh_gate : &maps.gate;
+                mm[NMAT - 1] = x.shared ? &maps.sh_up : &maps.up;
+                K = x.shared ? L.sh_gate.cols : L.gate.cols;
+                rows = x.shared ? L.sh_gate.rows : L.gate.rows;
             } else {
-                const DevMatrix &D = x.shared ? L.sh_down : L.down;
-                src[0] = {D.qs + (size_t)x.pr.expert * D.qs_estride, D.meta + (size_t)x.pr.expert * D.meta_estride,
-                          D.qs_rstride, D.meta_rstride};
-                K = D.cols;
-                rows = D.rows;
+                mm[0] = x.shared ? &maps.sh_down : &maps.down;
+                K = x.shared ? L.sh_down.cols : L.down.cols;
+                rows = x.shared ? L.sh_down.rows : L.down.rows;
             }
-            const int r0 = x.rt * kRows, nrow = min(kRows, rows - r0);
+            const int y = x.pr.expert * rows + x.rt * kRows;
             const int tiles = (x.pr.count + kTT - 1) / kTT, ns = (K + c.ks - 1) / c.ks;
             for (int tt = 0; tt < tiles; tt++) {
                 for (int sl = 0; sl < ns; sl++) {
                     const int st = g % c.stages;
                     const uint32_t use = g / c.stages;
-                    int ok = 1;
-                    if (use > 0 && lane == 0) ok = wait_bar(&s.empty[st], (use - 1) & 1, s.abort_flag, p.err);
-                    ok = __shfl_sync(0xffffffffu, ok, 0);
-                    if (!ok) {
-                        if (lane == 0) drain(s, c.stages, g);
+                    if (use > 0 && !wait_bar(&s.empty[st], (use - 1) & 1, s.abort_flag, p.err)) {
+                        drain(s, c.stages, g);
                         return;
                     }
-                    produce_chunk(s, c, st, src, NMAT, r0, nrow, sl, min(c.ks, K - sl * c.ks), FMT, lane);
+                    produce_chunk(s, c, st, mm, NMAT, y, sl);
                     g++;
                 }
             }
@@ -548,8 +532,8 @@ cudaError_t set_smem(Kern k, size_t bytes)
 }
 
 template <typename Kern>
-cudaError_t launch_stream(Kern kern, const FwdParams &p, const LayerDev &L, StreamCfg c, int upper, int num_sms,
-                          cudaStream_t st)
+cudaError_t launch_stream(Kern kern, const FwdParams &p, const LayerDev &L, const LayerMaps &maps, StreamCfg c,
+                          int upper, int num_sms, cudaStream_t st)
 {
     if (upper <= 0) return cudaSuccess;
     const size_t sm = smem_bytes(c);
@@ -560,18 +544,17 @@ cudaError_t launch_stream(Kern kern, const FwdParams &p, const LayerDev &L, Stre
         return err;
     if (per_sm < 1) return cudaErrorInvalidConfiguration;
     const int grid = upper < num_sms * per_sm ? upper : num_sms * per_sm;
-    kern<<<grid, kStreamThreads, sm, st>>>(p, L, c);
+    kern<<<grid, kStreamThreads, sm, st>>>(p, L, c, maps);
     return cudaGetLastError();
 }
 
-// K-slice, smem row strides, stage size and ring depth for matrices of one
-// format whose largest input dimension is kmax.
-void plan_stream(StreamCfg &c, int fmt, int kmax, int nmat)
+// Ring geometry from the slice plan of the matrices the launch streams (the
+// routed and shared matrices of one launch share a plan; see stream_plans_match).
+void plan_stream(StreamCfg &c, const DevMatrix &m, int nmat)
 {
-    const int cap = fmt == FMT_Q4_K ? 1024 : 512;
-    c.ks = kmax < cap ? kmax : cap;
-    c.qs_row = fmt == FMT_Q4_K ? c.ks / 2 : c.ks;
-    c.meta_row = fmt == FMT_Q4_K ? (c.ks / 256) * 16 : (((c.ks / 32) * 2 + 15) & ~15);
+    c.ks = m.ks;
+    c.qs_row = m.qs_box;
+    c.meta_row = m.meta_box;
     const size_t stage = (size_t)nmat * kRows * (c.qs_row + c.meta_row);
     c.stage_bytes = (int)((stage + 127) / 128 * 128);
     int stg = kRingBudget / c.stage_bytes;
@@ -580,7 +563,13 @@ void plan_stream(StreamCfg &c, int fmt, int kmax, int nmat)
 
 }  // namespace
 
-cudaError_t launch_gate_up(const FwdParams &p, const LayerDev &L, int mode, int num_sms, cudaStream_t st)
+bool stream_plans_match(const DevMatrix &a, const DevMatrix &b)
+{
+    return a.type == b.type && a.ks == b.ks && a.qs_box == b.qs_box && a.meta_box == b.meta_box;
+}
+
+cudaError_t launch_gate_up(const FwdParams &p, const LayerDev &L, const LayerMaps &maps, int mode, int num_sms,
+                           cudaStream_t st)
 {
     const DevMatrix &G0 = mode == 1 ? L.sh_gate : L.gate;
     if (G0.type == FMT_F32) {
@@ -596,13 +585,15 @@ cudaError_t launch_gate_up(const FwdParams &p, const LayerDev &L, int mode, int 
     c.rt_shared = (mode != 0 && p.S > 0) ? (L.sh_gate.rows + kRows - 1) / kRows : 0;
     c.down_f32 = (mode == 1 ? L.sh_down.type : L.down.type) == FMT_F32;
     c.act_k = p.H;
-    plan_stream(c, G0.type, p.H, 2);
+    plan_stream(c, G0, 2);
     const int upper = (mode == 1 ? 0 : (p.max_problems - (p.S > 0 ? 1 : 0)) * c.rt_routed) + c.rt_shared;
-    if (G0.type == FMT_Q4_K) return launch_stream(expert_stream_kernel<FMT_Q4_K, 2>, p, L, c, upper, num_sms, st);
-    return launch_stream(expert_stream_kernel<FMT_Q8_0, 2>, p, L, c, upper, num_sms, st);
+    if (G0.type == FMT_Q4_K)
+        return launch_stream(expert_stream_kernel<FMT_Q4_K, 2>, p, L, maps, c, upper, num_sms, st);
+    return launch_stream(expert_stream_kernel<FMT_Q8_0, 2>, p, L, maps, c, upper, num_sms, st);
 }
 
-cudaError_t launch_down(const FwdParams &p, const LayerDev &L, int mode, int num_sms, cudaStream_t st)
+cudaError_t launch_down(const FwdParams &p, const LayerDev &L, const LayerMaps &maps, int mode, int num_sms,
+                        cudaStream_t st)
 {
     const DevMatrix &D0 = mode == 1 ? L.sh_down : L.down;
     if (D0.type == FMT_F32) {
@@ -617,10 +608,11 @@ cudaError_t launch_down(const FwdParams &p, const LayerDev &L, int mode, int num
     int kmax = D0.cols;
     if (mode == 2 && L.sh_down.cols > kmax) kmax = L.sh_down.cols;
     c.act_k = kmax;
-    plan_stream(c, D0.type, kmax, 1);
+    plan_stream(c, D0, 1);
     const int upper = (mode == 1 ? 0 : (p.max_problems - (p.S > 0 ? 1 : 0)) * c.rt_routed) + c.rt_shared;
-    if (D0.type == FMT_Q4_K) return launch_stream(expert_stream_kernel<FMT_Q4_K, 1>, p, L, c, upper, num_sms, st);
-    return launch_stream(expert_stream_kernel<FMT_Q8_0, 1>, p, L, c, upper, num_sms, st);
+    if (D0.type == FMT_Q4_K)
+        return launch_stream(expert_stream_kernel<FMT_Q4_K, 1>, p, L, maps, c, upper, num_sms, st);
+    return launch_stream(expert_stream_kernel<FMT_Q8_0, 1>, p, L, maps, c, upper, num_sms, st);
 }
 
 cudaError_t launch_combine(const FwdParams &p, cudaStream_t st)

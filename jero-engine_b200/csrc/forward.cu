@@ -9,7 +9,8 @@
 
 namespace jmoe {
 
-int launch_forward(const FwdParams &p, const LayerDev &L, void *stream, const Marker &mk, int num_sms)
+int launch_forward(const FwdParams &p, const LayerDev &L, const LayerMaps &maps, void *stream, const Marker &mk,
+                   int num_sms)
 {
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     cudaError_t err;
@@ -25,19 +26,19 @@ int launch_forward(const FwdParams &p, const LayerDev &L, void *stream, const Ma
     mk.mark("scan");
 
     const bool has_sh = p.S > 0;
-    // one launch covers routed and shared problems when they share a format
-    const bool same_gu = has_sh && L.sh_gate.type == L.gate.type;
-    const bool same_d = has_sh && L.sh_down.type == L.down.type;
-    if ((err = launch_gate_up(p, L, same_gu ? 2 : 0, num_sms, st)) != cudaSuccess) return err;
+    // one launch covers routed and shared problems when they share a format and slice plan
+    const bool same_gu = has_sh && stream_plans_match(L.sh_gate, L.gate);
+    const bool same_d = has_sh && stream_plans_match(L.sh_down, L.down);
+    if ((err = launch_gate_up(p, L, maps, same_gu ? 2 : 0, num_sms, st)) != cudaSuccess) return err;
     mk.mark("gate_up");
     if (has_sh && !same_gu) {
-        if ((err = launch_gate_up(p, L, 1, num_sms, st)) != cudaSuccess) return err;
+        if ((err = launch_gate_up(p, L, maps, 1, num_sms, st)) != cudaSuccess) return err;
         mk.mark("gate_up_shared");
     }
-    if ((err = launch_down(p, L, same_d ? 2 : 0, num_sms, st)) != cudaSuccess) return err;
+    if ((err = launch_down(p, L, maps, same_d ? 2 : 0, num_sms, st)) != cudaSuccess) return err;
     mk.mark("down");
     if (has_sh && !same_d) {
-        if ((err = launch_down(p, L, 1, num_sms, st)) != cudaSuccess) return err;
+        if ((err = launch_down(p, L, maps, 1, num_sms, st)) != cudaSuccess) return err;
         mk.mark("down_shared");
     }
     if ((err = launch_combine(p, st)) != cudaSuccess) return err;

@@ -24,8 +24,12 @@ struct StreamCfg {
 cudaError_t launch_router(const FwdParams &p, cudaStream_t st);
 cudaError_t launch_topk(const FwdParams &p, cudaStream_t st);
 cudaError_t launch_scan(const FwdParams &p, cudaStream_t st);
-cudaError_t launch_gate_up(const FwdParams &p, const LayerDev &L, int mode, int num_sms, cudaStream_t st);
-cudaError_t launch_down(const FwdParams &p, const LayerDev &L, int mode, int num_sms, cudaStream_t st);
+// Routed and shared matrices can share one streaming launch when their slice plans match.
+bool stream_plans_match(const DevMatrix &a, const DevMatrix &b);
+cudaError_t launch_gate_up(const FwdParams &p, const LayerDev &L, const LayerMaps &maps, int mode, int num_sms,
+                           cudaStream_t st);
+cudaError_t launch_down(const FwdParams &p, const LayerDev &L, const LayerMaps &maps, int mode, int num_sms,
+                        cudaStream_t st);
 cudaError_t launch_combine(const FwdParams &p, cudaStream_t st);
 
 }  // namespace jmoe

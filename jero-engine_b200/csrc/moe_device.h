@@ -12,6 +12,7 @@
 // Every expert slab starts on a 128-byte boundary.
 #pragma once
 
+#include <cuda.h>
 #include <stddef.h>
 #include <stdint.h>
 
@@ -30,6 +31,20 @@ struct DevMatrix {
     size_t meta_estride;
     size_t qs_rstride;       // bytes per row
     size_t meta_rstride;
+    int ks;                  // values per K-slice streamed by the expert kernels
+    int qs_box;              // bytes of one row's slice of quants (TMA box width)
+    int meta_box;            // bytes of one row's slice of scales (TMA box width)
+    int _pad;
+};
+
+// 2-D TMA descriptors of one quantised stack viewed as [E*rows][row bytes]
+// (u64 elements); the box is 32 rows by one K-slice.
+struct MatMaps {
+    CUtensorMap qs, meta;
+};
+
+struct LayerMaps {
+    MatMaps gate, up, down, sh_gate, sh_up, sh_down;
 };
 
 // One group of slots that share a weight set: a routed expert, or the shared
@@ -91,7 +106,14 @@ struct Marker {
 
 // Launch sequence of one forward on stream; returns cudaError_t as int.
 // num_sms sizes the grids of the streaming expert kernels.
-int launch_forward(const FwdParams &p, const LayerDev &L, void *stream, const Marker &mk, int num_sms);
+int launch_forward(const FwdParams &p, const LayerDev &L, const LayerMaps &maps, void *stream, const Marker &mk,
+                   int num_sms);
+
+// K-slice and TMA box widths of a quantised matrix (host side, at upload).
+void plan_slices(DevMatrix &m);
+
+// Builds the two TMA descriptors of a quantised stack; returns a CUresult.
+int make_matrix_maps(const DevMatrix &m, MatMaps *out);
 
 // Integer block sums for the parity probe (same device code as the forward path).
 int launch_block_dots(const DevMatrix &m, const int8_t *xq, int n, int32_t *isum, void *stream);

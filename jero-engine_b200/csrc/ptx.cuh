@@ -2,6 +2,7 @@
 // (sm_90+ async proxy; used here on sm_100a).
 #pragma once
 
+#include <cuda.h>
 #include <stdint.h>
 
 namespace jmoe {
@@ -46,15 +47,51 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity)
     return ok != 0;
 }
 
-// Global -> shared bulk copy (no tensor map, no multicast) completing on bar.
-// dst, src 16-byte aligned; bytes a multiple of 16.
-__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar)
+// 2-D TMA tile load (no multicast) of the box at (x, y) of map into shared
+// memory, completing on bar. x in elements of the map; x * element size must
+// be a multiple of 16 bytes.
+__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar)
 {
     asm volatile(
-        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
             smem_addr(dst)),
-        "l"(src), "r"(bytes), "r"(smem_addr(bar))
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_addr(bar))
         : "memory");
+}
+
+__device__ __forceinline__ void prefetch_tmap(const CUtensorMap *map)
+{
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+// Shared-memory loads on 32-bit shared addresses (keeps the compiler from
+// falling back to generic 64-bit loads in the hot loops).
+__device__ __forceinline__ uint4 lds128(uint32_t a)
+{
+    uint4 v;
+    asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
+    return v;
+}
+
+__device__ __forceinline__ int4 lds128i(uint32_t a)
+{
+    int4 v;
+    asm volatile("ld.shared.v4.s32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
+    return v;
+}
+
+__device__ __forceinline__ float2 lds64f(uint32_t a)
+{
+    float2 v;
+    asm volatile("ld.shared.v2.f32 {%0, %1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(a));
+    return v;
+}
+
+__device__ __forceinline__ uint32_t lds16(uint32_t a)
+{
+    unsigned short v;
+    asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(a));
+    return v;
 }
 
 // Named barrier among `count` threads (id 1..15; id 0 is __syncthreads).

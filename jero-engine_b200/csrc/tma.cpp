@@ -1,0 +1,73 @@
+// tma.cpp -- K-slice planning and TMA tensor-map descriptors for the
+// quantised expert stacks (host side, built once at upload).
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_runtime.h>
+
+#include <cstring>
+
+#include "moe_device.h"
+
+namespace jmoe {
+
+namespace {
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn()
+{
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    if (!fn) {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    }
+    return fn;
+}
+
+// [rows_total][row_bytes] viewed as u64 elements, box = box_rows x box_bytes.
+CUresult encode(CUtensorMap *map, const void *base, uint64_t rows_total, uint64_t row_bytes, uint32_t box_rows,
+                uint32_t box_bytes)
+{
+    PFN_cuTensorMapEncodeTiled_v12000 fn = encode_fn();
+    if (!fn) return CUDA_ERROR_NOT_SUPPORTED;
+    cuuint64_t dims[2] = {row_bytes / 8, rows_total};
+    cuuint64_t strides[1] = {row_bytes};
+    cuuint32_t box[2] = {box_bytes / 8, box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, const_cast<void *>(base), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+}
+
+}  // namespace
+
+// A K-slice is at most 1024 values (Q4_K) or 512 (Q8_0), a whole number of
+// super-blocks, so one ring stage (2 matrices x 32 rows) stays near 36 KB and
+// every slice starts on a 16-byte boundary of its row (TMA box x-alignment).
+void plan_slices(DevMatrix &m)
+{
+    if (m.type == FMT_Q4_K) {
+        m.ks = m.cols < 1024 ? m.cols : 1024;
+        m.qs_box = m.ks / 2;
+        m.meta_box = (m.ks / 256) * 16;
+    } else if (m.type == FMT_Q8_0) {
+        m.ks = m.cols < 512 ? m.cols : 512;
+        m.qs_box = m.ks;
+        m.meta_box = ((m.ks / 32) * 2 + 15) & ~15;
+    } else {
+        m.ks = m.qs_box = m.meta_box = 0;
+    }
+}
+
+int make_matrix_maps(const DevMatrix &m, MatMaps *out)
+{
+    memset(out, 0, sizeof *out);
+    if (m.type != FMT_Q4_K && m.type != FMT_Q8_0) return CUDA_SUCCESS;
+    const uint64_t rows_total = (uint64_t)m.n_experts * m.rows;
+    CUresult r = encode(&out->qs, m.qs, rows_total, m.qs_rstride, 32, (uint32_t)m.qs_box);
+    if (r != CUDA_SUCCESS) return r;
+    return encode(&out->meta, m.meta, rows_total, m.meta_rstride, 32, (uint32_t)m.meta_box);
+}
+
+}  // namespace jmoe
