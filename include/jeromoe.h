@@ -208,6 +208,27 @@ int moe_debug_permutation(moe_ctx *ctx, int32_t *offsets, int32_t *perm_token, i
 int moe_debug_block_dots(int32_t device, int32_t quant, const void *w, const float *x, int32_t n,
                          int32_t cols, int32_t *isum, int8_t *xq, float *xd);
 
+/* ---- routing without allocation ----
+ * No counterpart in the reference. For callers that cannot allocate device
+ * memory or let a library do it (a runtime that owns all device memory
+ * through its own pool, or a decode loop held to zero allocations): the
+ * router logits, top-k selection and dispatch permutation of T tokens, with
+ * the kernels' working memory in one fixed 2 MiB static device array instead
+ * of a context. All pointers are device pointers on `device`; x [T x H] and
+ * router [E x H] f32 (16-byte aligned), logit_bias / sel_bias [E] or NULL
+ * (as moe_layer_desc's logit_bias / exp_probs_b); outputs sel_idx, sel_w
+ * [T x top_k], offsets [E+1], perm_token [T x top_k] as moe_forward and
+ * moe_debug_permutation report them. n_groups > 0 selects group-limited
+ * routing. Limits: T <= 1024, E <= 256, top_k <= 16; larger shapes return
+ * MOE_ERR_CONTEXT_LENGTH. Asynchronous on `stream` (a cudaStream_t). The
+ * first call on a device resolves the array's address, so make it before
+ * capturing the stream into a graph. Every call shares the array: calls that
+ * overlap on the GPU race. Errors: moe_last_error_message(NULL). */
+int moe_route_noalloc(int32_t device, const float *x, const float *router, const float *logit_bias,
+                      const float *sel_bias, int32_t T, int32_t H, int32_t E, int32_t top_k, int32_t normalize,
+                      float routed_scale, int32_t n_groups, int32_t topk_groups, int32_t *sel_idx, float *sel_w,
+                      int32_t *offsets, int32_t *perm_token, void *stream);
+
 /* ---- host utilities (no device work) ---- */
 
 /* GGUF row bytes for cols values of quant (0 if cols is not a whole number of blocks). */

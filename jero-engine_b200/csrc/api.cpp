@@ -825,3 +825,9 @@ int moe_debug_block_dots(int32_t device, int32_t quant, const void *w, const flo
 uint64_t moe_row_bytes(int32_t quant, int32_t cols) { return gguf_row_bytes(quant, cols); }
 
 }  // extern "C"
+
+void jmoe::record_error(const char *msg) { g_last_error = msg ? msg : ""; }
+
+extern "C" {
+
+}  // extern "C"

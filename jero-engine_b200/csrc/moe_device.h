@@ -115,6 +115,9 @@ void plan_slices(DevMatrix &m);
 // Builds the two TMA descriptors of a quantised stack; returns a CUresult.
 int make_matrix_maps(const DevMatrix &m, MatMaps *out);
 
+// Stores the message that moe_last_error_message(NULL) returns on this thread.
+void record_error(const char *msg);
+
 // Integer block sums for the parity probe (same device code as the forward path).
 int launch_block_dots(const DevMatrix &m, const int8_t *xq, int n, int32_t *isum, void *stream);
 int launch_quantize_rows(const float *x, int n, int cols, int8_t *xq, float *xd, float *xs,

@@ -138,6 +138,9 @@ EXPORTS = {
     "moe_debug_permutation": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.POINTER(C.c_int32)]),
     "moe_debug_block_dots": (C.c_int, [C.c_int32, C.c_int32, C.c_void_p, C.c_void_p, C.c_int32, C.c_int32,
                                        C.c_void_p, C.c_void_p, C.c_void_p]),
+    "moe_route_noalloc": (C.c_int, [C.c_int32, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int32,
+                                    C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_float, C.c_int32, C.c_int32,
+                                    C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]),
     "moe_row_bytes": (C.c_uint64, [C.c_int32, C.c_int32]),
     "moe_quantize_rows": (C.c_int, [C.c_int32, C.c_void_p, C.c_int64, C.c_int32, C.c_void_p, C.c_int32]),
     "moe_gen_normal": (C.c_int, [C.c_uint64, C.c_uint64, C.c_uint64, C.c_float, C.c_void_p, C.c_int32]),
