@@ -48,6 +48,15 @@ def rank_info():
     return int(os.environ.get("RANK", 0)), int(os.environ.get("LOCAL_RANK", 0)), int(os.environ.get("WORLD_SIZE", 1))
 
 
+def measured_traffic(workload, kernel):
+    """DRAM bytes per launch of `kernel` from the committed ncu summary, or None."""
+    try:
+        with open(os.path.join(ROOT, "profiles", "traffic.json")) as f:
+            return json.load(f).get(workload, {}).get(kernel)
+    except Exception:
+        return None
+
+
 def peaks():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     try:
@@ -323,7 +332,8 @@ def run_ours(args):
                        "parallelism": f"replicas{world}" if world > 1 else "single",
                        "l2": "flushed between timed steps (256 MiB write); per-step CUDA events"},
             "roofline": {"bound": "hbm", "kernel": dom, "achieved": round(achieved, 1), "peak": hbm,
-                         "unit": "GB/s", "frac": round(achieved / hbm, 4), "traffic": None,
+                         "unit": "GB/s", "frac": round(achieved / hbm, 4),
+                         "traffic": measured_traffic(f"{cfg.name} T={T}", dom),
                          "peak_source": peak_kind, "algorithmic_bytes_per_launch": int(kb[dom])},
             "layer_roofline": {"bytes": int(kb["layer"]), "gbs": round(kb["layer"] / (layer_ms / 1e3) / 1e9, 1),
                                "frac": round(kb["layer"] / (layer_ms / 1e3) / 1e9 / hbm, 4)},
