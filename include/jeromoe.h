@@ -98,9 +98,17 @@ typedef struct moe_device_spec {
     int32_t device;            /* CUDA ordinal */
     int32_t max_tokens;        /* largest T one forward may take (sizes the scratch) */
     int32_t max_layers;        /* layer slots in the device store */
-    int32_t flags;             /* reserved, 0 */
+    int32_t flags;             /* MOE_FLAG_* */
     uint64_t reserve_bytes;    /* HBM left free for other users of the device */
 } moe_device_spec;
+
+/* Expert path selection. By default forwards with at least
+ * MOE_TENSOR_CORE_MIN_TOKENS tokens run the experts as tensor-core GEMMs
+ * (f16 operands, f32 accumulation) and smaller ones as int8 weight-streaming
+ * kernels; these flags force one path for every forward of the context. */
+#define MOE_FLAG_TENSOR_CORES_ALWAYS 1
+#define MOE_FLAG_TENSOR_CORES_NEVER 2
+#define MOE_TENSOR_CORE_MIN_TOKENS 256
 
 /* Memory the admission check compares against. The real inspector reads
  * cudaMemGetInfo on spec->device; tests pass a fixed one, as the reference's

@@ -53,6 +53,10 @@ struct Scratch {
     int8_t *aq = nullptr;
     float *ad = nullptr, *as = nullptr, *af_buf = nullptr, *y = nullptr;
     int *err = nullptr;
+    int32_t *tile_off = nullptr;
+    void *a16 = nullptr, *a16dn = nullptr;   // tensor-core path operands (f16)
+    bool tc = false;
+    int slots_cap = 0;
 };
 
 }  // namespace
@@ -292,6 +296,7 @@ size_t layer_device_bytes(const Validated &v)
 struct ScratchDims {
     int Tm, H, E, k, W;
     bool af;
+    bool tc;   // buffers of the tensor-core expert path
 };
 
 // Carves the scratch block (or only measures it when base == nullptr).
@@ -327,22 +332,33 @@ size_t carve_scratch(const ScratchDims &d, uint8_t *base, Scratch *s)
     t.af_buf = d.af ? (float *)take(slots * W * 4) : nullptr;
     t.y = (float *)take(slots * H * 4);
     t.err = (int *)take(4);
+    t.tile_off = (int32_t *)take(4 * (size_t)kTileOffStride * 4);
+    t.a16 = d.tc ? take(slots * H * 2) : nullptr;
+    t.a16dn = d.tc ? take(slots * W * 2) : nullptr;
     if (s && base) {
         void *blk = s->block;
         *s = t;
         s->block = blk;
-        s->Tm = d.Tm; s->H = d.H; s->E = d.E; s->k = d.k; s->W = d.W; s->af = d.af;
+        s->Tm = d.Tm; s->H = d.H; s->E = d.E; s->k = d.k; s->W = d.W; s->af = d.af; s->tc = d.tc;
+        s->slots_cap = (int)slots;
         s->bytes = off;
     }
     return off;
 }
 
-ScratchDims scratch_dims(int Tm, const Validated &v)
+bool tc_possible(const moe_device_spec &spec)
+{
+    if (spec.flags & MOE_FLAG_TENSOR_CORES_NEVER) return false;
+    return (spec.flags & MOE_FLAG_TENSOR_CORES_ALWAYS) || spec.max_tokens >= MOE_TENSOR_CORE_MIN_TOKENS;
+}
+
+ScratchDims scratch_dims(int Tm, const Validated &v, bool tc)
 {
     ScratchDims d;
     d.Tm = Tm; d.H = v.H; d.E = v.E; d.k = v.k;
     d.W = std::max(v.I, v.S);
     d.af = v.down.type == MOE_QUANT_F32 || (v.S && v.sd.type == MOE_QUANT_F32);
+    d.tc = tc && v.gate.type != MOE_QUANT_F32;
     return d;
 }
 
@@ -351,7 +367,8 @@ ScratchDims scratch_dims(int Tm, const Validated &v)
 // dims that are all at least as large serves the layer.
 bool covers(const Scratch &s, const ScratchDims &d)
 {
-    return s.block && s.Tm >= d.Tm && s.H >= d.H && s.E >= d.E && s.k >= d.k && s.W >= d.W && (s.af || !d.af);
+    return s.block && s.Tm >= d.Tm && s.H >= d.H && s.E >= d.E && s.k >= d.k && s.W >= d.W && (s.af || !d.af) &&
+           (s.tc || !d.tc);
 }
 
 ScratchDims merge(const Scratch &s, const ScratchDims &d)
@@ -364,6 +381,7 @@ ScratchDims merge(const Scratch &s, const ScratchDims &d)
     m.k = std::max(s.k, d.k);
     m.W = std::max(s.W, d.W);
     m.af = s.af || d.af;
+    m.tc = s.tc || d.tc;
     return m;
 }
 
@@ -375,6 +393,23 @@ DevMatrix to_dev(const MatrixPlan &p, const uint8_t *qs, const uint8_t *meta)
     m.qs_estride = p.qs_estride; m.meta_estride = p.meta_estride;
     m.qs_rstride = p.qs_rstride; m.meta_rstride = p.meta_rstride;
     return m;
+}
+
+// The tensor-core path takes quantised matrices whose rows are whole 128-row
+// tiles and whose K is whole 64-value steps, when the scratch holds its buffers.
+bool tc_matrix_ok(const DevMatrix &m)
+{
+    return (m.type == FMT_Q4_K || m.type == FMT_Q8_0) && m.rows % 128 == 0 && m.cols % 64 == 0;
+}
+
+bool use_tensor_cores(const moe_device_spec &spec, const LayerStore &L, const Scratch &s, int T)
+{
+    if (!s.tc || (spec.flags & MOE_FLAG_TENSOR_CORES_NEVER)) return false;
+    if (!(spec.flags & MOE_FLAG_TENSOR_CORES_ALWAYS) && T < MOE_TENSOR_CORE_MIN_TOKENS) return false;
+    if (!tc_matrix_ok(L.dev.gate) || !tc_matrix_ok(L.dev.up) || !tc_matrix_ok(L.dev.down)) return false;
+    if (L.S && (!tc_matrix_ok(L.dev.sh_gate) || !tc_matrix_ok(L.dev.sh_up) || !tc_matrix_ok(L.dev.sh_down)))
+        return false;
+    return L.E + 2 <= kTileOffStride;
 }
 
 void free_layer(LayerStore &L)
@@ -452,7 +487,7 @@ int moe_admission_check(const moe_device_spec *spec, const moe_layer_desc *layer
         int rc = validate_desc(nullptr, &layers[i], &v);
         if (rc) return rc;
         weights += layer_device_bytes(v);
-        ScratchDims d = scratch_dims(std::min(spec->max_tokens, 64), v);
+        ScratchDims d = scratch_dims(std::min(spec->max_tokens, 64), v, false);
         if (!have) { acc = d; have = true; }
         else {
             acc.H = std::max(acc.H, d.H); acc.E = std::max(acc.E, d.E); acc.k = std::max(acc.k, d.k);
@@ -465,6 +500,7 @@ int moe_admission_check(const moe_device_spec *spec, const moe_layer_desc *layer
         if (spec->max_tokens > 64) {
             ScratchDims full = acc;
             full.Tm = spec->max_tokens;
+            full.tc = tc_possible(*spec);
             prefill = carve_scratch(full, nullptr, nullptr) - scratch;
         }
     }
@@ -513,7 +549,7 @@ int moe_layer_upload(moe_ctx *ctx, int32_t layer, const moe_layer_desc *desc)
 
     // admission against free HBM before allocating anything
     const size_t wbytes = layer_device_bytes(v);
-    ScratchDims sd = merge(ctx->scratch, scratch_dims(ctx->spec.max_tokens, v));
+    ScratchDims sd = merge(ctx->scratch, scratch_dims(ctx->spec.max_tokens, v, tc_possible(ctx->spec)));
     const size_t sbytes_new = covers(ctx->scratch, sd) ? 0 : carve_scratch(sd, nullptr, nullptr);
     size_t freeb = 0, totalb = 0;
     CUDA_TRY(ctx, cudaMemGetInfo(&freeb, &totalb), "cudaMemGetInfo");
@@ -588,17 +624,22 @@ int moe_layer_upload(moe_ctx *ctx, int32_t layer, const moe_layer_desc *desc)
     L.dev.gate = dev(pg); L.dev.up = dev(pu); L.dev.down = dev(pd);
     L.dev.sh_gate = dev(psg); L.dev.sh_up = dev(psu); L.dev.sh_down = dev(psd);
     // TMA descriptors: each quantised stack is a dense [E*rows][row bytes] array
-    const std::pair<const DevMatrix *, MatMaps *> mats[] = {
-        {&L.dev.gate, &L.maps.gate}, {&L.dev.up, &L.maps.up}, {&L.dev.down, &L.maps.down},
-        {&L.dev.sh_gate, &L.maps.sh_gate}, {&L.dev.sh_up, &L.maps.sh_up}, {&L.dev.sh_down, &L.maps.sh_down}};
+    struct MapSet { const DevMatrix *m; MatMaps *stream, *tc; };
+    const MapSet mats[] = {{&L.dev.gate, &L.maps.gate, &L.maps.gate_tc},
+                           {&L.dev.up, &L.maps.up, &L.maps.up_tc},
+                           {&L.dev.down, &L.maps.down, &L.maps.down_tc},
+                           {&L.dev.sh_gate, &L.maps.sh_gate, &L.maps.sh_gate_tc},
+                           {&L.dev.sh_up, &L.maps.sh_up, &L.maps.sh_up_tc},
+                           {&L.dev.sh_down, &L.maps.sh_down, &L.maps.sh_down_tc}};
     for (const auto &mm : mats) {
-        const DevMatrix &m = *mm.first;
+        const DevMatrix &m = *mm.m;
         if (m.rows && m.type != FMT_F32 &&
             (m.qs_estride != m.qs_rstride * m.rows || m.meta_estride != m.meta_rstride * m.rows)) {
             free_layer(L);
             return fail(ctx, MOE_ERR_CAPABILITY_MISMATCH, "expert slabs are not dense (rows %d)", m.rows);
         }
-        const int r = make_matrix_maps(m, mm.second);
+        int r = make_matrix_maps(m, mm.stream, 32);
+        if (r == 0 && m.rows % 128 == 0) r = make_matrix_maps(m, mm.tc, 128);
         if (r != 0) {
             free_layer(L);
             return fail(ctx, MOE_ERR_CUDA, "cuTensorMapEncodeTiled failed (CUresult %d)", r);
@@ -649,6 +690,10 @@ int moe_forward(moe_ctx *ctx, int32_t layer, int32_t T, const float *x, float *o
     p.problems = s.problems; p.n_active = s.n_active;
     p.aq = s.aq; p.ad = s.ad; p.as = s.as; p.af = s.af_buf; p.W = s.W; p.y = s.y;
     p.err = s.err;
+    p.tile_off = s.tile_off;
+    p.a16 = s.a16; p.a16dn = s.a16dn;
+    p.a16_stride = s.H; p.a16dn_stride = s.W; p.slots_cap = s.slots_cap;
+    p.use_tc = use_tensor_cores(ctx->spec, L, s, T);
 
     if (ptr_kind == MOE_PTR_HOST)
         CUDA_TRY(ctx, cudaMemcpyAsync(s.x, x, (size_t)T * L.H * 4, cudaMemcpyHostToDevice, st), "copy x");

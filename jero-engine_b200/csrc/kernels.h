@@ -32,4 +32,9 @@ cudaError_t launch_down(const FwdParams &p, const LayerDev &L, const LayerMaps &
                         cudaStream_t st);
 cudaError_t launch_combine(const FwdParams &p, cudaStream_t st);
 
+// Tensor-core expert path (gather of the f16 operand, item plan, gate/up and
+// down GEMMs); replaces launch_gate_up / launch_down for large token counts.
+cudaError_t launch_prefill(const FwdParams &p, const LayerDev &L, const LayerMaps &maps, int num_sms,
+                           const Marker &mk, cudaStream_t st);
+
 }  // namespace jmoe

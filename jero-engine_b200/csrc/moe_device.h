@@ -44,8 +44,12 @@ struct MatMaps {
 };
 
 struct LayerMaps {
-    MatMaps gate, up, down, sh_gate, sh_up, sh_down;
+    MatMaps gate, up, down, sh_gate, sh_up, sh_down;            // streaming kernels: 32-row boxes per K-slice
+    MatMaps gate_tc, up_tc, down_tc, sh_gate_tc, sh_up_tc, sh_down_tc;  // tensor-core path: 128-row boxes per 256 values
 };
+
+// Entries per launch layout in FwdParams::tile_off (problems + 2).
+constexpr int kTileOffStride = 260;
 
 // One group of slots that share a weight set: a routed expert, or the shared
 // expert (is_shared = 1, all T tokens in order).
@@ -63,6 +67,7 @@ struct FwdParams {
     int mask_words;              // ceil(T/32)
     int quant_x;                 // x needs int8 blocks (some gate/up matrix is quantised)
     int max_problems;            // grid.y of the expert kernels
+    int use_tc;                  // experts on the tensor-core path (prefill.cu)
 
     const float *x;              // [T][H]
     const float *router;         // [E][H]
@@ -90,6 +95,12 @@ struct FwdParams {
     float *y;                    // [slots][H] expert outputs
     float *out;                  // [T][H]
     int *err;                    // device status word: 0 ok, 1 a bounded wait ran out
+
+    // tensor-core (prefill) path
+    void *a16;                   // [slots_cap][a16_stride] f16: gate/up operand (activation blocks dequantised)
+    void *a16dn;                 // [slots_cap][a16dn_stride] f16: down operand (quantised SwiGLU output)
+    int a16_stride, a16dn_stride, slots_cap;
+    int32_t *tile_off;           // [4][kTileOffStride] work-item offsets of the tensor-core launches
 };
 
 struct LayerDev {
@@ -113,7 +124,15 @@ int launch_forward(const FwdParams &p, const LayerDev &L, const LayerMaps &maps,
 void plan_slices(DevMatrix &m);
 
 // Builds the two TMA descriptors of a quantised stack; returns a CUresult.
-int make_matrix_maps(const DevMatrix &m, MatMaps *out);
+// box_rows 32: one K-slice per box (streaming kernels); box_rows 128: 256 values
+// per box (tensor-core path).
+int make_matrix_maps(const DevMatrix &m, MatMaps *out, int box_rows);
+
+// 2-D tiled TMA descriptor. dtype 0: f16 elements, 1: u64 elements. cols in
+// elements, row_bytes the global row stride, box_cols x box_rows the box,
+// swizzle128: 128-byte swizzle (else none). Returns a CUresult.
+int encode_tiled(CUtensorMap *map, int dtype, const void *base, uint64_t rows, uint64_t cols, uint64_t row_bytes,
+                 uint32_t box_cols, uint32_t box_rows, int swizzle128);
 
 // Stores the message that moe_last_error_message(NULL) returns on this thread.
 void record_error(const char *msg);

@@ -1,5 +1,5 @@
 // tma.cpp -- K-slice planning and TMA tensor-map descriptors for the
-// quantised expert stacks (host side, built once at upload).
+// quantised expert stacks and the tensor-core operands (host side).
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <cuda_runtime.h>
@@ -25,22 +25,22 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn()
     return fn;
 }
 
-// [rows_total][row_bytes] viewed as u64 elements, box = box_rows x box_bytes.
-CUresult encode(CUtensorMap *map, const void *base, uint64_t rows_total, uint64_t row_bytes, uint32_t box_rows,
-                uint32_t box_bytes)
+}  // namespace
+
+int encode_tiled(CUtensorMap *map, int dtype, const void *base, uint64_t rows, uint64_t cols, uint64_t row_bytes,
+                 uint32_t box_cols, uint32_t box_rows, int swizzle128)
 {
     PFN_cuTensorMapEncodeTiled_v12000 fn = encode_fn();
     if (!fn) return CUDA_ERROR_NOT_SUPPORTED;
-    cuuint64_t dims[2] = {row_bytes / 8, rows_total};
+    cuuint64_t dims[2] = {cols, rows};
     cuuint64_t strides[1] = {row_bytes};
-    cuuint32_t box[2] = {box_bytes / 8, box_rows};
+    cuuint32_t box[2] = {box_cols, box_rows};
     cuuint32_t estr[2] = {1, 1};
-    return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, const_cast<void *>(base), dims, strides, box, estr,
-              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+    return fn(map, dtype == 0 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT64, 2,
+              const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+              swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
 }
-
-}  // namespace
 
 // A K-slice is at most 1024 values (Q4_K) or 512 (Q8_0), a whole number of
 // super-blocks, so one ring stage (2 matrices x 32 rows) stays near 36 KB and
@@ -60,14 +60,20 @@ void plan_slices(DevMatrix &m)
     }
 }
 
-int make_matrix_maps(const DevMatrix &m, MatMaps *out)
+// Each quantised stack is the dense array [E*rows][row bytes] of u64 elements.
+// box_rows 32: the streaming kernels' K-slice boxes; box_rows 128: the
+// tensor-core path's 256-value boxes (Q4_K 128 bytes, Q8_0 256 bytes of quants,
+// 16 bytes of scales per row).
+int make_matrix_maps(const DevMatrix &m, MatMaps *out, int box_rows)
 {
     memset(out, 0, sizeof *out);
     if (m.type != FMT_Q4_K && m.type != FMT_Q8_0) return CUDA_SUCCESS;
     const uint64_t rows_total = (uint64_t)m.n_experts * m.rows;
-    CUresult r = encode(&out->qs, m.qs, rows_total, m.qs_rstride, 32, (uint32_t)m.qs_box);
+    const uint32_t qbox = box_rows == 32 ? (uint32_t)m.qs_box : (m.type == FMT_Q4_K ? 128u : 256u);
+    const uint32_t mbox = box_rows == 32 ? (uint32_t)m.meta_box : 16u;
+    int r = encode_tiled(&out->qs, 1, m.qs, rows_total, m.qs_rstride / 8, m.qs_rstride, qbox / 8, box_rows, 0);
     if (r != CUDA_SUCCESS) return r;
-    return encode(&out->meta, m.meta, rows_total, m.meta_rstride, 32, (uint32_t)m.meta_box);
+    return encode_tiled(&out->meta, 1, m.meta, rows_total, m.meta_rstride / 8, m.meta_rstride, mbox / 8, box_rows, 0);
 }
 
 }  // namespace jmoe

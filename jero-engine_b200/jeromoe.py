@@ -38,6 +38,8 @@ F32, Q8_0, Q4_K = 0, 8, 12
 QUANT_NAMES = {F32: "F32", Q8_0: "Q8_0", Q4_K: "Q4_K"}
 ROUTE_SOFTMAX_TOPK, ROUTE_GROUP_LIMITED = 0, 1
 PTR_HOST, PTR_DEVICE = 0, 1
+FLAG_TENSOR_CORES_ALWAYS, FLAG_TENSOR_CORES_NEVER = 1, 2
+TENSOR_CORE_MIN_TOKENS = 256
 
 
 class MoeError(RuntimeError):
@@ -306,8 +308,9 @@ def layer_desc(weights: ModelWeights, layer: int, num_experts: int, top_k: int, 
 class Context:
     """One device context (moe_ctx): device-resident layers + forward scratch."""
 
-    def __init__(self, device: int = 0, max_tokens: int = 64, max_layers: int = 1, reserve_bytes: int = 0):
-        spec = moe_device_spec(device, max_tokens, max_layers, 0, reserve_bytes)
+    def __init__(self, device: int = 0, max_tokens: int = 64, max_layers: int = 1, reserve_bytes: int = 0,
+                 flags: int = 0):
+        spec = moe_device_spec(device, max_tokens, max_layers, flags, reserve_bytes)
         h = C.c_void_p()
         _check(lib.moe_ctx_create(C.byref(spec), C.byref(h)))
         self.h = h

@@ -21,8 +21,8 @@ W_RTOL = 1e-5
 KATS = load_kats()
 
 
-def gpu_layer(weights, E, k, I, use_shared, route, hidden, max_tokens, layer=0):
-    ctx = jm.Context(0, max_tokens, layer + 1)
+def gpu_layer(weights, E, k, I, use_shared, route, hidden, max_tokens, layer=0, flags=0):
+    ctx = jm.Context(0, max_tokens, layer + 1, flags=flags)
     d, keep = jm.layer_desc(weights, layer, E, k, I, use_shared, route, hidden)
     ctx.upload(layer, d)
     return ctx
@@ -163,6 +163,48 @@ def test_gpu_cfg4_skewed(T):
 
 def test_gpu_cfg5_group_limited():
     _full_size_parity(5, 8192, sample=12)
+
+
+# ------------------------------------------------- tensor-core expert path
+
+# Small layers whose matrices are whole 128-row tiles, forced onto the
+# tensor-core path (f16 operands, f32 accumulation) for every T.
+TC_CASES = {
+    "cfg2_q4k": (2, dict(E=16, I=256, H=512)),
+    "cfg1_q8_0": (1, dict(E=16, I=256, H=512)),
+    "cfg3_shared_q8_down": (3, dict(E=16, k=4, I=384, S=512, H=512)),
+    "cfg5_groups_shared": (5, dict(E=32, k=6, I=256, S=512, H=512, n_groups=8, topk_groups=3)),
+}
+
+
+@pytest.mark.parametrize("name", list(TC_CASES))
+@pytest.mark.parametrize("T", [1, 37, 300])
+def test_gpu_tensor_core_path(name, T):
+    cid, over = TC_CASES[name]
+    cfg = synth.CONFIGS[cid].scaled(**over)
+    w = synth.build_weights(cfg)
+    x = synth.gen_x(cfg, T)
+    with gpu_layer(w, cfg.E, cfg.k, cfg.I, cfg.S > 0, cfg.route, cfg.H, T, flags=jm.FLAG_TENSOR_CORES_ALWAYS) as ctx:
+        out, si, sw = ctx.forward(0, x)
+        prof_ok = ctx.device_status() == 0
+    assert prof_ok
+    ref = oracle_layer(w, cfg).forward(x, 8)
+    err = assert_parity(out, si, sw, *ref)
+    assert err < 5e-3, err
+
+
+def test_gpu_tensor_core_matches_streaming_path():
+    """Both expert paths on the same layer and tokens: same routing, outputs
+    within the tolerance (the tensor-core path rounds operands to f16)."""
+    cfg = synth.CONFIGS[2].scaled(E=32, I=256, H=512)
+    w = synth.build_weights(cfg)
+    x = synth.gen_x(cfg, 200)
+    outs = []
+    for flags in (jm.FLAG_TENSOR_CORES_ALWAYS, jm.FLAG_TENSOR_CORES_NEVER):
+        with gpu_layer(w, cfg.E, cfg.k, cfg.I, False, cfg.route, cfg.H, 200, flags=flags) as ctx:
+            outs.append(ctx.forward(0, x))
+    np.testing.assert_array_equal(outs[0][1], outs[1][1])
+    assert row_rel_err(outs[0][0], outs[1][0]).max() <= OUT_TOL
 
 
 # ------------------------------------------------------------- edge cases
