@@ -33,11 +33,14 @@ constexpr int kRingBudget = 80 * 1024;
 constexpr int kErrTimeout = 1;
 
 // Bounded mbarrier wait: gives up (and flags the CTA and the forward) after
-// kWaitCycles or when another thread of the CTA gave up.
+// kWaitCycles or when another thread of the CTA gave up. A waiting warp sleeps
+// in try_wait (suspend hint) rather than spinning, leaving the issue slots to
+// the warps with work; the flag and the clock are read only on a timeout.
 __device__ __forceinline__ bool wait_bar(uint64_t *bar, uint32_t parity, volatile int *abort_flag, int *err)
 {
+    if (mbar_try_wait(bar, parity)) return true;
     const long long t0 = clock64();
-    while (!mbar_try_wait(bar, parity)) {
+    while (!mbar_try_wait_sleep(bar, parity, 20000)) {
         if (*abort_flag) return false;
         if (clock64() - t0 > kWaitCycles) {
             *abort_flag = 1;
@@ -121,7 +124,7 @@ __device__ __forceinline__ void drain(const Smem &s, int stages, uint32_t g)
 {
     for (uint32_t k = g > (uint32_t)stages ? g - stages : 0; k < g; k++) {
         const long long t0 = clock64();
-        while (!mbar_try_wait(&s.full[k % stages], (k / stages) & 1))
+        while (!mbar_try_wait_sleep(&s.full[k % stages], (k / stages) & 1, 20000))
             if (clock64() - t0 > kWaitCycles) break;
     }
 }
@@ -226,7 +229,7 @@ __device__ __forceinline__ void consume_chunk(const Smem &s, const StreamCfg &c,
 // Consumer side of one (item, token tile) with NT tokens: all K-slices of the
 // 32-row tile, then the 8-lane reduction. Returns false when a wait gave up.
 template <int FMT, int NMAT, int NT>
-__device__ __forceinline__ bool consume_tile(const Smem &s, const StreamCfg &c, uint32_t &g, int K, int nu_s,
+__device__ __forceinline__ bool consume_tile(const Smem &s, const StreamCfg &c, RingPos &g, int K, int nu_s,
                                              int *err, float (&out)[NMAT][NT], int rw,
                                              int l8)
 {
@@ -237,14 +240,14 @@ __device__ __forceinline__ bool consume_tile(const Smem &s, const StreamCfg &c, 
         for (int t = 0; t < NT; t++) acc[m][t] = 0.0f;
     const int ns = (K + c.ks - 1) / c.ks;
     for (int sl = 0; sl < ns; sl++) {
-        const int st = g % c.stages;
-        if (!wait_bar(&s.full[st], (g / c.stages) & 1, s.abort_flag, err)) return false;
+        const int st = g.slot;
+        if (!wait_bar(&s.full[st], g.phase, s.abort_flag, err)) return false;
         const int ks_cur = min(c.ks, K - sl * c.ks);
         consume_chunk<FMT, NMAT, NT>(s, c, s.ring + (size_t)st * c.stage_bytes, rw, l8, ks_cur >> 5, sl * (c.ks >> 5),
                                      nu_s, acc);
         __syncwarp();
         if ((threadIdx.x & 31) == 0) mbar_arrive(&s.empty[st]);
-        g++;
+        g.advance(c.stages);
     }
 #pragma unroll
     for (int m = 0; m < NMAT; m++)
@@ -303,7 +306,8 @@ __global__ void __launch_bounds__(kStreamThreads, 2)
 
     if (warp == kConsumerWarps) {   // producer: one thread issues the TMA boxes
         if (lane != 0) return;
-        uint32_t g = 0;
+        RingPos r;
+        uint32_t g = 0;   // uses issued, for the drain after an abort
         for (int it = it0; it < it1; it++) {
             const Item x = item_at(p, c, nr, it);
             const MatMaps *mm[NMAT];
@@ -322,13 +326,12 @@ __global__ void __launch_bounds__(kStreamThreads, 2)
             const int tiles = (x.pr.count + kTT - 1) / kTT, ns = (K + c.ks - 1) / c.ks;
             for (int tt = 0; tt < tiles; tt++) {
                 for (int sl = 0; sl < ns; sl++) {
-                    const int st = g % c.stages;
-                    const uint32_t use = g / c.stages;
-                    if (use > 0 && !wait_bar(&s.empty[st], (use - 1) & 1, s.abort_flag, p.err)) {
+                    if (!wait_bar(&s.empty[r.slot], r.phase ^ 1u, s.abort_flag, p.err)) {
                         drain(s, c.stages, g);
                         return;
                     }
-                    produce_chunk(s, c, st, mm, NMAT, y, sl);
+                    produce_chunk(s, c, r.slot, mm, NMAT, y, sl);
+                    r.advance(c.stages);
                     g++;
                 }
             }
@@ -337,7 +340,7 @@ __global__ void __launch_bounds__(kStreamThreads, 2)
     }
 
     // consumers
-    uint32_t g = 0;
+    RingPos g;
     int staged_slot = -1, staged_tile = -1;
     const int rw = warp * 4 + (lane >> 3), l8 = lane & 7;
     const int nu_s = c.act_k >> 5;

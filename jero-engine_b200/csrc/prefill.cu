@@ -1,17 +1,23 @@
 // prefill.cu -- grouped expert GEMMs on the 5th-generation tensor cores for
 // large token counts (tcgen05.mma kind::f16, fp32 accumulators in TMEM).
 //
-// Tile: 128 slots (M, TMEM lanes) x 128 weight rows (N) of one expert, K in
-// steps of 64. Operands are K-major in the 128-byte swizzle layout:
-//   A = the problem's activations in f16, rows in slot order, loaded by TMA;
-//   B = the expert's weight rows, TMA-loaded as GGUF blocks (Q4_K / Q8_0) per
-//       256-value super-step and expanded to f16 by eight dequant warps.
-// gate/up tiles carry two accumulators (gate, up); their epilogue applies
+// One work item is (problem, 128 weight rows, chunk of up to 128 / 256 slots).
+// The MMA runs with the weights as the M = 128 operand and the expert's token
+// slots as N (a multiple of 16 up to the chunk cap), so the tensor work follows
+// the expert's real token count instead of padding it to a 128-slot tile:
+//   A = weight rows, TMA-loaded as GGUF blocks (Q4_K / Q8_0) in the 128-byte
+//       swizzle and expanded to f16 by eight dequant warps;
+//   B = the problem's activation slots in f16, TMA-loaded (boxes of 32 rows).
+// Both are K-major in the 128-byte swizzle layout. Each aligned group of four
+// K positions holds the values (0, 2, 1, 3): that is the order in which the
+// dequant warps unpack a 32-bit word of quants, and the activation operands
+// are written in the same order, so the dot products are unchanged.
+// gate/up items carry two accumulators (gate, up); their epilogue applies
 // SwiGLU and the int8 block quantiser of the decode path (so both paths feed
 // the down projection the same values) and stores the down operand in f16.
-// down tiles store y in f32. Work items (problem, n-tile, m-tile) are spread
-// over a persistent grid, m-tiles innermost so neighbouring CTAs share a
-// weight tile in L2. Every wait is bounded.
+// down items store y in f32. Items are spread over a persistent grid, slot
+// chunks innermost so neighbouring CTAs share a weight tile in L2. Every wait
+// is bounded.
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <math.h>
@@ -24,34 +30,45 @@
 namespace jmoe {
 namespace {
 
-constexpr int kTM = 128, kTN = 128, kKS = 64, kSuper = 256;
+constexpr int kM = 128;                         // weight rows per item (MMA M, TMEM lanes)
+constexpr int kKS = 64;                         // K per stage: one 128-byte swizzled row of f16
+constexpr int kCapGU = 128, kCapDN = 256;       // slots per item (MMA N) of the gate/up and down launches
+constexpr int kXBoxRows = 32, kXBoxBytes = kXBoxRows * 128;
 constexpr int kWarpTma = 0, kWarpMma = 1, kDeqWarp0 = 2, kDeqWarps = 8, kEpiWarp0 = 10, kEpiWarps = 4;
 constexpr int kTcThreads = (kEpiWarp0 + kEpiWarps) * 32;
-constexpr int kAStages = 4, kBStages = 2, kQStages = 2;
+constexpr int kMaxStages = 6;
+constexpr int kTmemCols = 512, kAccCols = 256;  // two accumulator buffers of 256 columns
 constexpr long long kWaitCycles = 4000000000LL;
 constexpr int kErrTimeout = 1;
-constexpr int kATileBytes = kTM * kKS * 2;    // 16 KB
-constexpr int kBTileBytes = kTN * kKS * 2;    // 16 KB per matrix
+constexpr int kWTileBytes = kM * 128;           // dequantised weights: one matrix, one K step (16 KB)
+constexpr int kQuantBox = kM * 128;             // quants of one matrix per quantised stage (16 KB)
+constexpr int kQBytes = kQuantBox + kM * 16;    // + 16 bytes of scales per row (18 KB)
 
 struct TcCfg {
-    int nmat;        // 2: gate + up, 1: down
-    int mode;        // 0 routed problems, 1 shared only, 2 both
-    int qs_box;      // bytes of one row's quants per 256-value super-step
-    int q_bytes;     // bytes of one quantized stage per matrix (quants + scales, 128 rows)
-    int qstages;     // quantized stages in flight (1 or 2, by shared-memory room)
-    int smem_a, smem_b, smem_q, smem_bar;   // region offsets
+    int mode;                // 0 routed problems, 1 shared only, 2 both
+    int cap;                 // slots per item
+    int xst, wst, qst;       // ring depths: activation tiles, dequantised tiles, quantised stages
+    int x_bytes;             // bytes of one activation stage (cap rows)
+    int max_q;               // capacity of the item table
+    int smem_x, smem_w, smem_q, smem_tab, smem_bar;   // region offsets
 };
 
 struct TcMaps {
-    CUtensorMap a;                        // activations f16 [slots][K], box 64 x 128, swizzle 128B
-    CUtensorMap wq[2], wm[2];             // routed weights: quants, scales (box 128 rows)
+    CUtensorMap a;                        // activations f16 [slots][K], box 64 x 32, swizzle 128B
+    CUtensorMap wq[2], wm[2];             // routed weights: quants (swizzle 128B), scales (box 128 rows)
     CUtensorMap sq[2], sm[2];             // shared expert weights
 };
 
+// Waiting warps sleep in try_wait (suspend hint) instead of spinning, so they
+// leave the issue slots to the dequant and epilogue warps; the abort flag and
+// the clock are checked only when a try_wait times out.
+constexpr uint32_t kSleepNs = 20000;
+
 __device__ __forceinline__ bool tc_wait(uint64_t *bar, uint32_t parity, volatile int *abort_flag, int *err)
 {
+    if (mbar_try_wait(bar, parity)) return true;
     const long long t0 = clock64();
-    while (!mbar_try_wait(bar, parity)) {
+    while (!mbar_try_wait_sleep(bar, parity, kSleepNs)) {
         if (*abort_flag) return false;
         if (clock64() - t0 > kWaitCycles) {
             *abort_flag = 1;
@@ -62,68 +79,89 @@ __device__ __forceinline__ bool tc_wait(uint64_t *bar, uint32_t parity, volatile
     return true;
 }
 
+// Bounded wait used while draining after an abort (no error recorded).
+__device__ __forceinline__ void drain_wait(uint64_t *bar, uint32_t parity)
+{
+    const long long t0 = clock64();
+    while (!mbar_try_wait_sleep(bar, parity, kSleepNs) && clock64() - t0 < kWaitCycles) {}
+}
+
 struct TcItem {
-    Problem pr;
+    int expert, slot, n, nt;   // n: slots of this item (1..cap)
     bool shared;
-    int mt, nt;
 };
 
-// tile_off[0..nq]: first item of each problem of the launch (routed problems in
-// list order, then the shared expert); binary search for the item's problem.
-__device__ __forceinline__ TcItem tc_item(const FwdParams &p, const int32_t *tile_off, int nq, int n_routed, int it)
+// Slot chunks of a problem: ceil(count / cap) chunks of equal size rounded up
+// to 16 (the MMA's N granularity); the last one takes the remainder.
+__device__ __forceinline__ int chunk_count(int count, int cap) { return (count + cap - 1) / cap; }
+__device__ __forceinline__ int chunk_size(int count, int nch) { return (((count + nch - 1) / nch) + 15) & ~15; }
+
+// The item table lives in shared memory: s_off[0..nq] is the first item of
+// each problem of the launch (routed problems in list order, then the shared
+// expert), s_prob[q] = (expert, slot0, count, is_shared).
+__device__ __forceinline__ TcItem tc_item(const int *s_off, const int4 *s_prob, int nq, int cap, int it)
 {
     int lo = 0, hi = nq - 1;
     while (lo < hi) {
         const int mid = (lo + hi + 1) >> 1;
-        if (tile_off[mid] <= it) lo = mid;
+        if (s_off[mid] <= it) lo = mid;
         else hi = mid - 1;
     }
+    const int4 pr = s_prob[lo];
+    const int nch = chunk_count(pr.z, cap), base = chunk_size(pr.z, nch);
+    const int local = it - s_off[lo];
+    const int ch = local % nch;
     TcItem x;
-    x.shared = lo >= n_routed;
-    x.pr = x.shared ? p.problems[p.max_problems - 1] : p.problems[lo];
-    const int mtiles = (x.pr.count + kTM - 1) / kTM;
-    const int local = it - tile_off[lo];
-    x.mt = local % mtiles;
-    x.nt = local / mtiles;
+    x.nt = local / nch;
+    x.expert = pr.x;
+    x.slot = pr.y + ch * base;
+    x.n = min(base, pr.z - ch * base);
+    x.shared = pr.w != 0;
     return x;
 }
 
-// Four f16 pairs of one 8-value chunk of a Q4_K sub-block: nibbles from the
-// 8 bytes (w0, w1), high nibbles when hi; w = q * dsc - dmn in one HFMA2.
-__device__ __forceinline__ uint4 q4_chunk_f16(uint32_t w0, uint32_t w1, bool hi, __half2 dsc, __half2 ndmn)
+// Output position of K index f within its group of four: (0, 2, 1, 3).
+__device__ __forceinline__ int k_perm(int f) { return (f & ~3) | ((f & 1) << 1) | ((f >> 1) & 1); }
+
+__device__ __forceinline__ uint32_t h2_bits(__half2 h) { return *reinterpret_cast<uint32_t *>(&h); }
+__device__ __forceinline__ __half2 bits_h2(uint32_t v) { return *reinterpret_cast<__half2 *>(&v); }
+
+// 16 values of a Q4_K sub-block word pair are unpacked per 32-bit quant word w
+// (bytes b0..b3): halves (b0, b2) and (b1, b3) of the low nibbles, then of the
+// high nibbles. 0x6400 | q is the f16 1024 + q; 0x6400 | (q << 4) is 1024 + 16q,
+// which (x / 16 - 64) turns into q exactly. Weight = q * dsc - dmn.
+__device__ __forceinline__ void q4_word_f16(uint32_t w, __half2 dsc, __half2 ndmn, uint32_t &lo0, uint32_t &lo1,
+                                            uint32_t &hi0, uint32_t &hi1)
 {
     const __half2 k1024 = __half2half2(__ushort_as_half(0x6400));
-    uint32_t src[4] = {__byte_perm(w0, 0, 0x4140), __byte_perm(w0, 0, 0x4342), __byte_perm(w1, 0, 0x4140),
-                       __byte_perm(w1, 0, 0x4342)};
-    uint4 out;
-    uint32_t *o = &out.x;
-#pragma unroll
-    for (int i = 0; i < 4; i++) {
-        uint32_t v = hi ? (src[i] >> 4) : src[i];
-        v = (v & 0x000F000Fu) | 0x64006400u;               // f16 (1024 + q) in each half
-        __half2 q = __hsub2(*reinterpret_cast<__half2 *>(&v), k1024);
-        __half2 w = __hfma2(q, dsc, ndmn);
-        o[i] = *reinterpret_cast<uint32_t *>(&w);
-    }
-    return out;
+    const __half2 k16th = __half2half2(__ushort_as_half(0x2C00));   // 1/16
+    const __half2 km64 = __half2half2(__ushort_as_half(0xD400));    // -64
+    const uint32_t w8 = w >> 8;
+    const __half2 l0 = __hsub2(bits_h2((w & 0x000F000Fu) | 0x64006400u), k1024);
+    const __half2 l1 = __hsub2(bits_h2((w8 & 0x000F000Fu) | 0x64006400u), k1024);
+    const __half2 h0 = __hfma2(bits_h2((w & 0x00F000F0u) | 0x64006400u), k16th, km64);
+    const __half2 h1 = __hfma2(bits_h2((w8 & 0x00F000F0u) | 0x64006400u), k16th, km64);
+    lo0 = h2_bits(__hfma2(l0, dsc, ndmn));
+    lo1 = h2_bits(__hfma2(l1, dsc, ndmn));
+    hi0 = h2_bits(__hfma2(h0, dsc, ndmn));
+    hi1 = h2_bits(__hfma2(h1, dsc, ndmn));
 }
 
-// Eight f16 values of a Q8_0 block: signed bytes (w0, w1) times the f16 scale.
-__device__ __forceinline__ uint4 q8_chunk_f16(uint32_t w0, uint32_t w1, __half2 d)
+// Four Q8_0 values of word w (signed bytes b0..b3) as halves (b0, b2), (b1, b3):
+// (byte ^ 0x80) | 0x6400 is the f16 1024 + 128 + b.
+__device__ __forceinline__ void q8_word_f16(uint32_t w, __half2 d, uint32_t &o0, uint32_t &o1)
 {
-    const __half2 k1152 = __half2half2(__ushort_as_half(0x6480));   // 1024 + 128
-    uint32_t src[4] = {__byte_perm(w0, 0, 0x4140), __byte_perm(w0, 0, 0x4342), __byte_perm(w1, 0, 0x4140),
-                       __byte_perm(w1, 0, 0x4342)};
-    uint4 out;
-    uint32_t *o = &out.x;
-#pragma unroll
-    for (int i = 0; i < 4; i++) {
-        uint32_t v = (src[i] ^ 0x00800080u) | 0x64006400u;   // f16 (1024 + q + 128)
-        __half2 q = __hsub2(*reinterpret_cast<__half2 *>(&v), k1152);
-        __half2 w = __hmul2(q, d);
-        o[i] = *reinterpret_cast<uint32_t *>(&w);
-    }
-    return out;
+    const __half2 k1152 = __half2half2(__ushort_as_half(0x6480));
+    const __half2 e = __hsub2(bits_h2((w & 0x00FF00FFu) ^ 0x64806480u), k1152);
+    const __half2 o = __hsub2(bits_h2(((w >> 8) & 0x00FF00FFu) ^ 0x64806480u), k1152);
+    o0 = h2_bits(__hmul2(e, d));
+    o1 = h2_bits(__hmul2(o, d));
+}
+
+__device__ __forceinline__ void sts128(uint32_t a, uint4 v)
+{
+    asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+                 : "memory");
 }
 
 template <int FMT, int NMAT>
@@ -133,240 +171,253 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     // 1024-byte alignment of the operand tiles (swizzle atoms)
     uint8_t *base = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
-    uint8_t *sa = base + c.smem_a, *sb = base + c.smem_b, *sq = base + c.smem_q;
+    uint8_t *sx = base + c.smem_x, *sw = base + c.smem_w, *sq = base + c.smem_q;
+    int *s_off = reinterpret_cast<int *>(base + c.smem_tab);
+    int4 *s_prob = reinterpret_cast<int4 *>(s_off + ((c.max_q + 4) & ~3));
     uint64_t *bars = reinterpret_cast<uint64_t *>(base + c.smem_bar);
-    uint64_t *a_full = bars, *a_empty = a_full + kAStages;
-    uint64_t *b_full = a_empty + kAStages, *b_empty = b_full + kBStages;
-    uint64_t *q_full = b_empty + kBStages, *q_empty = q_full + kQStages;
-    uint64_t *acc_full = q_empty + kQStages, *acc_empty = acc_full + 2, *drain_bar = acc_empty + 2;
+    uint64_t *x_full = bars, *x_empty = x_full + kMaxStages;
+    uint64_t *w_full = x_empty + kMaxStages, *w_empty = w_full + kMaxStages;
+    uint64_t *q_full = w_empty + kMaxStages, *q_empty = q_full + kMaxStages;
+    uint64_t *acc_full = q_empty + kMaxStages, *acc_empty = acc_full + 2, *drain_bar = acc_empty + 2;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain_bar + 1);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    constexpr int QK = FMT == FMT_Q4_K ? 4 : 2;   // K steps per quantised stage (256 / 128 values)
+
+    // the launch's problems: routed ones, then the shared expert
+    const int n_routed = c.mode == 1 ? 0 : *p.n_active;
+    const bool with_shared = c.mode != 0 && p.S > 0;
+    const int nq = min(n_routed + (with_shared ? 1 : 0), c.max_q);
+    const int32_t *tile_off = p.tile_off + (NMAT == 2 ? 0 : 2 * kTileOffStride) + (c.mode == 1 ? kTileOffStride : 0);
+    for (int i = threadIdx.x; i <= nq; i += blockDim.x) s_off[i] = tile_off[i];
+    for (int i = threadIdx.x; i < nq; i += blockDim.x) {
+        const bool sh = i >= n_routed;
+        const Problem pr = sh ? p.problems[p.max_problems - 1] : p.problems[i];
+        s_prob[i] = make_int4(pr.expert, pr.slot0, pr.count, sh ? 1 : 0);
+    }
     if (threadIdx.x == 0) {
-        for (int i = 0; i < kAStages; i++) { mbar_init(&a_full[i], 1); mbar_init(&a_empty[i], 1); }
-        for (int i = 0; i < kBStages; i++) { mbar_init(&b_full[i], kDeqWarps); mbar_init(&b_empty[i], 1); }
-        for (int i = 0; i < kQStages; i++) { mbar_init(&q_full[i], 1); mbar_init(&q_empty[i], kDeqWarps); }
+        for (int i = 0; i < c.xst; i++) { mbar_init(&x_full[i], 1); mbar_init(&x_empty[i], 1); }
+        for (int i = 0; i < c.wst; i++) { mbar_init(&w_full[i], kDeqWarps); mbar_init(&w_empty[i], 1); }
+        for (int i = 0; i < c.qst; i++) { mbar_init(&q_full[i], 1); mbar_init(&q_empty[i], kDeqWarps); }
         for (int i = 0; i < 2; i++) { mbar_init(&acc_full[i], 1); mbar_init(&acc_empty[i], kEpiWarps); }
         mbar_init(drain_bar, 1);
         *abort_flag = 0;
         fence_barrier_init();
     }
-    if (warp == kWarpMma) tmem_alloc(tmem_slot, NMAT == 2 ? 512 : 256);
+    if (warp == kWarpMma) tmem_alloc(tmem_slot, kTmemCols);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-
-    // the launch's problems: routed ones, then the shared expert
-    const int n_routed = c.mode == 1 ? 0 : *p.n_active;
-    const bool with_shared = c.mode != 0 && p.S > 0;
-    const int nq = n_routed + (with_shared ? 1 : 0);
-    const int32_t *tile_off = p.tile_off + (NMAT == 2 ? 0 : 2 * kTileOffStride) + (c.mode == 1 ? kTileOffStride : 0);
-    const int total = nq > 0 ? tile_off[nq] : 0;
+    const int total = nq > 0 ? s_off[nq] : 0;
 
     if (warp == kWarpTma) {
         if (lane == 0) {
-            uint32_t ga = 0, gq = 0;
+            RingPos xr, qr;
+            uint32_t gx = 0, gq = 0;   // uses issued, for the drain after an abort
             bool ok = true;
             for (int it = blockIdx.x; it < total && ok; it += gridDim.x) {
-                const TcItem x = tc_item(p, tile_off, nq, n_routed, it);
+                const TcItem x = tc_item(s_off, s_prob, nq, c.cap, it);
                 const DevMatrix &M0 = NMAT == 2 ? (x.shared ? L.sh_gate : L.gate) : (x.shared ? L.sh_down : L.down);
-                const int K = M0.cols, nk = (K + kKS - 1) / kKS;
-                const int ay = x.pr.slot0 + x.mt * kTM, wy = x.pr.expert * M0.rows + x.nt * kTN;
-                for (int kk = 0; kk < nk && ok; kk++) {
-                    if ((kk & 3) == 0) {
-                        const int s = gq % c.qstages;
-                        if (gq >= (uint32_t)c.qstages && !tc_wait(&q_empty[s], ((gq / c.qstages) - 1) & 1, abort_flag, p.err)) { ok = false; break; }
-                        mbar_arrive_expect_tx(&q_full[s], (uint32_t)(NMAT * c.q_bytes));
-                        for (int m = 0; m < NMAT; m++) {
-                            uint8_t *dst = sq + (size_t)(s * NMAT + m) * c.q_bytes;
-                            const CUtensorMap *mq = x.shared ? &maps.sq[m] : &maps.wq[m];
-                            const CUtensorMap *mm = x.shared ? &maps.sm[m] : &maps.wm[m];
-                            tma_load_2d(dst, mq, (kk >> 2) * (c.qs_box / 8), wy, &q_full[s]);
-                            tma_load_2d(dst + kTN * c.qs_box, mm, (kk >> 2) * 2, wy, &q_full[s]);
+                const int nk = M0.cols / kKS;
+                const int wy = x.expert * M0.rows + x.nt * kM;
+                const int nbox = (x.n + kXBoxRows - 1) / kXBoxRows;
+                const CUtensorMap *mq0 = x.shared ? &maps.sq[0] : &maps.wq[0], *mm0 = x.shared ? &maps.sm[0] : &maps.wm[0];
+                const CUtensorMap *mq1 = x.shared ? &maps.sq[1] : &maps.wq[1], *mm1 = x.shared ? &maps.sm[1] : &maps.wm[1];
+                for (int kk = 0; kk < nk; kk++) {
+                    if ((kk & (QK - 1)) == 0) {
+                        if (!tc_wait(&q_empty[qr.slot], qr.phase ^ 1u, abort_flag, p.err)) { ok = false; break; }
+                        uint64_t *bar = &q_full[qr.slot];
+                        mbar_arrive_expect_tx(bar, (uint32_t)(NMAT * kQBytes));
+                        uint8_t *dst = sq + (size_t)qr.slot * NMAT * kQBytes;
+                        tma_load_2d(dst, mq0, (kk / QK) * 16, wy, bar);
+                        tma_load_2d(dst + kQuantBox, mm0, (kk >> 2) * 2, wy, bar);
+                        if (NMAT == 2) {
+                            tma_load_2d(dst + kQBytes, mq1, (kk / QK) * 16, wy, bar);
+                            tma_load_2d(dst + kQBytes + kQuantBox, mm1, (kk >> 2) * 2, wy, bar);
                         }
+                        qr.advance(c.qst);
                         gq++;
                     }
-                    const int s = ga % kAStages;
-                    if (ga >= (uint32_t)kAStages && !tc_wait(&a_empty[s], ((ga / kAStages) - 1) & 1, abort_flag, p.err)) { ok = false; break; }
-                    mbar_arrive_expect_tx(&a_full[s], (uint32_t)kATileBytes);
-                    tma_load_2d(sa + (size_t)s * kATileBytes, &maps.a, kk * kKS, ay, &a_full[s]);
-                    ga++;
+                    if (!tc_wait(&x_empty[xr.slot], xr.phase ^ 1u, abort_flag, p.err)) { ok = false; break; }
+                    uint64_t *bar = &x_full[xr.slot];
+                    mbar_arrive_expect_tx(bar, (uint32_t)(nbox * kXBoxBytes));
+                    uint8_t *dst = sx + (size_t)xr.slot * c.x_bytes;
+                    for (int b = 0; b < nbox; b++)
+                        tma_load_2d(dst + b * kXBoxBytes, &maps.a, kk * kKS, x.slot + b * kXBoxRows, bar);
+                    xr.advance(c.xst);
+                    gx++;
                 }
             }
             if (!ok) {   // wait (bounded) for the copies still in flight
-                for (uint32_t g = ga > (uint32_t)kAStages ? ga - kAStages : 0; g < ga; g++) {
-                    const long long t0 = clock64();
-                    while (!mbar_try_wait(&a_full[g % kAStages], (g / kAStages) & 1) && clock64() - t0 < kWaitCycles) {}
-                }
-                for (uint32_t g = gq > (uint32_t)c.qstages ? gq - c.qstages : 0; g < gq; g++) {
-                    const long long t0 = clock64();
-                    while (!mbar_try_wait(&q_full[g % c.qstages], (g / c.qstages) & 1) && clock64() - t0 < kWaitCycles) {}
-                }
+                for (uint32_t g = gx > (uint32_t)c.xst ? gx - c.xst : 0; g < gx; g++)
+                    drain_wait(&x_full[g % c.xst], (g / c.xst) & 1);
+                for (uint32_t g = gq > (uint32_t)c.qst ? gq - c.qst : 0; g < gq; g++)
+                    drain_wait(&q_full[g % c.qst], (g / c.qst) & 1);
             }
         }
     } else if (warp == kWarpMma) {
         if (lane == 0) {
-            // instruction descriptor: f32 accumulate, f16 A and B, both K-major, N = 128, M = 128
-            const uint32_t idesc = (1u << 4) | ((uint32_t)(kTN >> 3) << 17) | ((uint32_t)(kTM >> 4) << 24);
-            uint32_t ga = 0, gb = 0, gt = 0;
+            RingPos xr, wr, ar;
             bool ok = true, issued = false;
             for (int it = blockIdx.x; it < total && ok; it += gridDim.x) {
-                const TcItem x = tc_item(p, tile_off, nq, n_routed, it);
+                const TcItem x = tc_item(s_off, s_prob, nq, c.cap, it);
                 const int K = NMAT == 2 ? (x.shared ? L.sh_gate.cols : L.gate.cols)
                                         : (x.shared ? L.sh_down.cols : L.down.cols);
-                const int nk = (K + kKS - 1) / kKS;
-                const int buf = gt & 1;
-                if (gt >= 2 && !tc_wait(&acc_empty[buf], ((gt >> 1) - 1) & 1, abort_flag, p.err)) { ok = false; break; }
+                const int nk = K / kKS;
+                const uint32_t npad = (uint32_t)((x.n + 15) & ~15);
+                // instruction descriptor: f32 accumulate, f16 A and B, both K-major, N = npad, M = 128
+                const uint32_t idesc = (1u << 4) | ((npad >> 3) << 17) | ((uint32_t)(kM >> 4) << 24);
+                if (!tc_wait(&acc_empty[ar.slot], ar.phase ^ 1u, abort_flag, p.err)) { ok = false; break; }
                 tc_fence_after();
+                const uint32_t dbase = tmem + (uint32_t)(ar.slot * kAccCols);
                 for (int kk = 0; kk < nk; kk++) {
-                    const int s_a = ga % kAStages, s_b = gb % kBStages;
-                    if (!tc_wait(&a_full[s_a], (ga / kAStages) & 1, abort_flag, p.err) ||
-                        !tc_wait(&b_full[s_b], (gb / kBStages) & 1, abort_flag, p.err)) { ok = false; break; }
+                    const int s_x = xr.slot, s_w = wr.slot;
+                    if (!tc_wait(&x_full[s_x], xr.phase, abort_flag, p.err) ||
+                        !tc_wait(&w_full[s_w], wr.phase, abort_flag, p.err)) { ok = false; break; }
                     tc_fence_after();
-                    const uint32_t a_addr = smem_addr(sa + (size_t)s_a * kATileBytes);
+                    const uint32_t b_addr = smem_addr(sx + (size_t)s_x * c.x_bytes);
 #pragma unroll
                     for (int m = 0; m < NMAT; m++) {
-                        const uint32_t b_addr = smem_addr(sb + (size_t)(s_b * NMAT + m) * kBTileBytes);
-                        const uint32_t d = tmem + (uint32_t)(buf * NMAT * kTN + m * kTN);
+                        const uint32_t a_addr = smem_addr(sw + (size_t)(s_w * NMAT + m) * kWTileBytes);
+                        const uint32_t d = dbase + (uint32_t)(m * kCapGU);
 #pragma unroll
                         for (int k16 = 0; k16 < kKS / 16; k16++)
                             tc_mma_f16(d, umma_desc_sw128(a_addr + 32 * k16), umma_desc_sw128(b_addr + 32 * k16), idesc,
                                        (kk | k16) != 0);
                     }
                     issued = true;
-                    tc_commit(&a_empty[s_a]);
-                    tc_commit(&b_empty[s_b]);
-                    ga++;
-                    gb++;
+                    tc_commit(&x_empty[s_x]);
+                    tc_commit(&w_empty[s_w]);
+                    xr.advance(c.xst);
+                    wr.advance(c.wst);
                 }
                 if (!ok) break;
-                tc_commit(&acc_full[buf]);
-                gt++;
+                tc_commit(&acc_full[ar.slot]);
+                ar.advance(2);
             }
             if (issued) {   // every MMA has completed before the CTA may release TMEM
                 tc_commit(drain_bar);
-                const long long t0 = clock64();
-                while (!mbar_try_wait(drain_bar, 0) && clock64() - t0 < kWaitCycles) {}
+                drain_wait(drain_bar, 0);
             }
         }
     } else if (warp < kEpiWarp0) {
-        // dequant warps: thread d owns weight row d >> 1 and one 32-value sub-block of each 64-value step
-        const int d = threadIdx.x - kDeqWarp0 * 32, r = d >> 1, hf = d & 1;
-        uint32_t gb = 0, gq = 0;
+        // dequant warps: thread d owns weight row d % 128 and one 32-value half of each 64-value K step
+        const int d = threadIdx.x - kDeqWarp0 * 32, r = d & (kM - 1), hf = d >> 7;
+        const uint32_t swz = (uint32_t)(r & 7);
+        const uint32_t q_row = smem_addr(sq) + (uint32_t)r * 128, m_row = smem_addr(sq) + kQuantBox + (uint32_t)r * 16;
+        const uint32_t w_row = smem_addr(sw) + (uint32_t)r * 128;
+        RingPos qr, wr;
         bool ok = true;
         for (int it = blockIdx.x; it < total && ok; it += gridDim.x) {
-            const TcItem x = tc_item(p, tile_off, nq, n_routed, it);
+            const TcItem x = tc_item(s_off, s_prob, nq, c.cap, it);
             const int K = NMAT == 2 ? (x.shared ? L.sh_gate.cols : L.gate.cols)
                                     : (x.shared ? L.sh_down.cols : L.down.cols);
-            const int nk = (K + kKS - 1) / kKS;
+            const int nk = K / kKS;
             for (int kk = 0; kk < nk; kk++) {
-                const int s_q = gq % c.qstages;
-                if ((kk & 3) == 0 && !tc_wait(&q_full[s_q], (gq / c.qstages) & 1, abort_flag, p.err)) { ok = false; break; }
-                const int s_b = gb % kBStages;
-                if (gb >= (uint32_t)kBStages && !tc_wait(&b_empty[s_b], ((gb / kBStages) - 1) & 1, abort_flag, p.err)) { ok = false; break; }
-                const int j = 2 * (kk & 3) + hf;   // sub-block of the super-step
+                const int qi = kk & (QK - 1), s_q = qr.slot, s_w = wr.slot;
+                if (qi == 0 && !tc_wait(&q_full[s_q], qr.phase, abort_flag, p.err)) { ok = false; break; }
+                if (!tc_wait(&w_empty[s_w], wr.phase ^ 1u, abort_flag, p.err)) { ok = false; break; }
 #pragma unroll
                 for (int m = 0; m < NMAT; m++) {
-                    const uint8_t *qrow = sq + (size_t)(s_q * NMAT + m) * c.q_bytes + (size_t)r * c.qs_box;
-                    const uint8_t *mrow = sq + (size_t)(s_q * NMAT + m) * c.q_bytes + (size_t)kTN * c.qs_box + (size_t)r * 16;
-                    uint8_t *brow = sb + (size_t)(s_b * NMAT + m) * kBTileBytes + (size_t)r * 128;
+                    const uint32_t qb = q_row + (uint32_t)(s_q * NMAT + m) * kQBytes;
+                    const uint32_t mb = m_row + (uint32_t)(s_q * NMAT + m) * kQBytes;
+                    const uint32_t wb = w_row + (uint32_t)(s_w * NMAT + m) * kWTileBytes;
                     uint4 out[4];
                     if (FMT == FMT_Q4_K) {
-                        const uint4 q = *reinterpret_cast<const uint4 *>(qrow + 16 * j);
-                        const float2 sc = q4_scales(*reinterpret_cast<const uint4 *>(mrow), j);   // (d*sc/16, dmin*m)
+                        const int j = 2 * qi + hf;   // sub-block of the super-step = 16-byte chunk of the row
+                        const uint4 q = lds128(qb + 16u * ((uint32_t)j ^ swz));
+                        const float2 sc = q4_scales(lds128(mb), j);   // (d*sc/16, dmin*m)
                         const __half2 dsc = __float2half2_rn(sc.x * 16.0f), ndmn = __float2half2_rn(-sc.y);
-                        out[0] = q4_chunk_f16(q.x, q.y, false, dsc, ndmn);
-                        out[1] = q4_chunk_f16(q.z, q.w, false, dsc, ndmn);
-                        out[2] = q4_chunk_f16(q.x, q.y, true, dsc, ndmn);
-                        out[3] = q4_chunk_f16(q.z, q.w, true, dsc, ndmn);
+                        q4_word_f16(q.x, dsc, ndmn, out[0].x, out[0].y, out[2].x, out[2].y);
+                        q4_word_f16(q.y, dsc, ndmn, out[0].z, out[0].w, out[2].z, out[2].w);
+                        q4_word_f16(q.z, dsc, ndmn, out[1].x, out[1].y, out[3].x, out[3].y);
+                        q4_word_f16(q.w, dsc, ndmn, out[1].z, out[1].w, out[3].z, out[3].w);
                     } else {
-                        const uint4 q0 = *reinterpret_cast<const uint4 *>(qrow + 32 * j);
-                        const uint4 q1 = *reinterpret_cast<const uint4 *>(qrow + 32 * j + 16);
-                        const __half2 dd = __half2half2(*reinterpret_cast<const __half *>(mrow + 2 * j));
-                        out[0] = q8_chunk_f16(q0.x, q0.y, dd);
-                        out[1] = q8_chunk_f16(q0.z, q0.w, dd);
-                        out[2] = q8_chunk_f16(q1.x, q1.y, dd);
-                        out[3] = q8_chunk_f16(q1.z, q1.w, dd);
+                        const int jb = 2 * qi + hf;   // 32-value block of the 128-value stage
+                        const uint4 q0 = lds128(qb + 16u * ((uint32_t)(2 * jb) ^ swz));
+                        const uint4 q1 = lds128(qb + 16u * ((uint32_t)(2 * jb + 1) ^ swz));
+                        const int blk = 4 * ((kk >> 1) & 1) + jb;   // block of the 256-value scale row
+                        const __half2 dd = __half2half2(__ushort_as_half((unsigned short)lds16(mb + 2u * blk)));
+                        q8_word_f16(q0.x, dd, out[0].x, out[0].y);
+                        q8_word_f16(q0.y, dd, out[0].z, out[0].w);
+                        q8_word_f16(q0.z, dd, out[1].x, out[1].y);
+                        q8_word_f16(q0.w, dd, out[1].z, out[1].w);
+                        q8_word_f16(q1.x, dd, out[2].x, out[2].y);
+                        q8_word_f16(q1.y, dd, out[2].z, out[2].w);
+                        q8_word_f16(q1.z, dd, out[3].x, out[3].y);
+                        q8_word_f16(q1.w, dd, out[3].z, out[3].w);
                     }
 #pragma unroll
-                    for (int cc = 0; cc < 4; cc++) {
-                        const int chunk = 4 * hf + cc;   // 16-byte chunk of the 128-byte row
-                        *reinterpret_cast<uint4 *>(brow + 16 * (chunk ^ (r & 7))) = out[cc];
-                    }
+                    for (int cc = 0; cc < 4; cc++) sts128(wb + 16u * ((uint32_t)(4 * hf + cc) ^ swz), out[cc]);
                 }
                 fence_async_smem();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&b_full[s_b]);
-                gb++;
-                if ((kk & 3) == 3 || kk == nk - 1) {
+                if (lane == 0) mbar_arrive(&w_full[s_w]);
+                wr.advance(c.wst);
+                if (qi == QK - 1 || kk == nk - 1) {
                     if (lane == 0) mbar_arrive(&q_empty[s_q]);
-                    gq++;
+                    qr.advance(c.qst);
                 }
             }
         }
     } else {
-        // epilogue warps: thread = one TMEM lane = one slot row of the tile
-        const int qw = warp & 3, row = 32 * qw + lane;
-        uint32_t gt = 0;
+        // epilogue warps: TMEM lane = weight row = output feature, column = slot
+        const int wq = warp & 3;
+        RingPos ar;
         bool ok = true;
         for (int it = blockIdx.x; it < total && ok; it += gridDim.x) {
-            const TcItem x = tc_item(p, tile_off, nq, n_routed, it);
-            const int buf = gt & 1;
-            if (!tc_wait(&acc_full[buf], (gt >> 1) & 1, abort_flag, p.err)) { ok = false; break; }
+            const TcItem x = tc_item(s_off, s_prob, nq, c.cap, it);
+            const int buf = ar.slot;
+            if (!tc_wait(&acc_full[buf], ar.phase, abort_flag, p.err)) { ok = false; break; }
             tc_fence_after();
-            const int ri = x.mt * kTM + row;
-            const bool valid = ri < x.pr.count;
-            const size_t slot = (size_t)x.pr.slot0 + ri;
-            const uint32_t tbase = tmem + ((uint32_t)(32 * qw) << 16) + (uint32_t)(buf * NMAT * kTN);
+            const int f = x.nt * kM + 32 * wq + lane;
+            const uint32_t tb = tmem + ((uint32_t)(32 * wq) << 16) + (uint32_t)(buf * kAccCols);
+            const int ncc = (x.n + 31) >> 5;
 #pragma unroll 1
-            for (int cc = 0; cc < kTN / 32; cc++) {
+            for (int cc = 0; cc < ncc; cc++) {
+                const int n_here = min(32, x.n - 32 * cc);
                 uint32_t g[32];
-                tmem_ld32(tbase + 32 * cc, g);
+                tmem_ld32(tb + 32 * cc, g);
                 if (NMAT == 2) {
                     uint32_t u[32];
-                    tmem_ld32(tbase + kTN + 32 * cc, u);
+                    tmem_ld32(tb + kCapGU + 32 * cc, u);
                     tmem_ld_wait();
+                    // one slot per column; the warp's 32 lanes are one 32-feature quantisation
+                    // block, so a column's amax is a warp max; lane i keeps column i's and
+                    // computes its scales once, the others read them with a shuffle
                     float a[32];
-                    float amax = 0.0f;
+                    uint32_t own = 0;
 #pragma unroll
                     for (int i = 0; i < 32; i++) {
                         a[i] = swiglu(__uint_as_float(g[i]), __uint_as_float(u[i]));
-                        amax = fmaxf(amax, fabsf(a[i]));
+                        const uint32_t m = __reduce_max_sync(0xffffffffu, __float_as_uint(fmaxf(fabsf(a[i]), 0.0f)));
+                        own = lane == i ? m : own;
                     }
-                    // the decode path's block quantiser, then f16 of q * d for the down operand
-                    const float id = amax > 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f;
-                    const float dq = __fdiv_rn(amax, 127.0f);
-                    uint32_t h[16];
+                    const float amax = __uint_as_float(own);
+                    const float id_own = amax > 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f;
+                    const float dq_own = __fdiv_rn(amax, 127.0f);
+                    __half *dst = static_cast<__half *>(p.a16dn) + (size_t)(x.slot + 32 * cc) * p.a16dn_stride + k_perm(f);
 #pragma unroll
-                    for (int i = 0; i < 16; i++) {
-                        float q0 = fminf(fmaxf(roundf(__fmul_rn(a[2 * i], id)), -127.0f), 127.0f);
-                        float q1 = fminf(fmaxf(roundf(__fmul_rn(a[2 * i + 1], id)), -127.0f), 127.0f);
-                        __half2 hv = __floats2half2_rn(q0 * dq, q1 * dq);
-                        h[i] = *reinterpret_cast<uint32_t *>(&hv);
-                    }
-                    if (valid) {
-                        uint4 *dst = reinterpret_cast<uint4 *>(static_cast<__half *>(p.a16dn) + slot * p.a16dn_stride +
-                                                               x.nt * kTN + 32 * cc);
-#pragma unroll
-                        for (int v = 0; v < 4; v++) dst[v] = make_uint4(h[4 * v], h[4 * v + 1], h[4 * v + 2], h[4 * v + 3]);
+                    for (int i = 0; i < 32; i++) {
+                        const float id = __shfl_sync(0xffffffffu, id_own, i);
+                        const float dq = __shfl_sync(0xffffffffu, dq_own, i);
+                        const float q = fminf(fmaxf(roundf(__fmul_rn(a[i], id)), -127.0f), 127.0f);
+                        if (i < n_here) dst[(size_t)i * p.a16dn_stride] = __float2half_rn(q * dq);
                     }
                 } else {
                     tmem_ld_wait();
-                    if (valid) {
-                        float4 *dst = reinterpret_cast<float4 *>(p.y + slot * p.H + x.nt * kTN + 32 * cc);
+                    float *dst = p.y + (size_t)(x.slot + 32 * cc) * p.H + f;
 #pragma unroll
-                        for (int v = 0; v < 8; v++)
-                            dst[v] = make_float4(__uint_as_float(g[4 * v]), __uint_as_float(g[4 * v + 1]),
-                                                 __uint_as_float(g[4 * v + 2]), __uint_as_float(g[4 * v + 3]));
-                    }
+                    for (int i = 0; i < 32; i++)
+                        if (i < n_here) dst[(size_t)i * p.H] = __uint_as_float(g[i]);
                 }
             }
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&acc_empty[buf]);
-            gt++;
+            ar.advance(2);
         }
     }
 
@@ -374,12 +425,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     __syncthreads();
     if (warp == kWarpMma) {
         tc_fence_after();
-        tmem_dealloc(tmem, NMAT == 2 ? 512 : 256);
+        tmem_dealloc(tmem, kTmemCols);
     }
 }
 
-// A operand of the gate/up GEMM: slot s holds f16(xq * d) of its token (the
-// activation blocks the decode path uses), 8 values per thread.
+// B operand of the gate/up GEMM: slot s holds f16(xq * d) of its token (the
+// activation blocks the decode path uses), 8 values per thread, each group of
+// four in the order (0, 2, 1, 3).
 __global__ void gather_act_f16_kernel(FwdParams p, int n_slots)
 {
     const int per_row = p.H >> 3;
@@ -392,48 +444,49 @@ __global__ void gather_act_f16_kernel(FwdParams p, int n_slots)
         const int8_t *qb = reinterpret_cast<const int8_t *>(&q);
         uint32_t h[4];
 #pragma unroll
-        for (int k = 0; k < 4; k++) {
-            __half2 v = __floats2half2_rn((float)qb[2 * k] * d, (float)qb[2 * k + 1] * d);
-            h[k] = *reinterpret_cast<uint32_t *>(&v);
+        for (int k = 0; k < 2; k++) {
+            h[2 * k] = h2_bits(__floats2half2_rn((float)qb[4 * k] * d, (float)qb[4 * k + 2] * d));
+            h[2 * k + 1] = h2_bits(__floats2half2_rn((float)qb[4 * k + 1] * d, (float)qb[4 * k + 3] * d));
         }
         *reinterpret_cast<uint4 *>(static_cast<__half *>(p.a16) + (size_t)s * p.a16_stride + 8 * c) =
             make_uint4(h[0], h[1], h[2], h[3]);
     }
 }
 
-// Item offsets of the tensor-core launches (one warp): for each launch
+// Item offsets of the tensor-core launches (one thread): for each launch
 // layout (gate/up routed+shared, gate/up shared only, down routed+shared, down
-// shared only) the prefix over problems of m_tiles * n_tiles.
+// shared only) the prefix over problems of slot chunks * 128-row weight tiles.
 __global__ void tile_plan_kernel(FwdParams p, int rows_gu, int rows_gu_sh, int rows_dn)
 {
     if (threadIdx.x != 0) return;
     const int nr = *p.n_active;
-    const int mtile_sh = p.S > 0 ? (p.T + kTM - 1) / kTM : 0;
+    const int sh_gu = p.S > 0 ? chunk_count(p.T, kCapGU) * (rows_gu_sh / kM) : 0;
+    const int sh_dn = p.S > 0 ? chunk_count(p.T, kCapDN) * (rows_dn / kM) : 0;
     int32_t *gu = p.tile_off, *gu_sh = p.tile_off + kTileOffStride;
     int32_t *dn = p.tile_off + 2 * kTileOffStride, *dn_sh = p.tile_off + 3 * kTileOffStride;
     int a = 0, b = 0;
     for (int q = 0; q < nr; q++) {
         gu[q] = a;
         dn[q] = b;
-        const int mt = (p.problems[q].count + kTM - 1) / kTM;
-        a += mt * (rows_gu / kTN);
-        b += mt * (rows_dn / kTN);
+        const int cnt = p.problems[q].count;
+        a += chunk_count(cnt, kCapGU) * (rows_gu / kM);
+        b += chunk_count(cnt, kCapDN) * (rows_dn / kM);
     }
     gu[nr] = a;
     dn[nr] = b;
-    gu[nr + 1] = a + mtile_sh * (rows_gu_sh / kTN);
-    dn[nr + 1] = b + mtile_sh * (rows_dn / kTN);
+    gu[nr + 1] = a + sh_gu;
+    dn[nr + 1] = b + sh_dn;
     gu_sh[0] = 0;
     dn_sh[0] = 0;
-    gu_sh[1] = mtile_sh * (rows_gu_sh / kTN);
-    dn_sh[1] = mtile_sh * (rows_dn / kTN);
+    gu_sh[1] = sh_gu;
+    dn_sh[1] = sh_dn;
 }
 
-// f16 activation operand [rows][cols] with row stride stride_elems: box 64 x 128, 128-byte swizzle.
+// f16 activation operand [rows][cols] with row stride stride_elems: box 64 x 32, 128-byte swizzle.
 cudaError_t encode_f16_map(CUtensorMap *m, const void *base, uint64_t rows, uint64_t cols, uint64_t stride_elems)
 {
-    return encode_tiled(m, 0, base, rows, cols, stride_elems * 2, kKS, kTM, 1) == 0 ? cudaSuccess
-                                                                                    : cudaErrorInvalidValue;
+    return encode_tiled(m, 0, base, rows, cols, stride_elems * 2, kKS, kXBoxRows, 1) == 0 ? cudaSuccess
+                                                                                          : cudaErrorInvalidValue;
 }
 
 template <int FMT, int NMAT>
@@ -456,16 +509,20 @@ cudaError_t launch_tc(const FwdParams &p, const LayerDev &L, const LayerMaps &lm
         maps.sq[0] = maps.sq[1] = lm.sh_down_tc.qs; maps.sm[0] = maps.sm[1] = lm.sh_down_tc.meta;
     }
     TcCfg c{};
-    c.nmat = NMAT;
     c.mode = mode;
-    c.qs_box = FMT == FMT_Q4_K ? kSuper / 2 : kSuper;
-    c.q_bytes = kTN * c.qs_box + kTN * 16;
-    c.qstages = (FMT == FMT_Q8_0 && NMAT == 2) ? 1 : kQStages;   // Q8_0 gate+up stages are 68 KB each
-    c.smem_a = 0;
-    c.smem_b = c.smem_a + kAStages * kATileBytes;
-    c.smem_q = c.smem_b + kBStages * NMAT * kBTileBytes;
-    c.smem_bar = c.smem_q + c.qstages * NMAT * c.q_bytes;
-    const size_t smem = (size_t)c.smem_bar + 256 + 1024;   // barriers + alignment slack
+    c.cap = NMAT == 2 ? kCapGU : kCapDN;
+    c.x_bytes = c.cap * 128;
+    // ring depths by shared-memory room (stage bytes: x 16 / 32 KB, w 32 / 16 KB, q 36 / 18 KB)
+    if (NMAT == 2) { c.xst = 3; c.wst = FMT == FMT_Q4_K ? 3 : 2; c.qst = FMT == FMT_Q4_K ? 2 : 3; }
+    else { c.xst = 4; c.wst = FMT == FMT_Q4_K ? 3 : 2; c.qst = FMT == FMT_Q4_K ? 2 : 3; }
+    c.max_q = p.max_problems;
+    c.smem_x = 0;
+    c.smem_w = c.smem_x + c.xst * c.x_bytes;
+    c.smem_q = c.smem_w + c.wst * NMAT * kWTileBytes;
+    c.smem_tab = c.smem_q + c.qst * NMAT * kQBytes;
+    c.smem_bar = c.smem_tab + (((c.max_q + 4) & ~3) * 4 + c.max_q * 16 + 15) / 16 * 16;
+    const size_t smem = (size_t)c.smem_bar + (6 * kMaxStages + 5) * 8 + 16 + 1024;   // barriers + alignment slack
+    if (smem > 232448) return cudaErrorInvalidValue;
     if ((e = cudaFuncSetAttribute(tc_expert_kernel<FMT, NMAT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   (int)smem)) != cudaSuccess)
         return e;

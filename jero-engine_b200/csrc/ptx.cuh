@@ -47,6 +47,37 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity)
     return ok != 0;
 }
 
+// try_wait with a suspend-time hint: the warp sleeps (issuing nothing) until
+// the phase completes or about hint_ns nanoseconds pass.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t *bar, uint32_t parity, uint32_t hint_ns)
+{
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_addr(bar)), "r"(parity), "r"(hint_ns)
+        : "memory");
+    return ok != 0;
+}
+
+// Slot and phase of a ring of n stages. Consumers wait for the full barrier
+// of the slot with the phase's parity; producers wait for the empty barrier
+// with the opposite parity, which a fresh barrier reports complete, so the
+// first round needs no special case. No division or modulo on the hot path.
+struct RingPos {
+    int slot = 0;
+    uint32_t phase = 0;
+    __device__ __forceinline__ void advance(int n)
+    {
+        if (++slot == n) {
+            slot = 0;
+            phase ^= 1u;
+        }
+    }
+};
+
 // 2-D TMA tile load (no multicast) of the box at (x, y) of map into shared
 // memory, completing on bar. x in elements of the map; x * element size must
 // be a multiple of 16 bytes.

@@ -62,16 +62,20 @@ void plan_slices(DevMatrix &m)
 
 // Each quantised stack is the dense array [E*rows][row bytes] of u64 elements.
 // box_rows 32: the streaming kernels' K-slice boxes; box_rows 128: the
-// tensor-core path's 256-value boxes (Q4_K 128 bytes, Q8_0 256 bytes of quants,
-// 16 bytes of scales per row).
+// tensor-core path's boxes of 128 bytes of quants per row (Q4_K 256 values,
+// Q8_0 128 values) and 16 bytes of scales per row (one 256-value super-step).
 int make_matrix_maps(const DevMatrix &m, MatMaps *out, int box_rows)
 {
     memset(out, 0, sizeof *out);
     if (m.type != FMT_Q4_K && m.type != FMT_Q8_0) return CUDA_SUCCESS;
     const uint64_t rows_total = (uint64_t)m.n_experts * m.rows;
-    const uint32_t qbox = box_rows == 32 ? (uint32_t)m.qs_box : (m.type == FMT_Q4_K ? 128u : 256u);
-    const uint32_t mbox = box_rows == 32 ? (uint32_t)m.meta_box : 16u;
-    int r = encode_tiled(&out->qs, 1, m.qs, rows_total, m.qs_rstride / 8, m.qs_rstride, qbox / 8, box_rows, 0);
+    // the tensor-core path lands quants in 128-byte rows with the 128-byte
+    // swizzle (Q8_0: two boxes per 256 values), so its dequant warps read them
+    // without bank conflicts
+    const bool tc = box_rows != 32;
+    const uint32_t qbox = tc ? 128u : (uint32_t)m.qs_box;
+    const uint32_t mbox = tc ? 16u : (uint32_t)m.meta_box;
+    int r = encode_tiled(&out->qs, 1, m.qs, rows_total, m.qs_rstride / 8, m.qs_rstride, qbox / 8, box_rows, tc);
     if (r != CUDA_SUCCESS) return r;
     return encode_tiled(&out->meta, 1, m.meta, rows_total, m.meta_rstride / 8, m.meta_rstride, mbox / 8, box_rows, 0);
 }
