@@ -47,7 +47,7 @@ constexpr int kQBytes = kQuantBox + kM * 16;    // + 16 bytes of scales per row 
 struct TcCfg {
     int mode;                // 0 routed problems, 1 shared only, 2 both
     int cap;                 // slots per item
-    int xst, wst, qst;       // ring depths: activation tiles, dequantised tiles, quantised stages
+    int kst, qst;            // ring depths: K steps (activation + dequantised tiles), quantised stages
     int x_bytes;             // bytes of one activation stage (cap rows)
     int max_q;               // capacity of the item table
     int smem_x, smem_w, smem_q, smem_tab, smem_bar;   // region offsets
@@ -175,9 +175,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     int *s_off = reinterpret_cast<int *>(base + c.smem_tab);
     int4 *s_prob = reinterpret_cast<int4 *>(s_off + ((c.max_q + 4) & ~3));
     uint64_t *bars = reinterpret_cast<uint64_t *>(base + c.smem_bar);
-    uint64_t *x_full = bars, *x_empty = x_full + kMaxStages;
-    uint64_t *w_full = x_empty + kMaxStages, *w_empty = w_full + kMaxStages;
-    uint64_t *q_full = w_empty + kMaxStages, *q_empty = q_full + kMaxStages;
+    // a K-step stage holds one activation tile (TMA, x_full) and the dequantised
+    // weight tiles (dequant warps, w_full); one tensor-core commit frees both
+    uint64_t *x_full = bars, *w_full = x_full + kMaxStages, *k_empty = w_full + kMaxStages;
+    uint64_t *q_full = k_empty + kMaxStages, *q_empty = q_full + kMaxStages;
     uint64_t *acc_full = q_empty + kMaxStages, *acc_empty = acc_full + 2, *drain_bar = acc_empty + 2;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain_bar + 1);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
@@ -197,8 +198,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         s_prob[i] = make_int4(pr.expert, pr.slot0, pr.count, sh ? 1 : 0);
     }
     if (threadIdx.x == 0) {
-        for (int i = 0; i < c.xst; i++) { mbar_init(&x_full[i], 1); mbar_init(&x_empty[i], 1); }
-        for (int i = 0; i < c.wst; i++) { mbar_init(&w_full[i], kDeqWarps); mbar_init(&w_empty[i], 1); }
+        for (int i = 0; i < c.kst; i++) {
+            mbar_init(&x_full[i], 1);
+            mbar_init(&w_full[i], kDeqWarps);
+            mbar_init(&k_empty[i], 1);
+        }
         for (int i = 0; i < c.qst; i++) { mbar_init(&q_full[i], 1); mbar_init(&q_empty[i], kDeqWarps); }
         for (int i = 0; i < 2; i++) { mbar_init(&acc_full[i], 1); mbar_init(&acc_empty[i], kEpiWarps); }
         mbar_init(drain_bar, 1);
@@ -214,7 +218,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
     if (warp == kWarpTma) {
         if (lane == 0) {
-            RingPos xr, qr;
+            RingPos kr, qr;
             uint32_t gx = 0, gq = 0;   // uses issued, for the drain after an abort
             bool ok = true;
             for (int it = blockIdx.x; it < total && ok; it += gridDim.x) {
@@ -240,27 +244,30 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                         qr.advance(c.qst);
                         gq++;
                     }
-                    if (!tc_wait(&x_empty[xr.slot], xr.phase ^ 1u, abort_flag, p.err)) { ok = false; break; }
-                    uint64_t *bar = &x_full[xr.slot];
+                    if (!tc_wait(&k_empty[kr.slot], kr.phase ^ 1u, abort_flag, p.err)) { ok = false; break; }
+                    uint64_t *bar = &x_full[kr.slot];
                     mbar_arrive_expect_tx(bar, (uint32_t)(nbox * kXBoxBytes));
-                    uint8_t *dst = sx + (size_t)xr.slot * c.x_bytes;
+                    uint8_t *dst = sx + (size_t)kr.slot * c.x_bytes;
                     for (int b = 0; b < nbox; b++)
                         tma_load_2d(dst + b * kXBoxBytes, &maps.a, kk * kKS, x.slot + b * kXBoxRows, bar);
-                    xr.advance(c.xst);
+                    kr.advance(c.kst);
                     gx++;
                 }
             }
             if (!ok) {   // wait (bounded) for the copies still in flight
-                for (uint32_t g = gx > (uint32_t)c.xst ? gx - c.xst : 0; g < gx; g++)
-                    drain_wait(&x_full[g % c.xst], (g / c.xst) & 1);
+                for (uint32_t g = gx > (uint32_t)c.kst ? gx - c.kst : 0; g < gx; g++)
+                    drain_wait(&x_full[g % c.kst], (g / c.kst) & 1);
                 for (uint32_t g = gq > (uint32_t)c.qst ? gq - c.qst : 0; g < gq; g++)
                     drain_wait(&q_full[g % c.qst], (g / c.qst) & 1);
             }
         }
     } else if (warp == kWarpMma) {
         if (lane == 0) {
-            RingPos xr, wr, ar;
+            RingPos kr, ar;
             bool ok = true, issued = false;
+            // smem descriptors of stage 0; a stage, matrix or 16-value K step moves the
+            // start address field (address / 16) by a constant
+            const uint64_t a_desc0 = umma_desc_sw128(smem_addr(sw)), b_desc0 = umma_desc_sw128(smem_addr(sx));
             for (int it = blockIdx.x; it < total && ok; it += gridDim.x) {
                 const TcItem x = tc_item(s_off, s_prob, nq, c.cap, it);
                 const int K = NMAT == 2 ? (x.shared ? L.sh_gate.cols : L.gate.cols)
@@ -273,25 +280,22 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 tc_fence_after();
                 const uint32_t dbase = tmem + (uint32_t)(ar.slot * kAccCols);
                 for (int kk = 0; kk < nk; kk++) {
-                    const int s_x = xr.slot, s_w = wr.slot;
-                    if (!tc_wait(&x_full[s_x], xr.phase, abort_flag, p.err) ||
-                        !tc_wait(&w_full[s_w], wr.phase, abort_flag, p.err)) { ok = false; break; }
+                    const int st = kr.slot;
+                    if (!tc_wait(&x_full[st], kr.phase, abort_flag, p.err) ||
+                        !tc_wait(&w_full[st], kr.phase, abort_flag, p.err)) { ok = false; break; }
                     tc_fence_after();
-                    const uint32_t b_addr = smem_addr(sx + (size_t)s_x * c.x_bytes);
+                    const uint64_t bd = b_desc0 + (uint64_t)((st * c.x_bytes) >> 4);
 #pragma unroll
                     for (int m = 0; m < NMAT; m++) {
-                        const uint32_t a_addr = smem_addr(sw + (size_t)(s_w * NMAT + m) * kWTileBytes);
+                        const uint64_t ad = a_desc0 + (uint64_t)(((st * NMAT + m) * kWTileBytes) >> 4);
                         const uint32_t d = dbase + (uint32_t)(m * kCapGU);
 #pragma unroll
                         for (int k16 = 0; k16 < kKS / 16; k16++)
-                            tc_mma_f16(d, umma_desc_sw128(a_addr + 32 * k16), umma_desc_sw128(b_addr + 32 * k16), idesc,
-                                       (kk | k16) != 0);
+                            tc_mma_f16(d, ad + 2 * k16, bd + 2 * k16, idesc, (kk | k16) != 0);
                     }
                     issued = true;
-                    tc_commit(&x_empty[s_x]);
-                    tc_commit(&w_empty[s_w]);
-                    xr.advance(c.xst);
-                    wr.advance(c.wst);
+                    tc_commit(&k_empty[st]);
+                    kr.advance(c.kst);
                 }
                 if (!ok) break;
                 tc_commit(&acc_full[ar.slot]);
@@ -308,7 +312,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         const uint32_t swz = (uint32_t)(r & 7);
         const uint32_t q_row = smem_addr(sq) + (uint32_t)r * 128, m_row = smem_addr(sq) + kQuantBox + (uint32_t)r * 16;
         const uint32_t w_row = smem_addr(sw) + (uint32_t)r * 128;
-        RingPos qr, wr;
+        RingPos qr, kr;
         bool ok = true;
         for (int it = blockIdx.x; it < total && ok; it += gridDim.x) {
             const TcItem x = tc_item(s_off, s_prob, nq, c.cap, it);
@@ -316,9 +320,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                                     : (x.shared ? L.sh_down.cols : L.down.cols);
             const int nk = K / kKS;
             for (int kk = 0; kk < nk; kk++) {
-                const int qi = kk & (QK - 1), s_q = qr.slot, s_w = wr.slot;
+                const int qi = kk & (QK - 1), s_q = qr.slot, s_w = kr.slot;
                 if (qi == 0 && !tc_wait(&q_full[s_q], qr.phase, abort_flag, p.err)) { ok = false; break; }
-                if (!tc_wait(&w_empty[s_w], wr.phase ^ 1u, abort_flag, p.err)) { ok = false; break; }
+                if (!tc_wait(&k_empty[s_w], kr.phase ^ 1u, abort_flag, p.err)) { ok = false; break; }
 #pragma unroll
                 for (int m = 0; m < NMAT; m++) {
                     const uint32_t qb = q_row + (uint32_t)(s_q * NMAT + m) * kQBytes;
@@ -355,7 +359,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 fence_async_smem();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&w_full[s_w]);
-                wr.advance(c.wst);
+                kr.advance(c.kst);
                 if (qi == QK - 1 || kk == nk - 1) {
                     if (lane == 0) mbar_arrive(&q_empty[s_q]);
                     qr.advance(c.qst);
@@ -512,16 +516,17 @@ cudaError_t launch_tc(const FwdParams &p, const LayerDev &L, const LayerMaps &lm
     c.mode = mode;
     c.cap = NMAT == 2 ? kCapGU : kCapDN;
     c.x_bytes = c.cap * 128;
-    // ring depths by shared-memory room (stage bytes: x 16 / 32 KB, w 32 / 16 KB, q 36 / 18 KB)
-    if (NMAT == 2) { c.xst = 3; c.wst = FMT == FMT_Q4_K ? 3 : 2; c.qst = FMT == FMT_Q4_K ? 2 : 3; }
-    else { c.xst = 4; c.wst = FMT == FMT_Q4_K ? 3 : 2; c.qst = FMT == FMT_Q4_K ? 2 : 3; }
+    // ring depths by shared-memory room: a K step is 48 KB (gate/up: x 16 + w 32;
+    // down: x 32 + w 16), a quantised stage 36 KB (gate/up) or 18 KB (down)
+    c.kst = 3;
+    c.qst = NMAT == 2 ? 2 : 3;
     c.max_q = p.max_problems;
     c.smem_x = 0;
-    c.smem_w = c.smem_x + c.xst * c.x_bytes;
-    c.smem_q = c.smem_w + c.wst * NMAT * kWTileBytes;
+    c.smem_w = c.smem_x + c.kst * c.x_bytes;
+    c.smem_q = c.smem_w + c.kst * NMAT * kWTileBytes;
     c.smem_tab = c.smem_q + c.qst * NMAT * kQBytes;
     c.smem_bar = c.smem_tab + (((c.max_q + 4) & ~3) * 4 + c.max_q * 16 + 15) / 16 * 16;
-    const size_t smem = (size_t)c.smem_bar + (6 * kMaxStages + 5) * 8 + 16 + 1024;   // barriers + alignment slack
+    const size_t smem = (size_t)c.smem_bar + (5 * kMaxStages + 5) * 8 + 16 + 1024;   // barriers + alignment slack
     if (smem > 232448) return cudaErrorInvalidValue;
     if ((e = cudaFuncSetAttribute(tc_expert_kernel<FMT, NMAT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   (int)smem)) != cudaSuccess)
