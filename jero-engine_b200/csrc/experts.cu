@@ -57,28 +57,16 @@ struct Item {
     int rt;
 };
 
-__device__ __forceinline__ Item item_at(const FwdParams &p, const StreamCfg &c, int nr, int it)
-{
-    Item x;
-    if (it < nr * c.rt_routed) {
-        x.pr = p.problems[it / c.rt_routed];
-        x.rt = it % c.rt_routed;
-        x.shared = false;
-    } else {
-        x.pr = p.problems[p.max_problems - 1];
-        x.rt = it - nr * c.rt_routed;
-        x.shared = true;
-    }
-    return x;
-}
-
 // Shared memory: ring [stages][stage_bytes] | xq int4 [kTT][2][act_k/32] |
-// xds float2 [kTT][act_k/32] | g, u [kTT][32] f32 | full[stages], empty[stages] | abort.
+// xds float2 [kTT][act_k/32] | g, u [kTT][32] f32 | problem table int4 [max_q] |
+// cost prefix int64 [max_q + 1] | full[stages], empty[stages] | abort.
 struct Smem {
     uint8_t *ring;
     int4 *xq;
     float2 *xds;
     float *g, *u;
+    int4 *prob;            // (expert, slot0, count, is_shared) of the launch's problems
+    long long *cpre;       // cost of all items of the problems before q
     uint64_t *full, *empty;
     volatile int *abort_flag;
 };
@@ -87,7 +75,47 @@ __host__ __device__ inline size_t smem_bytes(const StreamCfg &c)
 {
     const size_t nu = (size_t)c.act_k / 32;
     return (size_t)c.stages * c.stage_bytes + (size_t)kTT * nu * 32 + (size_t)kTT * nu * 8 + 2 * (size_t)kTT * 32 * 4 +
-           16 * (size_t)c.stages + 16;
+           16 * (size_t)c.max_q + 8 * ((size_t)c.max_q + 1) + 16 * (size_t)c.stages + 16;
+}
+
+__device__ __forceinline__ Item item_at(const Smem &s, const StreamCfg &c, int nr, int it)
+{
+    Item x;
+    const bool sh = it >= nr * c.rt_routed;
+    const int q = sh ? nr : it / c.rt_routed;
+    const int4 v = s.prob[q];
+    x.pr.expert = v.x;
+    x.pr.slot0 = v.y;
+    x.pr.count = v.z;
+    x.pr.is_shared = v.w;
+    x.rt = sh ? it - nr * c.rt_routed : it - q * c.rt_routed;
+    x.shared = sh;
+    return x;
+}
+
+// Estimated cost of one row-tile item of a problem with `count` tokens: the
+// weight stream and block decode once per token tile, the dots per token.
+__device__ __forceinline__ long long item_cost(int count)
+{
+    return 7LL * ((count + kTT - 1) / kTT) + 5LL * count;
+}
+
+// First item whose cost-prefix start is at or after X (items are ordered by
+// problem, then row tile, each problem's items all costing item_cost(count)).
+__device__ __forceinline__ int first_item_from(const Smem &s, const StreamCfg &c, int nq, int nr, long long X)
+{
+    if (X >= s.cpre[nq]) return nr * c.rt_routed + (nq > nr ? c.rt_shared : 0);
+    int lo = 0, hi = nq - 1;
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (s.cpre[mid] <= X) lo = mid;
+        else hi = mid - 1;
+    }
+    const long long cq = item_cost(s.prob[lo].z);
+    const int rt = lo < nr ? c.rt_routed : c.rt_shared;
+    const long long r = (X - s.cpre[lo] + cq - 1) / cq;
+    const int base = lo * c.rt_routed;   // the shared problem (lo == nr) starts at nr * rt_routed too
+    return r >= rt ? base + rt : base + (int)r;
 }
 
 __device__ __forceinline__ Smem carve(uint8_t *base, const StreamCfg &c)
@@ -99,7 +127,9 @@ __device__ __forceinline__ Smem carve(uint8_t *base, const StreamCfg &c)
     s.xds = reinterpret_cast<float2 *>(s.xq + (size_t)kTT * 2 * nu);
     s.g = reinterpret_cast<float *>(s.xds + (size_t)kTT * nu);
     s.u = s.g + kTT * 32;
-    s.full = reinterpret_cast<uint64_t *>(s.u + kTT * 32);
+    s.prob = reinterpret_cast<int4 *>(s.u + kTT * 32);
+    s.cpre = reinterpret_cast<long long *>(s.prob + c.max_q);
+    s.full = reinterpret_cast<uint64_t *>(s.cpre + c.max_q + 1);
     s.empty = s.full + c.stages;
     s.abort_flag = reinterpret_cast<volatile int *>(s.empty + c.stages);
     return s;
@@ -297,19 +327,45 @@ __global__ void __launch_bounds__(kStreamThreads, 2)
 {
     extern __shared__ __align__(128) uint8_t smem_raw[];
     const Smem s = carve(smem_raw, c);
-    init_ring(s, c.stages);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int nr = c.mode == 1 ? 0 : *p.n_active;
-    const int total = nr * c.rt_routed + ((c.mode != 0 && p.S > 0) ? c.rt_shared : 0);
-    const int it0 = (int)((long long)blockIdx.x * total / gridDim.x);
-    const int it1 = (int)((long long)(blockIdx.x + 1) * total / gridDim.x);
+    // the launch's problems (routed, then the shared expert) and their cost prefix
+    const int with_sh = (c.mode != 0 && p.S > 0) ? 1 : 0;
+    const int nr = min(c.mode == 1 ? 0 : *p.n_active, c.max_q - with_sh);
+    const int nq = nr + with_sh;
+    for (int i = threadIdx.x; i < nq; i += blockDim.x) {
+        const Problem pr = i < nr ? p.problems[i] : p.problems[p.max_problems - 1];
+        s.prob[i] = make_int4(pr.expert, pr.slot0, pr.count, i < nr ? 0 : 1);
+    }
+    __syncthreads();
+    if (warp == 0) {
+        const int per = (nq + 31) / 32, b = lane * per;
+        long long local = 0;
+        for (int i = b; i < min(b + per, nq); i++) local += item_cost(s.prob[i].z) * (i < nr ? c.rt_routed : c.rt_shared);
+        long long incl = local;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const long long v = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += v;
+        }
+        long long run = incl - local;
+        for (int i = b; i < min(b + per, nq); i++) {
+            s.cpre[i] = run;
+            run += item_cost(s.prob[i].z) * (i < nr ? c.rt_routed : c.rt_shared);
+        }
+        if (lane == 31) s.cpre[nq] = incl;
+    }
+    init_ring(s, c.stages);   // also publishes the tables (__syncthreads)
+    // contiguous item range of this CTA, balanced by estimated cost
+    const long long ctot = s.cpre[nq];
+    const int it0 = first_item_from(s, c, nq, nr, ctot * blockIdx.x / gridDim.x);
+    const int it1 = first_item_from(s, c, nq, nr, ctot * (blockIdx.x + 1) / gridDim.x);
 
     if (warp == kConsumerWarps) {   // producer: one thread issues the TMA boxes
         if (lane != 0) return;
         RingPos r;
         uint32_t g = 0;   // uses issued, for the drain after an abort
         for (int it = it0; it < it1; it++) {
-            const Item x = item_at(p, c, nr, it);
+            const Item x = item_at(s, c, nr, it);
             const MatMaps *mm[NMAT];
             int K, rows;
             if (NMAT == 2) {
@@ -345,7 +401,7 @@ __global__ void __launch_bounds__(kStreamThreads, 2)
     const int rw = warp * 4 + (lane >> 3), l8 = lane & 7;
     const int nu_s = c.act_k >> 5;
     for (int it = it0; it < it1; it++) {
-        const Item x = item_at(p, c, nr, it);
+        const Item x = item_at(s, c, nr, it);
         int K, rows;
         if (NMAT == 2) {
             const DevMatrix &G = x.shared ? L.sh_gate : L.gate;
@@ -588,6 +644,7 @@ cudaError_t launch_gate_up(const FwdParams &p, const LayerDev &L, const LayerMap
     c.rt_shared = (mode != 0 && p.S > 0) ? (L.sh_gate.rows + kRows - 1) / kRows : 0;
     c.down_f32 = (mode == 1 ? L.sh_down.type : L.down.type) == FMT_F32;
     c.act_k = p.H;
+    c.max_q = p.max_problems;
     plan_stream(c, G0, 2);
     const int upper = (mode == 1 ? 0 : (p.max_problems - (p.S > 0 ? 1 : 0)) * c.rt_routed) + c.rt_shared;
     if (G0.type == FMT_Q4_K)
@@ -611,6 +668,7 @@ cudaError_t launch_down(const FwdParams &p, const LayerDev &L, const LayerMaps &
     int kmax = D0.cols;
     if (mode == 2 && L.sh_down.cols > kmax) kmax = L.sh_down.cols;
     c.act_k = kmax;
+    c.max_q = p.max_problems;
     plan_stream(c, D0, 1);
     const int upper = (mode == 1 ? 0 : (p.max_problems - (p.S > 0 ? 1 : 0)) * c.rt_routed) + c.rt_shared;
     if (D0.type == FMT_Q4_K)

@@ -19,6 +19,7 @@ struct StreamCfg {
     int ks;            // values per K-slice (one ring stage holds 32 rows of one slice)
     int qs_row;        // shared-memory bytes of one row's slice of quants
     int meta_row;      // shared-memory bytes of one row's slice of scales (multiple of 16)
+    int max_q;         // capacity of the shared-memory problem table (routed + shared)
 };
 
 cudaError_t launch_router(const FwdParams &p, cudaStream_t st);
