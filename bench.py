@@ -11,8 +11,10 @@ synthetic inputs; the T=1..64 sweep is reported beside it.
 
 --impl reference times the CPU restatement of the reference MoE path (the
 reference is Rust and cannot be built here) on this host's cores, on the same
-workload. Under torchrun with N>1, each rank runs its own replica of the
-layer on its own T tokens (weak scaling) and rank 0 prints the line.
+workload. Under torchrun with N>1 the layer runs expert-parallel: rank g holds
+experts [g*E/N, (g+1)*E/N), routes its own T tokens and exchanges the routed
+rows over NCCL (moe_forward_ep); value = N*T tokens per step over the slowest
+rank's time (weak scaling). --strong splits T over the ranks instead.
 """
 import argparse
 import json
@@ -41,6 +43,7 @@ def parse():
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--strong", action="store_true", help="with N>1: T is the global batch, split over the ranks")
     return ap.parse_args()
 
 
@@ -81,9 +84,10 @@ def tensor_peak():
         return FALLBACK_BF16_TFLOPS, "fallback"
 
 
-def kernel_flops(cfg, T):
-    """Algorithmic FLOPs of the tensor-core expert GEMMs (no padding counted)."""
-    routed = 2 * T * cfg.k * cfg.H * cfg.I
+def kernel_flops(cfg, T, routed_rows=None):
+    """Algorithmic FLOPs of the tensor-core expert GEMMs (no padding counted);
+    routed_rows: the rows this rank's experts received (expert parallel)."""
+    routed = 2 * (T * cfg.k if routed_rows is None else routed_rows) * cfg.H * cfg.I
     shared = 2 * T * cfg.H * cfg.S
     return {"gate_up_tc": 2 * routed + 2 * shared, "down_tc": routed + shared}
 
@@ -149,13 +153,19 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def kernel_bytes(cfg, weights, sel_idx, T):
+def kernel_bytes(cfg, weights, sel_idx, T, expert_range=None, routed_rows=None):
     """Algorithmic bytes per launch of the expert kernels and of the whole layer.
     Weights of each routed expert are read once; activations travel as int8
-    blocks (1 byte + 8 bytes of scales per 32 values = 1.25 B/value)."""
+    blocks (1 byte + 8 bytes of scales per 32 values = 1.25 B/value). With
+    expert parallelism, sel_idx holds every rank's choices, expert_range the
+    rank's experts and routed_rows the rows it received; T its own tokens."""
     import numpy as np
-    U = len(np.unique(sel_idx[sel_idx >= 0]))
-    slots = T * cfg.k + (T if cfg.S else 0)
+    chosen = np.unique(sel_idx[sel_idx >= 0])
+    if expert_range is not None:
+        chosen = chosen[(chosen >= expert_range[0]) & (chosen < expert_range[1])]
+    U = len(chosen)
+    routed = T * cfg.k if routed_rows is None else routed_rows
+    slots = routed + (T if cfg.S else 0)
     per = {m: weights.tensor(f"blk.0.ffn_{m}_exps.weight").data.nbytes // cfg.E for m in ("gate", "up", "down")}
     sh = {m: (weights.tensor(f"blk.0.ffn_{m}_shexp.weight").data.nbytes if cfg.S else 0)
           for m in ("gate", "up", "down")}
@@ -163,7 +173,9 @@ def kernel_bytes(cfg, weights, sel_idx, T):
     gate_up = U * (per["gate"] + per["up"]) + sh["gate"] + sh["up"] + T * cfg.H * 1.25 + slots * W * 1.25
     down = U * per["down"] + sh["down"] + slots * W * 1.25 + slots * cfg.H * 4
     layer = (U * sum(per.values()) + sum(sh.values()) + cfg.E * cfg.H * 4 + 2 * T * cfg.H * 4 + T * cfg.k * 8)
-    return {"gate_up": gate_up, "down": down, "layer": layer, "U": U}
+    if expert_range is not None:   # activation rows out and expert outputs back through the exchange
+        layer += routed * cfg.H * 1.25 + routed * cfg.H * 4
+    return {"gate_up": gate_up, "down": down, "layer": layer, "U": U, "routed_rows": routed}
 
 
 def cpu_baseline(cfg, weights, x, seconds, threads):
@@ -232,11 +244,21 @@ def run_ours(args):
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=torch.device("cuda", local_rank))
     cfg = synth.CONFIGS[args.config]
-    T = args.tokens or max(cfg.tokens)
-    sweep_T = [] if args.no_sweep else [t for t in cfg.tokens if t != T]
+    T_arg = args.tokens or max(cfg.tokens)
+    ep = world > 1
+    # tokens of this rank: T (weak scaling) or T / world of a global batch of T (--strong)
+    T = T_arg // world if (ep and args.strong) else T_arg
+    if T < 1:
+        raise SystemExit(f"--strong needs at least {world} tokens")
+    sweep_T = [] if (args.no_sweep or ep) else [t for t in cfg.tokens if t != T]
     weights = synth.build_weights(cfg)
-    x_host = synth.gen_x(cfg, max([T] + sweep_T))
+    x_all = synth.gen_x(cfg, max([T] + sweep_T) * world)
+    x_host = x_all[rank * max([T] + sweep_T):(rank + 1) * max([T] + sweep_T)].copy()
     ctx = jm.Context(local_rank, max([T] + sweep_T), 1)
+    if ep:
+        ids = [jm.ep_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(ids, src=0)
+        ctx.ep_init(rank, world, ids[0])
     d, keep = synth.desc_for(cfg, weights)
     ctx.upload(0, d)
     # one dedicated stream for the library, the flush and the timing events
@@ -250,7 +272,10 @@ def run_ours(args):
     sw_dev = torch.empty((x_dev.shape[0], cfg.k), dtype=torch.float32, device="cuda")
 
     def step(t):
-        ctx.forward_ptrs(0, t, x_dev.data_ptr(), out_dev.data_ptr(), si_dev.data_ptr(), sw_dev.data_ptr())
+        if ep:
+            ctx.forward_ep_ptrs(0, t, x_dev.data_ptr(), out_dev.data_ptr())
+        else:
+            ctx.forward_ptrs(0, t, x_dev.data_ptr(), out_dev.data_ptr(), si_dev.data_ptr(), sw_dev.data_ptr())
 
     def barrier():
         if world > 1:
@@ -281,8 +306,18 @@ def run_ours(args):
         flush.fill_(i & 0xFF)
         step(T)
     torch.cuda.synchronize()
-    sel = si_dev[:T].cpu().numpy()
-    kb = kernel_bytes(cfg, weights, sel, T)
+    if ep:
+        # every rank's choices (one extra forward with selection output), for the rank's byte count
+        _, sel_local, _ = ctx.forward_ep(0, x_host[:T])
+        gathered = [torch.empty((T, cfg.k), dtype=torch.int32, device="cuda") for _ in range(world)]
+        dist.all_gather(gathered, torch.from_numpy(sel_local).cuda())
+        sel = torch.cat(gathered).cpu().numpy()
+        El = cfg.E // world
+        mine = (sel >= rank * El) & (sel < (rank + 1) * El)
+        kb = kernel_bytes(cfg, weights, sel, T, (rank * El, (rank + 1) * El), int(mine.sum()))
+    else:
+        sel = si_dev[:T].cpu().numpy()
+        kb = kernel_bytes(cfg, weights, sel, T)
     sampler.wait_first()
     # keep the GPU busy until the timed region starts so the samples see it under load
     for i in range(max(args.warmup, 20)):
@@ -296,13 +331,15 @@ def run_ours(args):
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
         total_ms = float(tt.item())
     value = world * T * args.steps / (total_ms / 1e3)
+    # the rank-0 kernels explain the rank-0 time; the slowest rank sets the value
     tc = "gate_up_tc" in prof
     cands = ("gate_up_tc", "down_tc") if tc else ("gate_up", "down")
+    rows_here = kb["routed_rows"]
     dom = max(cands, key=lambda k: prof.get(k, (0, 1))[0])
     dom_ms = prof[dom][0] / prof[dom][1]
     hbm, peak_kind = peaks()
     if tc:   # tensor-bound: algorithmic FLOPs of the dominant GEMM per launch over its duration
-        fl = kernel_flops(cfg, T)[dom]
+        fl = kernel_flops(cfg, T, rows_here)[dom]
         tpk, tpk_kind = tensor_peak()
         ach = fl / (dom_ms / 1e3) / 1e12
         roofline = {"bound": "tensor", "kernel": dom, "achieved": round(ach, 1), "peak": tpk, "unit": "TFLOP/s",
@@ -341,7 +378,10 @@ def run_ours(args):
         flush.fill_(i & 0xFF)
         torch.cuda.synchronize()
         t0 = time.perf_counter()
-        ctx.forward_ptrs(0, T, xh.data_ptr(), oh.data_ptr(), sih.data_ptr(), swh.data_ptr(), jm.PTR_HOST)
+        if ep:
+            ctx.forward_ep_ptrs(0, T, xh.data_ptr(), oh.data_ptr(), jm.PTR_HOST)
+        else:
+            ctx.forward_ptrs(0, T, xh.data_ptr(), oh.data_ptr(), sih.data_ptr(), swh.data_ptr(), jm.PTR_HOST)
         e2e_s += time.perf_counter() - t0
     if world > 1:
         tt = torch.tensor([e2e_s], device="cuda")
@@ -360,12 +400,13 @@ def run_ours(args):
         line = {
             "metric": "MoE-layer tokens/s", "value": round(value, 1), "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(layer_ms, 5),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
+            "higher_is_better": True, "scaling": "strong" if (ep and args.strong) else "weak",
+            "vs_baseline": None, "dtype": "int8",
             "data": "synthetic (seeded N(0,1) activations, N(0,0.02) weights quantised to GGUF blocks)",
             "config": {"workload": f"{cfg.name} T={T}", "T": T, "H": cfg.H, "E": cfg.E, "k": cfg.k, "I": cfg.I,
                        "S": cfg.S, "quant": "Q4_K" if cfg.quant == 12 else "Q8_0",
                        "experts_routed": kb["U"], "global_batch": world * T,
-                       "parallelism": f"replicas{world}" if world > 1 else "single",
+                       "parallelism": f"ep{world}" if ep else "single",
                        "l2": "flushed between timed steps (256 MiB write); per-step CUDA events"},
             "roofline": roofline,
             "layer_roofline": {"bytes": int(kb["layer"]), "gbs": round(kb["layer"] / (layer_ms / 1e3) / 1e9, 1),
@@ -374,7 +415,7 @@ def run_ours(args):
             "gpu_launches": int(launches),
             "e2e": {"value": round(e2e, 1), "unit": "tokens/s",
                     "h2d_bytes_per_step": int(T * cfg.H * 4),
-                    "d2h_bytes_per_step": int(T * cfg.H * 4 + T * cfg.k * 8)},
+                    "d2h_bytes_per_step": int(T * cfg.H * 4 + (0 if ep else T * cfg.k * 8))},
             "sweep": sweep,
             "cpu_baseline": cpu,
             "clocks": clocks,

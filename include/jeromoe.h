@@ -237,6 +237,48 @@ int moe_route_noalloc(int32_t device, const float *x, const float *router, const
                       float routed_scale, int32_t n_groups, int32_t topk_groups, int32_t *sel_idx, float *sel_w,
                       int32_t *offsets, int32_t *perm_token, void *stream);
 
+/* ---- expert parallelism (one process per GPU) ----
+ * No counterpart in the reference, which runs the block on one host. A world
+ * of G contexts (one per GPU, typically one process each) shards the routed
+ * experts: rank g holds experts [g*E/G, (g+1)*E/G) of every layer, the router
+ * and the shared expert are replicated, and each rank routes its own tokens.
+ * A forward exchanges the routed token rows (int8 activation blocks with
+ * their scales) with the owning ranks and the expert outputs back over NCCL
+ * (send/recv, one group per direction); the combine is local. Row t of a
+ * rank's result equals moe_forward of that rank's tokens on one GPU holding
+ * all experts.
+ *
+ * Bootstrap: one rank calls moe_ep_unique_id and passes the bytes to every
+ * rank out of band; each rank then calls moe_ep_init before uploading layers.
+ * Every rank must call moe_forward_ep for the same layers in the same order
+ * (T may differ per rank, 0 included). NCCL is loaded at run time
+ * (libnccl.so.2, the one already in the process when there is one). */
+#define MOE_EP_ID_BYTES 128
+
+int moe_ep_unique_id(uint8_t *id_out);
+
+/* Binds ctx to rank `rank` of `world` (E of every layer must be a multiple of
+ * world). Collective: blocks until all ranks have joined. world == 1 is
+ * allowed (an exchange with itself). */
+int moe_ep_init(moe_ctx *ctx, int32_t rank, int32_t world, const uint8_t *id);
+
+/* moe_forward for this rank's T tokens with the experts sharded across the
+ * world. Host synchronisation: once per call, after the all-gather of the
+ * per-expert slot counts (the exchange sizes). */
+int moe_forward_ep(moe_ctx *ctx, int32_t layer, int32_t T, const float *x, float *out,
+                   int32_t *sel_idx, float *sel_w, int32_t ptr_kind);
+
+/* The exchange plan of one rank, as moe_forward_ep computes it from the
+ * all-gathered slot offsets all_offsets [world][E+1] (host work only):
+ * send_cnt / send_off / recv_cnt / recv_off [world] rows per peer; problems
+ * [E/world][3] = (local expert, first slot, slot count) for the local experts
+ * that received rows, in expert order (*n_problems of them); segments
+ * [world*E/world][3] = (first slot, first received row, rows) of each
+ * (local expert, source rank) pair (*n_segments). */
+int moe_ep_plan(int32_t rank, int32_t world, int32_t E, const int32_t *all_offsets, int32_t *send_cnt,
+                int32_t *send_off, int32_t *recv_cnt, int32_t *recv_off, int32_t *problems, int32_t *n_problems,
+                int32_t *segments, int32_t *n_segments);
+
 /* ---- host utilities (no device work) ---- */
 
 /* GGUF row bytes for cols values of quant (0 if cols is not a whole number of blocks). */

@@ -12,8 +12,11 @@
 #include <vector>
 
 #include "../../include/jeromoe.h"
+#include "ep_plan.h"
+#include "kernels.h"
 #include "layout.h"
 #include "moe_device.h"
+#include "nccl_dl.h"
 
 using namespace jmoe;
 
@@ -106,6 +109,34 @@ struct Profiler {
 
 }  // namespace
 
+namespace {
+
+// Expert-parallel state of a context: the communicator and a device arena for
+// the exchange buffers and the local expert stage, grown on demand.
+struct EpState {
+    int rank = 0, world = 0;   // world == 0: not in expert-parallel mode
+    ncclComm_t comm = nullptr;
+    void *arena = nullptr;
+    size_t arena_bytes = 0;
+    int rows_cap = 0, send_cap = 0, H = 0, W = 0, E = 0;   // dims the arena was carved for
+    bool tc = false;
+    int32_t *all_off = nullptr;   // [world][E+1]
+    uint8_t *send_buf = nullptr, *recv_buf = nullptr;
+    int8_t *xq = nullptr;
+    float *xd = nullptr, *xs = nullptr;
+    int32_t *perm = nullptr;      // local slot -> received row
+    uint8_t *plan_dev = nullptr;  // n_active | problems | segments (one upload)
+    int8_t *aq = nullptr;
+    float *ad = nullptr, *as = nullptr, *y = nullptr;
+    int32_t *tile_off = nullptr, *zero = nullptr;
+    void *a16 = nullptr, *a16dn = nullptr;
+    int32_t *h_off = nullptr;     // pinned: all-gathered offsets
+    uint8_t *h_plan = nullptr;    // pinned: plan upload staging
+    size_t h_off_bytes = 0, h_plan_bytes = 0;
+};
+
+}  // namespace
+
 struct moe_ctx {
     moe_device_spec spec{};
     cudaStream_t own_stream = nullptr;
@@ -119,6 +150,7 @@ struct moe_ctx {
     int num_sms = 148;
     int *status_host = nullptr;   // pinned word for the device status flag
     Profiler prof;
+    EpState ep;
 };
 
 namespace {
@@ -418,6 +450,143 @@ void free_layer(LayerStore &L)
     L = LayerStore{};
 }
 
+// Parameters of a forward over this context's T tokens (routing, local slots,
+// combine); buffers from the scratch, or the caller's device buffers.
+FwdParams local_params(moe_ctx *ctx, const LayerStore &L, int T, int ptr_kind, const float *x, float *out,
+                       int32_t *sel_idx, float *sel_w)
+{
+    Scratch &s = ctx->scratch;
+    FwdParams p{};
+    p.T = T; p.H = L.H; p.E = L.E; p.k = L.k; p.I = L.I; p.S = L.S;
+    p.route_mode = L.route_mode; p.normalize = L.normalize;
+    p.n_groups = L.n_groups; p.topk_groups = L.topk_groups; p.routed_scale = L.routed_scale;
+    p.mask_words = (T + 31) / 32;
+    p.quant_x = L.dev.gate.type != FMT_F32 || (L.S && L.dev.sh_gate.type != FMT_F32);
+    p.max_problems = std::min(L.E, T * L.k) + (L.S ? 1 : 0);
+    p.router = L.router; p.logit_bias = L.logit_bias; p.sel_bias = L.sel_bias;
+    p.x = ptr_kind == MOE_PTR_DEVICE ? x : s.x;
+    p.out = ptr_kind == MOE_PTR_DEVICE ? out : s.out;
+    p.xq = s.xq; p.xd = s.xd; p.xs = s.xs; p.logits = s.logits;
+    p.sel_idx = (ptr_kind == MOE_PTR_DEVICE && sel_idx) ? sel_idx : s.sel_idx;
+    p.sel_w = (ptr_kind == MOE_PTR_DEVICE && sel_w) ? sel_w : s.sel_w;
+    p.mask = s.mask; p.wprefix = s.wprefix; p.offsets = s.offsets; p.perm_token = s.perm_token;
+    p.problems = s.problems; p.n_active = s.n_active;
+    p.aq = s.aq; p.ad = s.ad; p.as = s.as; p.af = s.af_buf; p.W = s.W; p.y = s.y;
+    p.y_rows = nullptr;
+    p.err = s.err;
+    p.tile_off = s.tile_off;
+    p.a16 = s.a16; p.a16dn = s.a16dn;
+    p.a16_stride = s.H; p.a16dn_stride = s.W; p.slots_cap = s.slots_cap;
+    p.use_tc = use_tensor_cores(ctx->spec, L, s, T);
+    return p;
+}
+
+// ------------------------------------------------------ expert parallelism
+
+struct EpDims {
+    int world, E, H, W, rows, send;   // rows: received-slot capacity; send: sent-row capacity
+    bool tc;
+};
+
+// Bytes of the plan upload: n_active (padded to 16) | problems [E] | segments [world * E].
+size_t ep_plan_bytes(int world, int E)
+{
+    return 16 + align_up((size_t)E * sizeof(Problem), 16) + (size_t)world * E * sizeof(EpSegment);
+}
+
+// Carves the expert-parallel arena (or only measures it when base == nullptr).
+size_t ep_carve(const EpDims &d, uint8_t *base, EpState *ep)
+{
+    size_t off = 0;
+    auto take = [&](size_t bytes) -> uint8_t * {
+        uint8_t *q = base ? base + off : nullptr;
+        off += align_up(bytes ? bytes : 1, 256);
+        return q;
+    };
+    const size_t R = (size_t)std::max(d.rows, 1), H = d.H, W = std::max(d.W, 32), rb = ep_row_bytes(d.H);
+    EpState t;
+    t.all_off = (int32_t *)take((size_t)d.world * (d.E + 1) * 4);
+    t.send_buf = take((size_t)std::max(d.send, 1) * rb);
+    t.recv_buf = take(R * rb);
+    t.xq = (int8_t *)take(R * H);
+    t.xd = (float *)take(R * (H / 32) * 4);
+    t.xs = (float *)take(R * (H / 32) * 4);
+    t.perm = (int32_t *)take(R * 4);
+    t.plan_dev = take(ep_plan_bytes(d.world, d.E));
+    t.aq = (int8_t *)take(R * W);
+    t.ad = (float *)take(R * (W / 32) * 4);
+    t.as = (float *)take(R * (W / 32) * 4);
+    t.y = (float *)take(R * H * 4);
+    t.tile_off = (int32_t *)take(4 * (size_t)kTileOffStride * 4);
+    t.zero = (int32_t *)take(4);
+    t.a16 = d.tc ? take(R * H * 2) : nullptr;
+    t.a16dn = d.tc ? take(R * W * 2) : nullptr;
+    if (ep && base) {
+        ep->all_off = t.all_off; ep->send_buf = t.send_buf; ep->recv_buf = t.recv_buf;
+        ep->xq = t.xq; ep->xd = t.xd; ep->xs = t.xs; ep->perm = t.perm; ep->plan_dev = t.plan_dev;
+        ep->aq = t.aq; ep->ad = t.ad; ep->as = t.as; ep->y = t.y; ep->tile_off = t.tile_off; ep->zero = t.zero;
+        ep->a16 = t.a16; ep->a16dn = t.a16dn;
+        ep->rows_cap = (int)R; ep->send_cap = std::max(d.send, 1); ep->H = d.H; ep->W = (int)W; ep->E = d.E;
+        ep->tc = d.tc;
+        ep->arena_bytes = off;
+    }
+    return off;
+}
+
+// Grows the arena (and the pinned staging) to hold d.
+int ep_reserve(moe_ctx *ctx, EpDims d)
+{
+    EpState &ep = ctx->ep;
+    const bool fits = ep.arena && ep.rows_cap >= d.rows && ep.send_cap >= d.send && ep.H >= d.H &&
+                      ep.W >= std::max(d.W, 32) && ep.E >= d.E && (ep.tc || !d.tc);
+    if (!fits) {
+        if (ep.arena) {
+            // an earlier device-pointer forward may still be using the old arena
+            CUDA_TRY(ctx, cudaStreamSynchronize(ctx->stream), "cudaStreamSynchronize");
+            d.rows = std::max(d.rows, 2 * ep.rows_cap);
+            d.send = std::max(d.send, ep.send_cap);
+            d.H = std::max(d.H, ep.H);
+            d.W = std::max(d.W, ep.W);
+            d.E = std::max(d.E, ep.E);
+            d.tc = d.tc || ep.tc;
+            cudaFree(ep.arena);
+            ep.arena = nullptr;
+        }
+        d.rows = std::max(d.rows, 256);
+        const size_t bytes = ep_carve(d, nullptr, nullptr);
+        void *blk = nullptr;
+        CUDA_TRY(ctx, cudaMalloc(&blk, bytes), "cudaMalloc(expert-parallel arena)");
+        ep.arena = blk;
+        ep_carve(d, static_cast<uint8_t *>(blk), &ep);
+        CUDA_TRY(ctx, cudaMemset(ep.zero, 0, 4), "cudaMemset");
+    }
+    const size_t off_bytes = (size_t)ep.world * (ep.E + 1) * 4, plan_bytes = ep_plan_bytes(ep.world, ep.E);
+    if (ep.h_off_bytes < off_bytes) {
+        if (ep.h_off) cudaFreeHost(ep.h_off);
+        ep.h_off = nullptr;
+        CUDA_TRY(ctx, cudaMallocHost(&ep.h_off, off_bytes), "cudaMallocHost");
+        ep.h_off_bytes = off_bytes;
+    }
+    if (ep.h_plan_bytes < plan_bytes) {
+        if (ep.h_plan) cudaFreeHost(ep.h_plan);
+        ep.h_plan = nullptr;
+        CUDA_TRY(ctx, cudaMallocHost(&ep.h_plan, plan_bytes), "cudaMallocHost");
+        ep.h_plan_bytes = plan_bytes;
+    }
+    return MOE_OK;
+}
+
+int nccl_fail(moe_ctx *ctx, const NcclApi *nc, ncclResult_t r, const char *what)
+{
+    return fail(ctx, MOE_ERR_NCCL, "%s: %s", what, nc ? nc->GetErrorString(r) : "NCCL unavailable");
+}
+
+#define NCCL_TRY(ctx, nc, call, what)                              \
+    do {                                                           \
+        ncclResult_t r_ = (call);                                  \
+        if (r_ != ncclSuccess) return nccl_fail(ctx, nc, r_, what); \
+    } while (0)
+
 }  // namespace
 
 // ================================================================= C ABI
@@ -461,6 +630,13 @@ int moe_ctx_destroy(moe_ctx *ctx)
     if (ctx->scratch.block) cudaFree(ctx->scratch.block);
     ctx->prof.release();
     if (ctx->status_host) cudaFreeHost(ctx->status_host);
+    EpState &ep = ctx->ep;
+    if (ep.comm) {
+        if (const NcclApi *nc = nccl_api()) nc->CommDestroy(ep.comm);
+    }
+    if (ep.arena) cudaFree(ep.arena);
+    if (ep.h_off) cudaFreeHost(ep.h_off);
+    if (ep.h_plan) cudaFreeHost(ep.h_plan);
     if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
     delete ctx;
     return MOE_OK;
@@ -545,6 +721,19 @@ int moe_layer_upload(moe_ctx *ctx, int32_t layer, const moe_layer_desc *desc)
     Validated v;
     int rc = validate_desc(ctx, desc, &v);
     if (rc) return rc;
+    if (ctx->ep.world) {
+        // expert parallel: this rank keeps its contiguous share of the routed experts
+        const int G = ctx->ep.world;
+        if (v.E % G)
+            return fail(ctx, MOE_ERR_CAPABILITY_MISMATCH, "%d experts do not split over %d ranks", v.E, G);
+        if (v.gate.type == MOE_QUANT_F32)
+            return fail(ctx, MOE_ERR_CAPABILITY_MISMATCH, "expert parallelism needs quantised expert stacks");
+        const int El = v.E / G, e0 = ctx->ep.rank * El;
+        for (MatSpec *m : {&v.gate, &v.up, &v.down}) {
+            m->data += (size_t)e0 * m->rows * gguf_row_bytes(m->type, m->cols);
+            m->experts = El;
+        }
+    }
     CUDA_TRY(ctx, cudaSetDevice(ctx->spec.device), "cudaSetDevice");
 
     // admission against free HBM before allocating anything
@@ -645,7 +834,7 @@ int moe_layer_upload(moe_ctx *ctx, int32_t layer, const moe_layer_desc *desc)
             return fail(ctx, MOE_ERR_CUDA, "cuTensorMapEncodeTiled failed (CUresult %d)", r);
         }
     }
-    L.gguf_bytes = (size_t)v.E * v.H * 4;
+    L.gguf_bytes = (size_t)v.E * v.H * 4;   // the router is replicated; expert stacks count this rank's share
     for (const MatSpec *m : {&v.gate, &v.up, &v.down, &v.sg, &v.su, &v.sd})
         if (m->present) L.gguf_bytes += gguf_row_bytes(m->type, m->cols) * m->rows * m->experts;
     ctx->upload_count++;
@@ -672,28 +861,7 @@ int moe_forward(moe_ctx *ctx, int32_t layer, int32_t T, const float *x, float *o
     CUDA_TRY(ctx, cudaSetDevice(ctx->spec.device), "cudaSetDevice");
     Scratch &s = ctx->scratch;
     cudaStream_t st = ctx->stream;
-
-    FwdParams p{};
-    p.T = T; p.H = L.H; p.E = L.E; p.k = L.k; p.I = L.I; p.S = L.S;
-    p.route_mode = L.route_mode; p.normalize = L.normalize;
-    p.n_groups = L.n_groups; p.topk_groups = L.topk_groups; p.routed_scale = L.routed_scale;
-    p.mask_words = (T + 31) / 32;
-    p.quant_x = L.dev.gate.type != FMT_F32 || (L.S && L.dev.sh_gate.type != FMT_F32);
-    p.max_problems = std::min(L.E, T * L.k) + (L.S ? 1 : 0);
-    p.router = L.router; p.logit_bias = L.logit_bias; p.sel_bias = L.sel_bias;
-    p.x = ptr_kind == MOE_PTR_DEVICE ? x : s.x;
-    p.out = ptr_kind == MOE_PTR_DEVICE ? out : s.out;
-    p.xq = s.xq; p.xd = s.xd; p.xs = s.xs; p.logits = s.logits;
-    p.sel_idx = (ptr_kind == MOE_PTR_DEVICE && sel_idx) ? sel_idx : s.sel_idx;
-    p.sel_w = (ptr_kind == MOE_PTR_DEVICE && sel_w) ? sel_w : s.sel_w;
-    p.mask = s.mask; p.wprefix = s.wprefix; p.offsets = s.offsets; p.perm_token = s.perm_token;
-    p.problems = s.problems; p.n_active = s.n_active;
-    p.aq = s.aq; p.ad = s.ad; p.as = s.as; p.af = s.af_buf; p.W = s.W; p.y = s.y;
-    p.err = s.err;
-    p.tile_off = s.tile_off;
-    p.a16 = s.a16; p.a16dn = s.a16dn;
-    p.a16_stride = s.H; p.a16dn_stride = s.W; p.slots_cap = s.slots_cap;
-    p.use_tc = use_tensor_cores(ctx->spec, L, s, T);
+    FwdParams p = local_params(ctx, L, T, ptr_kind, x, out, sel_idx, sel_w);
 
     if (ptr_kind == MOE_PTR_HOST)
         CUDA_TRY(ctx, cudaMemcpyAsync(s.x, x, (size_t)T * L.H * 4, cudaMemcpyHostToDevice, st), "copy x");
@@ -865,6 +1033,268 @@ int moe_debug_block_dots(int32_t device, int32_t quant, const void *w, const flo
     } while (0);
     cudaFree(dq); cudaFree(dm); cudaFree(dxq); cudaFree(dx); cudaFree(dxd); cudaFree(dxs); cudaFree(dis);
     return rc;
+}
+
+int moe_ep_unique_id(uint8_t *id_out)
+{
+    if (!id_out) return fail(nullptr, MOE_ERR_INVALID_ARGS, "null id buffer");
+    const char *why = nullptr;
+    const NcclApi *nc = nccl_api(&why);
+    if (!nc) return fail(nullptr, MOE_ERR_NCCL, "%s", why);
+    ncclUniqueId uid;
+    NCCL_TRY(nullptr, nc, nc->GetUniqueId(&uid), "ncclGetUniqueId");
+    static_assert(sizeof(uid.internal) == MOE_EP_ID_BYTES, "NCCL unique id size");
+    memcpy(id_out, uid.internal, MOE_EP_ID_BYTES);
+    return MOE_OK;
+}
+
+int moe_ep_init(moe_ctx *ctx, int32_t rank, int32_t world, const uint8_t *id)
+{
+    if (!ctx || !id) return fail(ctx, MOE_ERR_INVALID_ARGS, "null argument");
+    if (world < 1 || rank < 0 || rank >= world)
+        return fail(ctx, MOE_ERR_INVALID_ARGS, "rank %d outside a world of %d", rank, world);
+    if (ctx->ep.world) return fail(ctx, MOE_ERR_INVALID_ARGS, "context is already expert-parallel");
+    for (const auto &L : ctx->layers)
+        if (L.present) return fail(ctx, MOE_ERR_INVALID_ARGS, "moe_ep_init must come before the layer uploads");
+    const char *why = nullptr;
+    const NcclApi *nc = nccl_api(&why);
+    if (!nc) return fail(ctx, MOE_ERR_NCCL, "%s", why);
+    CUDA_TRY(ctx, cudaSetDevice(ctx->spec.device), "cudaSetDevice");
+    ncclUniqueId uid;
+    memcpy(uid.internal, id, MOE_EP_ID_BYTES);
+    ncclComm_t comm = nullptr;
+    NCCL_TRY(ctx, nc, nc->CommInitRank(&comm, world, uid, rank), "ncclCommInitRank");
+    ctx->ep.comm = comm;
+    ctx->ep.rank = rank;
+    ctx->ep.world = world;
+    return MOE_OK;
+}
+
+int moe_ep_plan(int32_t rank, int32_t world, int32_t E, const int32_t *all_offsets, int32_t *send_cnt,
+                int32_t *send_off, int32_t *recv_cnt, int32_t *recv_off, int32_t *problems, int32_t *n_problems,
+                int32_t *segments, int32_t *n_segments)
+{
+    if (!all_offsets || !send_cnt || !send_off || !recv_cnt || !recv_off || !problems || !n_problems || !segments ||
+        !n_segments)
+        return fail(nullptr, MOE_ERR_INVALID_ARGS, "null argument");
+    EpPlan plan;
+    if (!ep_plan(rank, world, E, all_offsets, plan))
+        return fail(nullptr, MOE_ERR_INVALID_ARGS, "bad plan input (rank %d, world %d, %d experts)", rank, world, E);
+    for (int r = 0; r < world; r++) {
+        send_cnt[r] = plan.send_cnt[r];
+        send_off[r] = plan.send_off[r];
+        recv_cnt[r] = plan.recv_cnt[r];
+        recv_off[r] = plan.recv_off[r];
+    }
+    *n_problems = (int32_t)plan.problems.size();
+    for (size_t i = 0; i < plan.problems.size(); i++) {
+        problems[3 * i] = plan.problems[i].expert;
+        problems[3 * i + 1] = plan.problems[i].slot0;
+        problems[3 * i + 2] = plan.problems[i].count;
+    }
+    *n_segments = (int32_t)plan.segs.size();
+    for (size_t i = 0; i < plan.segs.size(); i++) {
+        segments[3 * i] = plan.segs[i].slot_base;
+        segments[3 * i + 1] = plan.segs[i].row_base;
+        segments[3 * i + 2] = plan.segs[i].count;
+    }
+    return MOE_OK;
+}
+
+// Expert-parallel forward: route the local tokens, all-gather the slot
+// offsets (the one host synchronisation), send each routed row to the rank
+// that owns its expert, run the local experts over the received rows (outputs
+// written at their received row), send the outputs back, then the local
+// shared expert and the combine.
+int moe_forward_ep(moe_ctx *ctx, int32_t layer, int32_t T, const float *x, float *out, int32_t *sel_idx,
+                   float *sel_w, int32_t ptr_kind)
+{
+    if (!ctx) return fail(nullptr, MOE_ERR_INVALID_ARGS, "null context");
+    EpState &ep = ctx->ep;
+    if (!ep.world) return fail(ctx, MOE_ERR_INVALID_ARGS, "moe_ep_init was not called on this context");
+    if (layer < 0 || layer >= (int)ctx->layers.size())
+        return fail(ctx, MOE_ERR_INVALID_ARGS, "layer %d outside 0..%d", layer, (int)ctx->layers.size() - 1);
+    LayerStore &L = ctx->layers[layer];
+    if (!L.present) return fail(ctx, MOE_ERR_NOT_UPLOADED, "layer %d was never uploaded", layer);
+    if (T < 0) return fail(ctx, MOE_ERR_INVALID_ARGS, "negative token count");
+    if (T > ctx->spec.max_tokens)
+        return fail(ctx, MOE_ERR_CONTEXT_LENGTH, "T=%d exceeds max_tokens=%d", T, ctx->spec.max_tokens);
+    if (ptr_kind != MOE_PTR_HOST && ptr_kind != MOE_PTR_DEVICE)
+        return fail(ctx, MOE_ERR_INVALID_ARGS, "unknown pointer kind %d", ptr_kind);
+    if (T > 0 && (!x || !out)) return fail(ctx, MOE_ERR_INVALID_ARGS, "null x or out");
+    if (T > 0 && ptr_kind == MOE_PTR_DEVICE && (((uintptr_t)x | (uintptr_t)out) & 15))
+        return fail(ctx, MOE_ERR_INVALID_ARGS, "device x and out must be 16-byte aligned");
+    const NcclApi *nc = nccl_api();
+    if (!nc) return fail(ctx, MOE_ERR_NCCL, "NCCL unavailable");
+    CUDA_TRY(ctx, cudaSetDevice(ctx->spec.device), "cudaSetDevice");
+    Scratch &s = ctx->scratch;
+    cudaStream_t st = ctx->stream;
+    const int G = ep.world, me = ep.rank, E = L.E, El = E / G, H = L.H;
+    FwdParams p = local_params(ctx, L, T, ptr_kind, x, out, sel_idx, sel_w);
+    Marker mk{nullptr, nullptr};
+    if (ctx->prof.on) {
+        ctx->prof.stream = st;
+        mk = Marker{&Profiler::mark_cb, &ctx->prof};
+    }
+    int rc;
+    // the arena's all-gather buffer and pinned staging (rows and sends sized below)
+    EpDims dims{G, E, H, std::max(L.I, s.W), 1, std::max(T * L.k, 1), tc_possible(ctx->spec)};
+    if ((rc = ep_reserve(ctx, dims))) return rc;
+
+    mk.mark(nullptr);
+    cudaError_t ce;
+    if (T > 0) {
+        if (ptr_kind == MOE_PTR_HOST)
+            CUDA_TRY(ctx, cudaMemcpyAsync(s.x, x, (size_t)T * H * 4, cudaMemcpyHostToDevice, st), "copy x");
+        CUDA_TRY(ctx, cudaMemsetAsync(p.mask, 0, sizeof(uint32_t) * (size_t)E * p.mask_words, st), "memset");
+        if ((ce = launch_router(p, st)) != cudaSuccess) return cuda_fail(ctx, ce, "router");
+        mk.mark("router");
+        if ((ce = launch_topk(p, st)) != cudaSuccess) return cuda_fail(ctx, ce, "topk");
+        mk.mark("topk");
+        if ((ce = launch_scan(p, st)) != cudaSuccess) return cuda_fail(ctx, ce, "scan");
+        mk.mark("scan");
+    } else {
+        CUDA_TRY(ctx, cudaMemsetAsync(s.offsets, 0, (size_t)(E + 1) * 4, st), "memset");
+    }
+
+    // exchange sizes: every rank's slot offsets by expert
+    NCCL_TRY(ctx, nc, nc->AllGather(s.offsets, ep.all_off, (size_t)E + 1, ncclInt32, ep.comm, st), "ncclAllGather");
+    CUDA_TRY(ctx, cudaMemcpyAsync(ep.h_off, ep.all_off, (size_t)G * (E + 1) * 4, cudaMemcpyDeviceToHost, st),
+             "copy offsets");
+    CUDA_TRY(ctx, cudaStreamSynchronize(st), "exchange sizes");
+    mk.mark("ep_sizes");
+    EpPlan plan;
+    if (!ep_plan(me, G, E, ep.h_off, plan)) return fail(ctx, MOE_ERR_CUDA, "inconsistent slot offsets from the ranks");
+    dims.rows = plan.n_recv;
+    if ((rc = ep_reserve(ctx, dims))) return rc;
+    const size_t rb = ep_row_bytes(H);
+
+    // plan upload: n_active | problems | segments
+    {
+        uint8_t *h = ep.h_plan;
+        *reinterpret_cast<int32_t *>(h) = (int32_t)plan.problems.size();
+        Problem *hp = reinterpret_cast<Problem *>(h + 16);
+        for (size_t i = 0; i < plan.problems.size(); i++)
+            hp[i] = Problem{plan.problems[i].expert, plan.problems[i].slot0, plan.problems[i].count, 0};
+        EpSegment *hs = reinterpret_cast<EpSegment *>(h + 16 + align_up((size_t)ep.E * sizeof(Problem), 16));
+        for (size_t i = 0; i < plan.segs.size(); i++) hs[i] = plan.segs[i];
+        CUDA_TRY(ctx, cudaMemcpyAsync(ep.plan_dev, h, ep_plan_bytes(G, ep.E), cudaMemcpyHostToDevice, st),
+                 "copy plan");
+    }
+    int32_t *d_nact = reinterpret_cast<int32_t *>(ep.plan_dev);
+    Problem *d_prob = reinterpret_cast<Problem *>(ep.plan_dev + 16);
+    const void *d_segs = ep.plan_dev + 16 + align_up((size_t)ep.E * sizeof(Problem), 16);
+    if ((ce = launch_ep_segments(d_segs, (int)plan.segs.size(), ep.perm, ctx->num_sms, st)) != cudaSuccess)
+        return cuda_fail(ctx, ce, "ep segments");
+
+    // dispatch: routed rows to the owners of their experts
+    if (T > 0 && (ce = launch_ep_pack(p.xq, p.xd, p.xs, p.perm_token, T * L.k, H, ep.send_buf, ctx->num_sms, st)) !=
+                     cudaSuccess)
+        return cuda_fail(ctx, ce, "ep pack");
+    NCCL_TRY(ctx, nc, nc->GroupStart(), "ncclGroupStart");
+    for (int r = 0; r < G; r++) {
+        if (plan.send_cnt[r])
+            NCCL_TRY(ctx, nc,
+                     nc->Send(ep.send_buf + (size_t)plan.send_off[r] * rb, (size_t)plan.send_cnt[r] * rb, ncclUint8,
+                              r, ep.comm, st),
+                     "ncclSend");
+        if (plan.recv_cnt[r])
+            NCCL_TRY(ctx, nc,
+                     nc->Recv(ep.recv_buf + (size_t)plan.recv_off[r] * rb, (size_t)plan.recv_cnt[r] * rb, ncclUint8,
+                              r, ep.comm, st),
+                     "ncclRecv");
+    }
+    NCCL_TRY(ctx, nc, nc->GroupEnd(), "ncclGroupEnd");
+    if ((ce = launch_ep_unpack(ep.recv_buf, plan.n_recv, H, ep.xq, ep.xd, ep.xs, ctx->num_sms, st)) != cudaSuccess)
+        return cuda_fail(ctx, ce, "ep unpack");
+    mk.mark("ep_dispatch");
+
+    // the local experts over the received rows
+    if (plan.n_recv > 0) {
+        FwdParams pe{};
+        pe.T = plan.n_recv; pe.H = H; pe.E = El; pe.k = 1; pe.I = L.I; pe.S = 0;
+        pe.quant_x = 1;
+        pe.max_problems = std::max(El, 1);
+        pe.xq = ep.xq; pe.xd = ep.xd; pe.xs = ep.xs;
+        pe.perm_token = ep.perm; pe.problems = d_prob; pe.n_active = d_nact;
+        pe.aq = ep.aq; pe.ad = ep.ad; pe.as = ep.as; pe.af = nullptr; pe.W = ep.W;
+        pe.y = ep.y; pe.y_rows = ep.perm;
+        pe.err = s.err;
+        pe.tile_off = ep.tile_off;
+        pe.a16 = ep.a16; pe.a16dn = ep.a16dn; pe.a16_stride = H; pe.a16dn_stride = ep.W; pe.slots_cap = ep.rows_cap;
+        Scratch tcs{};
+        tcs.tc = ep.tc;
+        pe.use_tc = use_tensor_cores(ctx->spec, L, tcs, plan.n_recv);
+        if (pe.use_tc) {
+            if ((ce = launch_prefill(pe, L.dev, L.maps, ctx->num_sms, mk, st)) != cudaSuccess)
+                return cuda_fail(ctx, ce, "experts (tensor cores)");
+        } else {
+            if ((ce = launch_gate_up(pe, L.dev, L.maps, 0, ctx->num_sms, st)) != cudaSuccess)
+                return cuda_fail(ctx, ce, "gate_up");
+            mk.mark("gate_up");
+            if ((ce = launch_down(pe, L.dev, L.maps, 0, ctx->num_sms, st)) != cudaSuccess)
+                return cuda_fail(ctx, ce, "down");
+            mk.mark("down");
+        }
+    }
+
+    // combine exchange: outputs back to their source ranks, in the sources' slot order
+    NCCL_TRY(ctx, nc, nc->GroupStart(), "ncclGroupStart");
+    for (int r = 0; r < G; r++) {
+        if (plan.recv_cnt[r])
+            NCCL_TRY(ctx, nc,
+                     nc->Send(ep.y + (size_t)plan.recv_off[r] * H, (size_t)plan.recv_cnt[r] * H, ncclFloat32, r,
+                              ep.comm, st),
+                     "ncclSend");
+        if (plan.send_cnt[r])
+            NCCL_TRY(ctx, nc,
+                     nc->Recv(s.y + (size_t)plan.send_off[r] * H, (size_t)plan.send_cnt[r] * H, ncclFloat32, r,
+                              ep.comm, st),
+                     "ncclRecv");
+    }
+    NCCL_TRY(ctx, nc, nc->GroupEnd(), "ncclGroupEnd");
+    mk.mark("ep_return");
+
+    if (T > 0) {
+        if (L.S > 0) {   // the replicated shared expert over the local tokens
+            if (p.use_tc) {
+                FwdParams ps = p;
+                ps.n_active = ep.zero;   // no routed problems in this pass
+                if ((ce = launch_prefill(ps, L.dev, L.maps, ctx->num_sms, mk, st)) != cudaSuccess)
+                    return cuda_fail(ctx, ce, "shared expert (tensor cores)");
+            } else {
+                if ((ce = launch_gate_up(p, L.dev, L.maps, 1, ctx->num_sms, st)) != cudaSuccess)
+                    return cuda_fail(ctx, ce, "shared gate_up");
+                if ((ce = launch_down(p, L.dev, L.maps, 1, ctx->num_sms, st)) != cudaSuccess)
+                    return cuda_fail(ctx, ce, "shared down");
+                mk.mark("shared");
+            }
+        }
+        if ((ce = launch_combine(p, st)) != cudaSuccess) return cuda_fail(ctx, ce, "combine");
+        mk.mark("combine");
+    }
+    ctx->last_layer = layer;
+    ctx->last_T = T;
+    if (ptr_kind == MOE_PTR_HOST) {
+        if (T > 0) {
+            CUDA_TRY(ctx, cudaMemcpyAsync(out, s.out, (size_t)T * H * 4, cudaMemcpyDeviceToHost, st), "copy out");
+            if (sel_idx)
+                CUDA_TRY(ctx, cudaMemcpyAsync(sel_idx, s.sel_idx, (size_t)T * L.k * 4, cudaMemcpyDeviceToHost, st),
+                         "copy sel_idx");
+            if (sel_w)
+                CUDA_TRY(ctx, cudaMemcpyAsync(sel_w, s.sel_w, (size_t)T * L.k * 4, cudaMemcpyDeviceToHost, st),
+                         "copy sel_w");
+        }
+        CUDA_TRY(ctx, cudaMemcpyAsync(ctx->status_host, s.err, sizeof(int), cudaMemcpyDeviceToHost, st),
+                 "copy status");
+        CUDA_TRY(ctx, cudaStreamSynchronize(st), "forward");
+        if (*ctx->status_host) {
+            cudaMemsetAsync(s.err, 0, sizeof(int), st);
+            return fail(ctx, MOE_ERR_TIMEOUT, "a bounded device wait ran out in layer %d (status %d)", layer,
+                        *ctx->status_host);
+        }
+    }
+    return MOE_OK;
 }
 
 uint64_t moe_row_bytes(int32_t quant, int32_t cols) { return gguf_row_bytes(quant, cols); }

@@ -144,6 +144,12 @@ __device__ __forceinline__ int q8_isum(uint4 q0, uint4 q1, int4 a, int4 b)
 }
 
 // SiLU(g) * u with silu(g) = g / (1 + exp(-g)), each operation rounded (the oracle's form).
+// Row of y that holds the expert output of slot s.
+__device__ __forceinline__ size_t y_row(const FwdParams &p, size_t s)
+{
+    return p.y_rows ? (size_t)p.y_rows[s] : s;
+}
+
 __device__ __forceinline__ float swiglu(float g, float u)
 {
     return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);

@@ -313,7 +313,7 @@ __device__ __forceinline__ void publish_y(const FwdParams &p, const float (&o)[1
     if (l8 == 0) {
 #pragma unroll
         for (int t = 0; t < NT; t++)
-            if (t < nt) p.y[(slot0 + t) * p.H + row] = o[0][t];
+            if (t < nt) p.y[(size_t)y_row(p, slot0 + t) * p.H + row] = o[0][t];
     }
 }
 
@@ -545,7 +545,7 @@ __global__ void __launch_bounds__(256) down_f32_kernel(FwdParams p, LayerDev L, 
             for (int c = l8; c < K; c += 8) v = __fmaf_rn(dw[c], a[c], v);
 #pragma unroll
         for (int o = 4; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-        if (l8 == 0 && row < rows) p.y[slot * p.H + row] = v;
+        if (l8 == 0 && row < rows) p.y[(size_t)y_row(p, slot) * p.H + row] = v;
     }
 }
 

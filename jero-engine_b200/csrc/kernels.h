@@ -38,4 +38,13 @@ cudaError_t launch_combine(const FwdParams &p, cudaStream_t st);
 cudaError_t launch_prefill(const FwdParams &p, const LayerDev &L, const LayerMaps &maps, int num_sms,
                            const Marker &mk, cudaStream_t st);
 
+// Expert-parallel exchange (ep.cu): bytes of one packed token row, and the
+// pack / unpack / receive-plan kernels.
+size_t ep_row_bytes(int H);
+cudaError_t launch_ep_pack(const int8_t *xq, const float *xd, const float *xs, const int32_t *perm, int n_rows, int H,
+                           void *out, int num_sms, cudaStream_t st);
+cudaError_t launch_ep_unpack(const void *in, int n_rows, int H, int8_t *xq, float *xd, float *xs, int num_sms,
+                             cudaStream_t st);
+cudaError_t launch_ep_segments(const void *segs, int n_segs, int32_t *perm, int num_sms, cudaStream_t st);
+
 }  // namespace jmoe

@@ -93,6 +93,8 @@ struct FwdParams {
     float *af;                   // [slots][W] f32 SwiGLU output (F32 down matrices)
     int W;
     float *y;                    // [slots][H] expert outputs
+    const int32_t *y_rows;       // null: y row = slot; else y row of slot s = y_rows[s] (expert-parallel
+                                 // receive order, so rows go back to their source rank in its order)
     float *out;                  // [T][H]
     int *err;                    // device status word: 0 ok, 1 a bounded wait ran out
 

@@ -412,10 +412,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     }
                 } else {
                     tmem_ld_wait();
-                    float *dst = p.y + (size_t)(x.slot + 32 * cc) * p.H + f;
+                    const size_t s0 = (size_t)x.slot + 32 * cc;
 #pragma unroll
                     for (int i = 0; i < 32; i++)
-                        if (i < n_here) dst[(size_t)i * p.H] = __uint_as_float(g[i]);
+                        if (i < n_here) p.y[(size_t)y_row(p, s0 + i) * p.H + f] = __uint_as_float(g[i]);
                 }
             }
             tc_fence_before();

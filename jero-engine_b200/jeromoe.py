@@ -143,6 +143,12 @@ EXPORTS = {
     "moe_route_noalloc": (C.c_int, [C.c_int32, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int32,
                                     C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_float, C.c_int32, C.c_int32,
                                     C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]),
+    "moe_ep_unique_id": (C.c_int, [C.c_void_p]),
+    "moe_ep_init": (C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.c_void_p]),
+    "moe_forward_ep": (C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
+                                 C.c_int32]),
+    "moe_ep_plan": (C.c_int, [C.c_int32, C.c_int32, C.c_int32, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
+                              C.c_void_p, C.c_void_p, C.POINTER(C.c_int32), C.c_void_p, C.POINTER(C.c_int32)]),
     "moe_row_bytes": (C.c_uint64, [C.c_int32, C.c_int32]),
     "moe_quantize_rows": (C.c_int, [C.c_int32, C.c_void_p, C.c_int64, C.c_int32, C.c_void_p, C.c_int32]),
     "moe_gen_normal": (C.c_int, [C.c_uint64, C.c_uint64, C.c_uint64, C.c_float, C.c_void_p, C.c_int32]),
@@ -358,6 +364,30 @@ class Context:
         _check(lib.moe_forward(self.h, layer, T, C.c_void_p(x_ptr), C.c_void_p(out_ptr),
                                C.c_void_p(sel_idx_ptr or None), C.c_void_p(sel_w_ptr or None), ptr_kind), self.h)
 
+    # ---- expert parallelism (moe_ep_init / moe_forward_ep)
+
+    def ep_init(self, rank: int, world: int, uid: bytes):
+        """Joins an expert-parallel world (collective); call before any upload."""
+        buf = (C.c_uint8 * EP_ID_BYTES).from_buffer_copy(uid)
+        _check(lib.moe_ep_init(self.h, rank, world, buf), self.h)
+        self.ep = (rank, world)
+
+    def forward_ep(self, layer: int, x: np.ndarray, want_selection: bool = True):
+        """moe_forward_ep with host arrays; every rank of the world calls it (T may be 0)."""
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        T, H = x.shape
+        k = self.layers.get(layer, {"k": 1})["k"]
+        out = np.empty((T, H), dtype=np.float32)
+        si = np.empty((T, k), dtype=np.int32) if want_selection else None
+        sw = np.empty((T, k), dtype=np.float32) if want_selection else None
+        _check(lib.moe_forward_ep(self.h, layer, T, _ptr(x) if T else None, _ptr(out) if T else None,
+                                  _ptr(si) if T else None, _ptr(sw) if T else None, PTR_HOST), self.h)
+        return out, si, sw
+
+    def forward_ep_ptrs(self, layer: int, T: int, x_ptr: int, out_ptr: int, ptr_kind: int = PTR_DEVICE):
+        _check(lib.moe_forward_ep(self.h, layer, T, C.c_void_p(x_ptr or None), C.c_void_p(out_ptr or None), None,
+                                  None, ptr_kind), self.h)
+
     def device_status(self) -> int:
         st = C.c_int32()
         _check(lib.moe_device_status(self.h, C.byref(st)), self.h)
@@ -385,6 +415,39 @@ class Context:
         perm = np.empty(self.max_tokens * k, dtype=np.int32)
         _check(lib.moe_debug_permutation(self.h, _ptr(offs), _ptr(perm), C.byref(T)), self.h)
         return offs, perm[: T.value * k]
+
+
+EP_ID_BYTES = 128
+
+
+def ep_unique_id() -> bytes:
+    """NCCL unique id bytes for moe_ep_init (made on one rank, shared out of band)."""
+    buf = (C.c_uint8 * EP_ID_BYTES)()
+    _check(lib.moe_ep_unique_id(buf))
+    return bytes(buf)
+
+
+@dataclass
+class EpPlan:
+    send_cnt: np.ndarray
+    send_off: np.ndarray
+    recv_cnt: np.ndarray
+    recv_off: np.ndarray
+    problems: np.ndarray   # [n, 3] (local expert, first slot, slots)
+    segments: np.ndarray   # [n, 3] (first slot, first received row, rows)
+
+
+def ep_plan(rank: int, world: int, E: int, all_offsets: np.ndarray) -> EpPlan:
+    """The exchange plan moe_forward_ep derives from all ranks' slot offsets [world, E+1] (host only)."""
+    offs = np.ascontiguousarray(all_offsets, dtype=np.int32).reshape(world, E + 1)
+    v = [np.empty(world, dtype=np.int32) for _ in range(4)]
+    El = max(1, E // max(world, 1))
+    probs = np.empty((El, 3), dtype=np.int32)
+    segs = np.empty((world * El, 3), dtype=np.int32)
+    npb, nsg = C.c_int32(), C.c_int32()
+    _check(lib.moe_ep_plan(rank, world, E, _ptr(offs), _ptr(v[0]), _ptr(v[1]), _ptr(v[2]), _ptr(v[3]), _ptr(probs),
+                           C.byref(npb), _ptr(segs), C.byref(nsg)))
+    return EpPlan(v[0], v[1], v[2], v[3], probs[: npb.value].copy(), segs[: nsg.value].copy())
 
 
 def admission_check(device: int, max_tokens: int, descs: Sequence[moe_layer_desc],
