@@ -78,7 +78,7 @@ struct RingPos {
     }
 };
 
-// 2-D TMA tile load (no multicast) of the box at (x, y) of map into shared
+// 2-D TMA tile load (this CTA only) of the box at (x, y) of map into shared
 // memory, completing on bar. x in elements of the map; x * element size must
 // be a multiple of 16 bytes.
 __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar)
