@@ -576,6 +576,18 @@ int ep_reserve(moe_ctx *ctx, EpDims d)
     return MOE_OK;
 }
 
+// Profiling names of the replicated shared-expert pass of an expert-parallel
+// forward, so its launches are not folded into the routed expert stage's.
+void shared_mark_cb(void *user, const char *kernel)
+{
+    const Marker *inner = static_cast<const Marker *>(user);
+    const char *name = kernel;
+    if (kernel && !strcmp(kernel, "prefill_prep")) name = "shared_prefill_prep";
+    else if (kernel && !strcmp(kernel, "gate_up_tc")) name = "shared_gate_up_tc";
+    else if (kernel && !strcmp(kernel, "down_tc")) name = "shared_down_tc";
+    inner->mark(name);
+}
+
 int nccl_fail(moe_ctx *ctx, const NcclApi *nc, ncclResult_t r, const char *what)
 {
     return fail(ctx, MOE_ERR_NCCL, "%s: %s", what, nc ? nc->GetErrorString(r) : "NCCL unavailable");
@@ -1260,7 +1272,8 @@ int moe_forward_ep(moe_ctx *ctx, int32_t layer, int32_t T, const float *x, float
             if (p.use_tc) {
                 FwdParams ps = p;
                 ps.n_active = ep.zero;   // no routed problems in this pass
-                if ((ce = launch_prefill(ps, L.dev, L.maps, ctx->num_sms, mk, st)) != cudaSuccess)
+                const Marker smk{mk.fn ? &shared_mark_cb : nullptr, const_cast<Marker *>(&mk)};
+                if ((ce = launch_prefill(ps, L.dev, L.maps, ctx->num_sms, smk, st)) != cudaSuccess)
                     return cuda_fail(ctx, ce, "shared expert (tensor cores)");
             } else {
                 if ((ce = launch_gate_up(p, L.dev, L.maps, 1, ctx->num_sms, st)) != cudaSuccess)
