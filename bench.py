@@ -85,10 +85,11 @@ def tensor_peak():
 
 
 def kernel_flops(cfg, T, routed_rows=None):
-    """Algorithmic FLOPs of the tensor-core expert GEMMs (no padding counted);
-    routed_rows: the rows this rank's experts received (expert parallel)."""
+    """Algorithmic FLOPs of the tensor-core expert GEMMs (no padding counted).
+    Expert parallel (routed_rows = rows this rank's experts received): the
+    launches time the routed experts only; the shared expert is its own pass."""
     routed = 2 * (T * cfg.k if routed_rows is None else routed_rows) * cfg.H * cfg.I
-    shared = 2 * T * cfg.H * cfg.S
+    shared = 2 * T * cfg.H * cfg.S if routed_rows is None else 0
     return {"gate_up_tc": 2 * routed + 2 * shared, "down_tc": routed + shared}
 
 
@@ -170,8 +171,12 @@ def kernel_bytes(cfg, weights, sel_idx, T, expert_range=None, routed_rows=None):
     sh = {m: (weights.tensor(f"blk.0.ffn_{m}_shexp.weight").data.nbytes if cfg.S else 0)
           for m in ("gate", "up", "down")}
     W = max(cfg.I, cfg.S)
-    gate_up = U * (per["gate"] + per["up"]) + sh["gate"] + sh["up"] + T * cfg.H * 1.25 + slots * W * 1.25
-    down = U * per["down"] + sh["down"] + slots * W * 1.25 + slots * cfg.H * 4
+    if expert_range is None:
+        gate_up = U * (per["gate"] + per["up"]) + sh["gate"] + sh["up"] + T * cfg.H * 1.25 + slots * W * 1.25
+        down = U * per["down"] + sh["down"] + slots * W * 1.25 + slots * cfg.H * 4
+    else:   # the routed expert stage over the received rows (the shared expert is its own pass)
+        gate_up = U * (per["gate"] + per["up"]) + routed * cfg.H * 1.25 + routed * cfg.I * 1.25
+        down = U * per["down"] + routed * cfg.I * 1.25 + routed * cfg.H * 4
     layer = (U * sum(per.values()) + sum(sh.values()) + cfg.E * cfg.H * 4 + 2 * T * cfg.H * 4 + T * cfg.k * 8)
     if expert_range is not None:   # activation rows out and expert outputs back through the exchange
         layer += routed * cfg.H * 1.25 + routed * cfg.H * 4
