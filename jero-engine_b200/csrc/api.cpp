@@ -50,6 +50,7 @@ struct Scratch {
     int8_t *xq = nullptr;
     float *xd = nullptr, *xs = nullptr, *logits = nullptr, *sel_w = nullptr;
     int32_t *sel_idx = nullptr;
+    int *sync = nullptr;
     uint32_t *mask = nullptr;
     int32_t *wprefix = nullptr, *offsets = nullptr, *perm_token = nullptr, *n_active = nullptr;
     Problem *problems = nullptr;
@@ -352,7 +353,9 @@ size_t carve_scratch(const ScratchDims &d, uint8_t *base, Scratch *s)
     t.logits = (float *)take(Tm * E * 4);
     t.sel_idx = (int32_t *)take(Tm * k * 4);
     t.sel_w = (float *)take(Tm * k * 4);
-    t.mask = (uint32_t *)take(E * mw * 4);
+    uint8_t *sync_mask = take(16 + E * mw * 4);   // selection ticket, then the masks (one memset)
+    t.sync = (int *)sync_mask;
+    t.mask = sync_mask ? (uint32_t *)(sync_mask + 16) : nullptr;
     t.wprefix = (int32_t *)take(E * mw * 4);
     t.offsets = (int32_t *)take((E + 1) * 4);
     t.perm_token = (int32_t *)take(slots * 4);
@@ -469,7 +472,7 @@ FwdParams local_params(moe_ctx *ctx, const LayerStore &L, int T, int ptr_kind, c
     p.xq = s.xq; p.xd = s.xd; p.xs = s.xs; p.logits = s.logits;
     p.sel_idx = (ptr_kind == MOE_PTR_DEVICE && sel_idx) ? sel_idx : s.sel_idx;
     p.sel_w = (ptr_kind == MOE_PTR_DEVICE && sel_w) ? sel_w : s.sel_w;
-    p.mask = s.mask; p.wprefix = s.wprefix; p.offsets = s.offsets; p.perm_token = s.perm_token;
+    p.sync = s.sync; p.mask = s.mask; p.wprefix = s.wprefix; p.offsets = s.offsets; p.perm_token = s.perm_token;
     p.problems = s.problems; p.n_active = s.n_active;
     p.aq = s.aq; p.ad = s.ad; p.as = s.as; p.af = s.af_buf; p.W = s.W; p.y = s.y;
     p.y_rows = nullptr;
@@ -1158,13 +1161,11 @@ int moe_forward_ep(moe_ctx *ctx, int32_t layer, int32_t T, const float *x, float
     if (T > 0) {
         if (ptr_kind == MOE_PTR_HOST)
             CUDA_TRY(ctx, cudaMemcpyAsync(s.x, x, (size_t)T * H * 4, cudaMemcpyHostToDevice, st), "copy x");
-        CUDA_TRY(ctx, cudaMemsetAsync(p.mask, 0, sizeof(uint32_t) * (size_t)E * p.mask_words, st), "memset");
+        if ((ce = clear_routing_state(p, st)) != cudaSuccess) return cuda_fail(ctx, ce, "memset");
         if ((ce = launch_router(p, st)) != cudaSuccess) return cuda_fail(ctx, ce, "router");
         mk.mark("router");
-        if ((ce = launch_topk(p, st)) != cudaSuccess) return cuda_fail(ctx, ce, "topk");
-        mk.mark("topk");
-        if ((ce = launch_scan(p, st)) != cudaSuccess) return cuda_fail(ctx, ce, "scan");
-        mk.mark("scan");
+        if ((ce = launch_select(p, st)) != cudaSuccess) return cuda_fail(ctx, ce, "select");
+        mk.mark("select");
     } else {
         CUDA_TRY(ctx, cudaMemsetAsync(s.offsets, 0, (size_t)(E + 1) * 4, st), "memset");
     }

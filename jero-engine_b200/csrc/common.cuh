@@ -13,6 +13,7 @@ namespace jmoe {
 constexpr int kTT = 8;         // tokens per expert-kernel tile
 constexpr int kMaxK = 16;      // largest top_k
 constexpr int kMaxLaneE = 8;   // experts per lane in topk (E <= 256)
+constexpr int kMaxRouteExperts = 32 * kMaxLaneE;
 
 // Rust f32::total_cmp order as a signed integer (src/gemma.rs:417).
 __device__ __forceinline__ int32_t total_key(float f)

@@ -23,8 +23,10 @@ struct StreamCfg {
 };
 
 cudaError_t launch_router(const FwdParams &p, cudaStream_t st);
-cudaError_t launch_topk(const FwdParams &p, cudaStream_t st);
-cudaError_t launch_scan(const FwdParams &p, cudaStream_t st);
+// Clears the expert masks and the selection ticket (one memset), then the
+// selection: top-k per token and the dispatch permutation (fused for T <= 256).
+cudaError_t clear_routing_state(const FwdParams &p, cudaStream_t st);
+cudaError_t launch_select(const FwdParams &p, cudaStream_t st);
 // Routed and shared matrices can share one streaming launch when their slice plans match.
 bool stream_plans_match(const DevMatrix &a, const DevMatrix &b);
 cudaError_t launch_gate_up(const FwdParams &p, const LayerDev &L, const LayerMaps &maps, int mode, int num_sms,

@@ -80,6 +80,7 @@ struct FwdParams {
     float *logits;               // [T][E]
     int32_t *sel_idx;            // [T][k]
     float *sel_w;                // [T][k]
+    int *sync;                   // selection ticket; the masks start 16 bytes after it (one memset clears both)
     uint32_t *mask;              // [E][mask_words]: bit t of expert e = token t chose e
     int32_t *wprefix;            // [E][mask_words]: set bits of expert e before word w
     int32_t *offsets;            // [E+1]

@@ -77,7 +77,7 @@ extern "C" int moe_route_noalloc(int32_t device, const float *x, const float *ro
     const int max_problems = (E < T * top_k ? E : T * top_k);
     size_t off = 0;
     const size_t o_logits = off;   off += align256((size_t)T * E * 4);
-    const size_t o_mask = off;     off += align256((size_t)E * mw * 4);
+    const size_t o_mask = off;     off += align256(16 + (size_t)E * mw * 4);   // selection ticket + masks
     const size_t o_wprefix = off;  off += align256((size_t)E * mw * 4);
     const size_t o_problems = off; off += align256((size_t)(max_problems + 1) * sizeof(Problem));
     const size_t o_nactive = off;  off += 256;
@@ -110,17 +110,16 @@ extern "C" int moe_route_noalloc(int32_t device, const float *x, const float *ro
     p.max_problems = max_problems;
     p.x = x; p.router = router; p.logit_bias = logit_bias; p.sel_bias = sel_bias;
     p.logits = reinterpret_cast<float *>(base + o_logits);
-    p.mask = reinterpret_cast<uint32_t *>(base + o_mask);
+    p.sync = reinterpret_cast<int *>(base + o_mask);
+    p.mask = reinterpret_cast<uint32_t *>(base + o_mask + 16);
     p.wprefix = reinterpret_cast<int32_t *>(base + o_wprefix);
     p.problems = reinterpret_cast<Problem *>(base + o_problems);
     p.n_active = reinterpret_cast<int32_t *>(base + o_nactive);
     p.sel_idx = sel_idx; p.sel_w = sel_w; p.offsets = offsets; p.perm_token = perm_token;
 
-    // the array keeps the previous call's contents: the expert masks must start at zero
-    if ((e = cudaMemsetAsync(p.mask, 0, (size_t)E * mw * 4, st)) != cudaSuccess)
-        return fail(MOE_ERR_CUDA, cudaGetErrorString(e));
-    if ((e = launch_router(p, st)) != cudaSuccess || (e = launch_topk(p, st)) != cudaSuccess ||
-        (e = launch_scan(p, st)) != cudaSuccess)
+    // the array keeps the previous call's contents: masks and ticket must start at zero
+    if ((e = clear_routing_state(p, st)) != cudaSuccess) return fail(MOE_ERR_CUDA, cudaGetErrorString(e));
+    if ((e = launch_router(p, st)) != cudaSuccess || (e = launch_select(p, st)) != cudaSuccess)
         return fail(MOE_ERR_CUDA, cudaGetErrorString(e));
     return MOE_OK;
 }

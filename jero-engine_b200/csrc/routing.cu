@@ -133,22 +133,90 @@ __global__ void __launch_bounds__(128) router_kernel(FwdParams p)
     }
 }
 
-// One warp per token: softmax over all E logits, (group-limited) top-k on the
-// total_cmp key with ties to the lower index, the weights, and the token's bit
-// in each chosen expert's mask. Semantics of select_top_k_experts and
-// select_experts_with_optional_bias (src/gemma.rs:362-442,
-// src/qwen_deepseek.rs:773-831); selection list and weights stay in registers.
-__global__ void __launch_bounds__(128) topk_kernel(FwdParams p)
+// Small batches (T <= 256): the same canonical order, with the token tile
+// staged in shared memory and each warp's router row held in registers 2048
+// values at a time, so a warp waits for one DRAM round trip per 2048 values
+// instead of one per 256.
+template <int TT>
+__global__ void __launch_bounds__(128) router_small_kernel(FwdParams p)
 {
+    extern __shared__ float4 xs4[];   // [TT][H/4]
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int t = blockIdx.x * 4 + warp;
-    if (t >= p.T) return;
-    const int E = p.E;
-    float lg[kMaxLaneE];
-    int32_t key[kMaxLaneE];
-    bool cand[kMaxLaneE];
+    const int e = blockIdx.x * 4 + warp;
+    const int t0 = blockIdx.y * TT;
+    const int H = p.H, E = p.E, n4 = H >> 2;
+    const int ntok = min(TT, p.T - t0);
+    const float4 zero4 = make_float4(0.f, 0.f, 0.f, 0.f);
+    const float4 *wr = reinterpret_cast<const float4 *>(p.router + (size_t)min(e, E - 1) * H);
+
+    // issue the first row chunk before staging the tile, so both loads overlap
+    float4 w[16];
 #pragma unroll
-    for (int i = 0; i < kMaxLaneE; i++) {
+    for (int i = 0; i < 16; i++) {
+        const int h4 = lane + 32 * i;
+        w[i] = h4 < n4 ? __ldg(wr + h4) : zero4;
+    }
+    for (int i = threadIdx.x; i < TT * n4; i += blockDim.x) {
+        const int t = i / n4, c = i - t * n4;
+        xs4[i] = t < ntok ? __ldg(reinterpret_cast<const float4 *>(p.x + (size_t)(t0 + t) * H) + c) : zero4;
+    }
+    __syncthreads();
+
+    float acc[TT];
+#pragma unroll
+    for (int t = 0; t < TT; t++) acc[t] = 0.0f;
+    for (int base = 0; base < n4; base += 512) {
+        if (base > 0) {
+#pragma unroll
+            for (int i = 0; i < 16; i++) {
+                const int h4 = base + lane + 32 * i;
+                w[i] = h4 < n4 ? __ldg(wr + h4) : zero4;
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < 16; i++) {
+            const int h4 = base + lane + 32 * i;
+            if (h4 < n4) {
+#pragma unroll
+                for (int t = 0; t < TT; t++) {
+                    const float4 xv = xs4[t * n4 + h4];
+                    acc[t] = __fmaf_rn(w[i].x, xv.x, acc[t]);
+                    acc[t] = __fmaf_rn(w[i].y, xv.y, acc[t]);
+                    acc[t] = __fmaf_rn(w[i].z, xv.z, acc[t]);
+                    acc[t] = __fmaf_rn(w[i].w, xv.w, acc[t]);
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (int t = 0; t < TT; t++) {
+        float v = acc[t];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
+        if (lane == 0 && t < ntok && e < E) {
+            if (p.logit_bias) v = __fadd_rn(v, p.logit_bias[e]);
+            p.logits[(size_t)(t0 + t) * E + e] = v;
+        }
+    }
+    if (p.quant_x) quantize_tile(p, t0, ntok, blockIdx.x * 4 + warp, gridDim.x * 4, lane);
+}
+
+// Selection of token t by one warp: softmax over all E logits, (group-limited)
+// top-k on the total_cmp key with ties to the lower index, the weights, and
+// the token's bit in each chosen expert's mask. Semantics of
+// select_top_k_experts and select_experts_with_optional_bias
+// (src/gemma.rs:362-442, src/qwen_deepseek.rs:773-831). Each candidate's rank
+// is the number of candidates ranking before it (one pass of shuffles, no
+// sequential rounds); rank r < k is the r-th choice.
+template <int NL>   // experts per lane: E <= 32 * NL
+__device__ __forceinline__ void select_token(const FwdParams &p, int t, int lane)
+{
+    const int E = p.E;
+    float lg[NL];
+    int32_t key[NL];
+    bool cand[NL];
+#pragma unroll
+    for (int i = 0; i < NL; i++) {
         const int e = lane + 32 * i;
         const bool valid = e < E;
         lg[i] = valid ? p.logits[(size_t)t * E + e] : 0.0f;
@@ -160,13 +228,13 @@ __global__ void __launch_bounds__(128) topk_kernel(FwdParams p)
     // softmax of the logits (logit_bias already added) over all E
     float mx = -INFINITY;
 #pragma unroll
-    for (int i = 0; i < kMaxLaneE; i++)
+    for (int i = 0; i < NL; i++)
         if (lane + 32 * i < E && isfinite(lg[i])) mx = fmaxf(mx, lg[i]);
     mx = warp_max(mx);
-    float pv[kMaxLaneE];
+    float pv[NL];
     float psum = 0.0f;
 #pragma unroll
-    for (int i = 0; i < kMaxLaneE; i++) {
+    for (int i = 0; i < NL; i++) {
         const bool ok = lane + 32 * i < E && isfinite(lg[i]) && isfinite(mx);
         pv[i] = ok ? expf(__fsub_rn(lg[i], mx)) : 0.0f;
         psum = __fadd_rn(psum, pv[i]);
@@ -181,7 +249,7 @@ __global__ void __launch_bounds__(128) topk_kernel(FwdParams p)
         for (int g = 0; g < G; g++) {
             int32_t local = INT32_MIN;
 #pragma unroll
-            for (int i = 0; i < kMaxLaneE; i++) {
+            for (int i = 0; i < NL; i++) {
                 const int e = lane + 32 * i;
                 if (e < E && e / gs == g) local = max(local, key[i]);
             }
@@ -189,54 +257,58 @@ __global__ void __launch_bounds__(128) topk_kernel(FwdParams p)
             for (int o = 16; o > 0; o >>= 1) local = max(local, __shfl_xor_sync(0xffffffffu, local, o));
             if (lane == g) mykey = local;
         }
-        uint32_t gmask = 0;
-        for (int r = 0; r < p.topk_groups; r++) {
-            const bool live = lane < G && !((gmask >> lane) & 1u);
-            int32_t bk = live ? mykey : INT32_MIN;
-            int bi = live ? lane : 0x7fffffff;
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) {
-                const int32_t ok = __shfl_xor_sync(0xffffffffu, bk, o);
-                const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-                if (oi != 0x7fffffff && (bi == 0x7fffffff || rank_before(ok, oi, bk, bi))) { bk = ok; bi = oi; }
-            }
-            gmask |= 1u << bi;
+        // group g (lane g) is kept when fewer than topk_groups groups rank before it
+        int grank = 0;
+        for (int src = 0; src < G; src++) {
+            const int32_t ok = __shfl_sync(0xffffffffu, mykey, src);
+            if (lane < G && rank_before(ok, src, mykey, lane)) grank++;
         }
+        const uint32_t gmask = __ballot_sync(0xffffffffu, lane < G && grank < p.topk_groups);
 #pragma unroll
-        for (int i = 0; i < kMaxLaneE; i++) {
+        for (int i = 0; i < NL; i++) {
             const int e = lane + 32 * i;
             cand[i] = cand[i] && ((gmask >> (e / gs)) & 1u);
         }
         k = min(k, p.topk_groups * gs);
     }
 
-    // The rank list lives one entry per lane: lane r holds the r-th choice.
+    // rank of each candidate among the candidates
+    int32_t ckey[NL];
+    int rank[NL];
+#pragma unroll
+    for (int i = 0; i < NL; i++) {
+        ckey[i] = cand[i] ? key[i] : INT32_MIN;   // below every candidate's key
+        rank[i] = 0;
+    }
+    const int nlane = (E + 31) >> 5;
+#pragma unroll
+    for (int j = 0; j < NL; j++) {
+        if (j >= nlane) break;
+#pragma unroll 4
+        for (int src = 0; src < 32; src++) {
+            const int32_t ok = __shfl_sync(0xffffffffu, ckey[j], src);
+            const int oe = src + 32 * j;
+#pragma unroll
+            for (int i = 0; i < NL; i++)
+                if (rank_before(ok, oe, ckey[i], lane + 32 * i)) rank[i]++;
+        }
+    }
+
+    // lane r collects the r-th choice
     int my_e = -1;
     float my_w = 0.0f;
     int nsel = 0;
-#pragma unroll 1
     for (int r = 0; r < k; r++) {
-        int32_t bk = INT32_MIN;
-        int bi = 0x7fffffff;
-        float bp = 0.0f;
+        int has = -1;
+        float hp = 0.0f;
 #pragma unroll
-        for (int i = 0; i < kMaxLaneE; i++) {
-            const int e = lane + 32 * i;
-            if (cand[i] && (bi == 0x7fffffff || rank_before(key[i], e, bk, bi))) { bk = key[i]; bi = e; bp = pv[i]; }
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            const int32_t ok = __shfl_xor_sync(0xffffffffu, bk, o);
-            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-            const float op = __shfl_xor_sync(0xffffffffu, bp, o);
-            if (oi != 0x7fffffff && (bi == 0x7fffffff || rank_before(ok, oi, bk, bi))) { bk = ok; bi = oi; bp = op; }
-        }
-        if (bi == 0x7fffffff) break;
-        if ((bi & 31) == lane) {
-#pragma unroll
-            for (int i = 0; i < kMaxLaneE; i++)
-                if (i == (bi >> 5)) cand[i] = false;
-        }
+        for (int i = 0; i < NL; i++)
+            if (cand[i] && rank[i] == r) { has = lane + 32 * i; hp = pv[i]; }
+        const uint32_t b = __ballot_sync(0xffffffffu, has >= 0);
+        if (!b) break;
+        const int src = __ffs(b) - 1;
+        const int bi = __shfl_sync(0xffffffffu, has, src);
+        const float bp = __shfl_sync(0xffffffffu, hp, src);
         if (lane == r) {
             my_e = bi;
             if (p.sel_bias) my_w = sum_ok ? __fdiv_rn(bp, psum) : 0.0f;
@@ -260,14 +332,12 @@ __global__ void __launch_bounds__(128) topk_kernel(FwdParams p)
     }
 }
 
-// Single CTA: per-expert token counts from the bit masks, slot offsets
-// (experts ascending), the list of experts that received tokens, and the
-// slot -> token permutation (tokens ascending inside an expert).
-__global__ void __launch_bounds__(1024) scan_kernel(FwdParams p)
+// The dispatch permutation from the expert masks, by nthreads threads of one
+// CTA: per-expert token counts, slot offsets (experts ascending), the list of
+// experts that received tokens, and slot -> token (tokens ascending inside an
+// expert). s_count [E], s_off [E+1] in shared memory.
+__device__ void build_permutation(const FwdParams &p, int *s_count, int *s_off)
 {
-    extern __shared__ int s_scan[];
-    int *s_count = s_scan;       // [E]
-    int *s_off = s_scan + p.E;   // [E+1]
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
     const int E = p.E, mw = p.mask_words;
 
@@ -363,6 +433,38 @@ __global__ void __launch_bounds__(1024) scan_kernel(FwdParams p)
         for (int i = threadIdx.x; i < p.T; i += blockDim.x) p.perm_token[(size_t)p.T * p.k + i] = i;
 }
 
+constexpr int kFusedScanMaxT = 256;
+
+// One warp per token. With FUSE_SCAN (1024-thread CTAs) the last CTA to
+// finish (a fence and a ticket on p.sync, which the forward clears with the
+// masks) also builds the dispatch permutation with all of its 32 warps, so
+// small batches need no separate scan launch.
+template <bool FUSE_SCAN, int NL>
+__global__ void __launch_bounds__(FUSE_SCAN ? 1024 : 128, 1) select_kernel(FwdParams p)
+{
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int t = blockIdx.x * (blockDim.x >> 5) + warp;
+    if (t < p.T) select_token<NL>(p, t, lane);
+    if (!FUSE_SCAN) return;
+    __shared__ int s_scan[2 * kMaxRouteExperts + 1];
+    __shared__ int s_last;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        s_last = atomicAdd(p.sync, 1) == (int)gridDim.x - 1;
+    }
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    build_permutation(p, s_scan, s_scan + p.E);
+}
+
+__global__ void __launch_bounds__(1024) scan_kernel(FwdParams p)
+{
+    extern __shared__ int s_scan[];
+    build_permutation(p, s_scan, s_scan + p.E);
+}
+
 // ------------------------------------------------------------ parity probes
 
 __global__ void quantize_rows_kernel(const float *x, int n, int cols, int8_t *xq, float *xd, float *xs)
@@ -398,7 +500,17 @@ __global__ void block_dots_kernel(DevMatrix m, const int8_t *xq, int n, int32_t 
 
 cudaError_t launch_router(const FwdParams &p, cudaStream_t st)
 {
-    if (p.T <= 256) {
+    if (p.T <= 256 && (p.H & 3) == 0 && p.H <= 12288) {   // token tile fits in shared memory
+        constexpr int TT = 4;
+        const size_t smem = (size_t)TT * p.H * 4;
+        if (smem > 48 * 1024) {
+            cudaError_t e = cudaFuncSetAttribute(router_small_kernel<TT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 (int)smem);
+            if (e != cudaSuccess) return e;
+        }
+        dim3 grid((p.E + 3) / 4, (p.T + TT - 1) / TT);
+        router_small_kernel<TT><<<grid, 128, smem, st>>>(p);
+    } else if (p.T <= 256) {
         dim3 grid((p.E + 3) / 4, (p.T + 3) / 4);
         router_kernel<4, 1><<<grid, 128, 0, st>>>(p);
     } else {
@@ -408,14 +520,25 @@ cudaError_t launch_router(const FwdParams &p, cudaStream_t st)
     return cudaGetLastError();
 }
 
-cudaError_t launch_topk(const FwdParams &p, cudaStream_t st)
+cudaError_t clear_routing_state(const FwdParams &p, cudaStream_t st)
 {
-    topk_kernel<<<(p.T + 3) / 4, 128, 0, st>>>(p);
-    return cudaGetLastError();
+    // the selection ticket (16 bytes) and the expert masks are one region
+    return cudaMemsetAsync(p.sync, 0, 16 + sizeof(uint32_t) * (size_t)p.E * p.mask_words, st);
 }
 
-cudaError_t launch_scan(const FwdParams &p, cudaStream_t st)
+cudaError_t launch_select(const FwdParams &p, cudaStream_t st)
 {
+    if (p.E > kMaxRouteExperts) return cudaErrorInvalidValue;
+    const bool small_e = p.E <= 128;
+    if (p.T <= kFusedScanMaxT) {
+        if (small_e) select_kernel<true, 4><<<(p.T + 31) / 32, 1024, 0, st>>>(p);
+        else select_kernel<true, 8><<<(p.T + 31) / 32, 1024, 0, st>>>(p);
+        return cudaGetLastError();
+    }
+    if (small_e) select_kernel<false, 4><<<(p.T + 3) / 4, 128, 0, st>>>(p);
+    else select_kernel<false, 8><<<(p.T + 3) / 4, 128, 0, st>>>(p);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
     scan_kernel<<<1, 1024, sizeof(int) * (2 * (size_t)p.E + 1), st>>>(p);
     return cudaGetLastError();
 }
