@@ -52,7 +52,7 @@ struct Scratch {
     int32_t *sel_idx = nullptr;
     int *sync = nullptr;
     uint32_t *mask = nullptr;
-    int32_t *wprefix = nullptr, *offsets = nullptr, *perm_token = nullptr, *n_active = nullptr;
+    int32_t *wprefix = nullptr, *offsets = nullptr, *perm_token = nullptr, *n_active = nullptr, *slot_of = nullptr;
     Problem *problems = nullptr;
     int8_t *aq = nullptr;
     float *ad = nullptr, *as = nullptr, *af_buf = nullptr, *y = nullptr;
@@ -353,12 +353,13 @@ size_t carve_scratch(const ScratchDims &d, uint8_t *base, Scratch *s)
     t.logits = (float *)take(Tm * E * 4);
     t.sel_idx = (int32_t *)take(Tm * k * 4);
     t.sel_w = (float *)take(Tm * k * 4);
-    uint8_t *sync_mask = take(16 + E * mw * 4);   // selection ticket, then the masks (one memset)
+    uint8_t *sync_mask = take(kRoutingTicketBytes + E * mw * 4);   // routing tickets, then the masks (one memset)
     t.sync = (int *)sync_mask;
-    t.mask = sync_mask ? (uint32_t *)(sync_mask + 16) : nullptr;
+    t.mask = sync_mask ? (uint32_t *)(sync_mask + kRoutingTicketBytes) : nullptr;
     t.wprefix = (int32_t *)take(E * mw * 4);
     t.offsets = (int32_t *)take((E + 1) * 4);
     t.perm_token = (int32_t *)take(slots * 4);
+    t.slot_of = (int32_t *)take(Tm * k * 4);
     t.problems = (Problem *)take(maxp * sizeof(Problem));
     t.n_active = (int32_t *)take(4);
     t.aq = (int8_t *)take(slots * W);
@@ -473,6 +474,7 @@ FwdParams local_params(moe_ctx *ctx, const LayerStore &L, int T, int ptr_kind, c
     p.sel_idx = (ptr_kind == MOE_PTR_DEVICE && sel_idx) ? sel_idx : s.sel_idx;
     p.sel_w = (ptr_kind == MOE_PTR_DEVICE && sel_w) ? sel_w : s.sel_w;
     p.sync = s.sync; p.mask = s.mask; p.wprefix = s.wprefix; p.offsets = s.offsets; p.perm_token = s.perm_token;
+    p.slot_of = s.slot_of;
     p.problems = s.problems; p.n_active = s.n_active;
     p.aq = s.aq; p.ad = s.ad; p.as = s.as; p.af = s.af_buf; p.W = s.W; p.y = s.y;
     p.y_rows = nullptr;
@@ -797,6 +799,7 @@ int moe_layer_upload(moe_ctx *ctx, int32_t layer, const moe_layer_desc *desc)
         ctx->scratch.block = blk;
         carve_scratch(sd, static_cast<uint8_t *>(blk), &ctx->scratch);
         CUDA_TRY(ctx, cudaMemset(ctx->scratch.err, 0, sizeof(int)), "cudaMemset(status)");
+        CUDA_TRY(ctx, cudaMemset(ctx->scratch.sync, 0, kRoutingTicketBytes), "cudaMemset(routing tickets)");
     }
     LayerStore &L = ctx->layers[layer];
     void *blk = nullptr;
@@ -1161,11 +1164,7 @@ int moe_forward_ep(moe_ctx *ctx, int32_t layer, int32_t T, const float *x, float
     if (T > 0) {
         if (ptr_kind == MOE_PTR_HOST)
             CUDA_TRY(ctx, cudaMemcpyAsync(s.x, x, (size_t)T * H * 4, cudaMemcpyHostToDevice, st), "copy x");
-        if ((ce = clear_routing_state(p, st)) != cudaSuccess) return cuda_fail(ctx, ce, "memset");
-        if ((ce = launch_router(p, st)) != cudaSuccess) return cuda_fail(ctx, ce, "router");
-        mk.mark("router");
-        if ((ce = launch_select(p, st)) != cudaSuccess) return cuda_fail(ctx, ce, "select");
-        mk.mark("select");
+        if ((ce = launch_routing(p, st, mk)) != cudaSuccess) return cuda_fail(ctx, ce, "routing");
     } else {
         CUDA_TRY(ctx, cudaMemsetAsync(s.offsets, 0, (size_t)(E + 1) * 4, st), "memset");
     }

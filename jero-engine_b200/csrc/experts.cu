@@ -557,16 +557,10 @@ __global__ void __launch_bounds__(256) combine_kernel(FwdParams p)
 {
     __shared__ long long s_pos[kMaxK];
     __shared__ float s_w[kMaxK];
-    const int t = blockIdx.y, k = p.k, mw = p.mask_words;
+    const int t = blockIdx.y, k = p.k;
     if (threadIdx.x < k) {
         const int r = threadIdx.x;
-        const int e = p.sel_idx[(size_t)t * k + r];
-        long long pos = -1;
-        if (e >= 0) {
-            const uint32_t m = p.mask[(size_t)e * mw + (t >> 5)];
-            pos = p.offsets[e] + p.wprefix[(size_t)e * mw + (t >> 5)] + __popc(m & ((1u << (t & 31)) - 1u));
-        }
-        s_pos[r] = pos;
+        s_pos[r] = p.slot_of[(size_t)t * k + r];
         s_w[r] = p.sel_w[(size_t)t * k + r];
     }
     __syncthreads();

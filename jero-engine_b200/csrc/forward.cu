@@ -1,5 +1,5 @@
 // forward.cu -- the launch sequence of one batched MoE forward:
-// memset(mask) -> router -> select (top-k + permutation) -> gate_up -> down -> combine.
+// routing (router, top-k, permutation) -> gate_up -> down -> combine.
 // Each kernel reads its work from device-side counters written by the one
 // before it, so the sequence needs no host round trip.
 #include <cuda_runtime.h>
@@ -16,11 +16,7 @@ int launch_forward(const FwdParams &p, const LayerDev &L, const LayerMaps &maps,
     cudaError_t err;
     if (p.T == 0) return cudaSuccess;
     mk.mark(nullptr);
-    if ((err = clear_routing_state(p, st)) != cudaSuccess) return err;
-    if ((err = launch_router(p, st)) != cudaSuccess) return err;
-    mk.mark("router");
-    if ((err = launch_select(p, st)) != cudaSuccess) return err;
-    mk.mark("select");
+    if ((err = launch_routing(p, st, mk)) != cudaSuccess) return err;
 
     if (p.use_tc) {
         if ((err = launch_prefill(p, L, maps, num_sms, mk, st)) != cudaSuccess) return err;

@@ -22,11 +22,10 @@ struct StreamCfg {
     int max_q;         // capacity of the shared-memory problem table (routed + shared)
 };
 
-cudaError_t launch_router(const FwdParams &p, cudaStream_t st);
-// Clears the expert masks and the selection ticket (one memset), then the
-// selection: top-k per token and the dispatch permutation (fused for T <= 256).
-cudaError_t clear_routing_state(const FwdParams &p, cudaStream_t st);
-cudaError_t launch_select(const FwdParams &p, cudaStream_t st);
+// Router logits, top-k selection and the dispatch permutation. Small batches
+// (T <= 256) run it as one kernel; larger ones clear the expert masks, then
+// router, selection and scan kernels. Marks "routing" or "router"/"select".
+cudaError_t launch_routing(const FwdParams &p, cudaStream_t st, const Marker &mk);
 // Routed and shared matrices can share one streaming launch when their slice plans match.
 bool stream_plans_match(const DevMatrix &a, const DevMatrix &b);
 cudaError_t launch_gate_up(const FwdParams &p, const LayerDev &L, const LayerMaps &maps, int mode, int num_sms,

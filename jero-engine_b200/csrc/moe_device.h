@@ -48,6 +48,10 @@ struct LayerMaps {
     MatMaps gate_tc, up_tc, down_tc, sh_gate_tc, sh_up_tc, sh_down_tc;  // tensor-core path: 128-row boxes per 256 values
 };
 
+// Bytes of the routing tickets in front of the expert masks: [0] the last
+// token tile, [1 + j] the CTAs of token tile j (fused routing, T <= 256).
+constexpr int kRoutingTicketBytes = 1024;
+
 // Entries per launch layout in FwdParams::tile_off (problems + 2).
 constexpr int kTileOffStride = 260;
 
@@ -80,11 +84,12 @@ struct FwdParams {
     float *logits;               // [T][E]
     int32_t *sel_idx;            // [T][k]
     float *sel_w;                // [T][k]
-    int *sync;                   // selection ticket; the masks start 16 bytes after it (one memset clears both)
+    int *sync;                   // routing tickets [kRoutingTicketBytes / 4]; the masks follow (one memset clears both)
     uint32_t *mask;              // [E][mask_words]: bit t of expert e = token t chose e
     int32_t *wprefix;            // [E][mask_words]: set bits of expert e before word w
     int32_t *offsets;            // [E+1]
     int32_t *perm_token;         // [T*k + T]
+    int32_t *slot_of;            // [T][k] slot of each choice (-1: none), for the combine
     Problem *problems;           // [max_problems]
     int32_t *n_active;           // [1]
 

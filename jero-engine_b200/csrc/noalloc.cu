@@ -76,11 +76,14 @@ extern "C" int moe_route_noalloc(int32_t device, const float *x, const float *ro
     const int mw = (T + 31) / 32;
     const int max_problems = (E < T * top_k ? E : T * top_k);
     size_t off = 0;
+    // the selection ticket sits at a fixed place (offset 0): small batches leave
+    // it at zero when they finish, and the array starts zeroed
+    const size_t o_mask = off;     off += align256(kRoutingTicketBytes + (size_t)E * mw * 4);   // tickets + masks
     const size_t o_logits = off;   off += align256((size_t)T * E * 4);
-    const size_t o_mask = off;     off += align256(16 + (size_t)E * mw * 4);   // selection ticket + masks
     const size_t o_wprefix = off;  off += align256((size_t)E * mw * 4);
     const size_t o_problems = off; off += align256((size_t)(max_problems + 1) * sizeof(Problem));
     const size_t o_nactive = off;  off += 256;
+    const size_t o_slot_of = off;  off += align256((size_t)T * top_k * 4);
     if (off > kNoAllocScratchBytes) return fail(MOE_ERR_CONTEXT_LENGTH, "routing scratch for this shape exceeds 2 MiB");
 
     cudaError_t e = cudaSetDevice(device);
@@ -111,15 +114,14 @@ extern "C" int moe_route_noalloc(int32_t device, const float *x, const float *ro
     p.x = x; p.router = router; p.logit_bias = logit_bias; p.sel_bias = sel_bias;
     p.logits = reinterpret_cast<float *>(base + o_logits);
     p.sync = reinterpret_cast<int *>(base + o_mask);
-    p.mask = reinterpret_cast<uint32_t *>(base + o_mask + 16);
+    p.mask = reinterpret_cast<uint32_t *>(base + o_mask + kRoutingTicketBytes);
     p.wprefix = reinterpret_cast<int32_t *>(base + o_wprefix);
     p.problems = reinterpret_cast<Problem *>(base + o_problems);
     p.n_active = reinterpret_cast<int32_t *>(base + o_nactive);
+    p.slot_of = reinterpret_cast<int32_t *>(base + o_slot_of);
     p.sel_idx = sel_idx; p.sel_w = sel_w; p.offsets = offsets; p.perm_token = perm_token;
 
-    // the array keeps the previous call's contents: masks and ticket must start at zero
-    if ((e = clear_routing_state(p, st)) != cudaSuccess) return fail(MOE_ERR_CUDA, cudaGetErrorString(e));
-    if ((e = launch_router(p, st)) != cudaSuccess || (e = launch_select(p, st)) != cudaSuccess)
+    if ((e = launch_routing(p, st, Marker{nullptr, nullptr})) != cudaSuccess)
         return fail(MOE_ERR_CUDA, cudaGetErrorString(e));
     return MOE_OK;
 }

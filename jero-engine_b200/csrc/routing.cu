@@ -9,6 +9,11 @@
 namespace jmoe {
 namespace {
 
+// Batches up to this many tokens build the dispatch permutation inside the
+// selection kernel (shared-memory masks); larger ones use scan_kernel.
+constexpr int kFusedScanMaxT = 256;
+constexpr int kFusedMaskWords = kFusedScanMaxT / 32;
+
 // Quantises the activation blocks of tokens [t0, t0 + ntok): eight lanes per
 // 32-value block, four blocks per warp pass; tasks are spread over the warps
 // of all CTAs that share this token tile. Same arithmetic as quant_block32.
@@ -131,74 +136,6 @@ __global__ void __launch_bounds__(128) router_kernel(FwdParams p)
             }
         }
     }
-}
-
-// Small batches (T <= 256): the same canonical order, with the token tile
-// staged in shared memory and each warp's router row held in registers 2048
-// values at a time, so a warp waits for one DRAM round trip per 2048 values
-// instead of one per 256.
-template <int TT>
-__global__ void __launch_bounds__(128) router_small_kernel(FwdParams p)
-{
-    extern __shared__ float4 xs4[];   // [TT][H/4]
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int e = blockIdx.x * 4 + warp;
-    const int t0 = blockIdx.y * TT;
-    const int H = p.H, E = p.E, n4 = H >> 2;
-    const int ntok = min(TT, p.T - t0);
-    const float4 zero4 = make_float4(0.f, 0.f, 0.f, 0.f);
-    const float4 *wr = reinterpret_cast<const float4 *>(p.router + (size_t)min(e, E - 1) * H);
-
-    // issue the first row chunk before staging the tile, so both loads overlap
-    float4 w[16];
-#pragma unroll
-    for (int i = 0; i < 16; i++) {
-        const int h4 = lane + 32 * i;
-        w[i] = h4 < n4 ? __ldg(wr + h4) : zero4;
-    }
-    for (int i = threadIdx.x; i < TT * n4; i += blockDim.x) {
-        const int t = i / n4, c = i - t * n4;
-        xs4[i] = t < ntok ? __ldg(reinterpret_cast<const float4 *>(p.x + (size_t)(t0 + t) * H) + c) : zero4;
-    }
-    __syncthreads();
-
-    float acc[TT];
-#pragma unroll
-    for (int t = 0; t < TT; t++) acc[t] = 0.0f;
-    for (int base = 0; base < n4; base += 512) {
-        if (base > 0) {
-#pragma unroll
-            for (int i = 0; i < 16; i++) {
-                const int h4 = base + lane + 32 * i;
-                w[i] = h4 < n4 ? __ldg(wr + h4) : zero4;
-            }
-        }
-#pragma unroll
-        for (int i = 0; i < 16; i++) {
-            const int h4 = base + lane + 32 * i;
-            if (h4 < n4) {
-#pragma unroll
-                for (int t = 0; t < TT; t++) {
-                    const float4 xv = xs4[t * n4 + h4];
-                    acc[t] = __fmaf_rn(w[i].x, xv.x, acc[t]);
-                    acc[t] = __fmaf_rn(w[i].y, xv.y, acc[t]);
-                    acc[t] = __fmaf_rn(w[i].z, xv.z, acc[t]);
-                    acc[t] = __fmaf_rn(w[i].w, xv.w, acc[t]);
-                }
-            }
-        }
-    }
-#pragma unroll
-    for (int t = 0; t < TT; t++) {
-        float v = acc[t];
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
-        if (lane == 0 && t < ntok && e < E) {
-            if (p.logit_bias) v = __fadd_rn(v, p.logit_bias[e]);
-            p.logits[(size_t)(t0 + t) * E + e] = v;
-        }
-    }
-    if (p.quant_x) quantize_tile(p, t0, ntok, blockIdx.x * 4 + warp, gridDim.x * 4, lane);
 }
 
 // Selection of token t by one warp: softmax over all E logits, (group-limited)
@@ -328,7 +265,8 @@ __device__ __forceinline__ void select_token(const FwdParams &p, int t, int lane
     if (lane < p.k) {
         p.sel_idx[(size_t)t * p.k + lane] = my_e;
         p.sel_w[(size_t)t * p.k + lane] = my_e >= 0 ? my_w : 0.0f;
-        if (my_e >= 0) atomicOr(p.mask + (size_t)my_e * p.mask_words + (t >> 5), 1u << (t & 31));
+        if (my_e >= 0 && p.T > kFusedScanMaxT)   // small batches rebuild the masks in shared memory
+            atomicOr(p.mask + (size_t)my_e * p.mask_words + (t >> 5), 1u << (t & 31));
     }
 }
 
@@ -431,14 +369,197 @@ __device__ void build_permutation(const FwdParams &p, int *s_count, int *s_off)
     }
     if (p.S > 0)
         for (int i = threadIdx.x; i < p.T; i += blockDim.x) p.perm_token[(size_t)p.T * p.k + i] = i;
+    // slot of each (token, rank) choice, for the combine
+    for (int i = threadIdx.x; i < p.T * p.k; i += blockDim.x) {
+        const int t = i / p.k, e = p.sel_idx[i];
+        int slot = -1;
+        if (e >= 0) {
+            const uint32_t m = p.mask[(size_t)e * mw + (t >> 5)];
+            slot = s_off[e] + p.wprefix[(size_t)e * mw + (t >> 5)] + __popc(m & ((1u << (t & 31)) - 1u));
+        }
+        p.slot_of[i] = slot;
+    }
 }
 
-constexpr int kFusedScanMaxT = 256;
+// The same permutation for T <= 256 by the last CTA of the selection, in
+// shared memory: per-expert token bit masks (shared-memory atomics on the
+// selections), counts, slot offsets, problem list, slot -> token and the slot
+// of each choice. No global masks are read or written.
+__device__ void build_permutation_small(const FwdParams &p)
+{
+    __shared__ uint32_t s_mask[kMaxRouteExperts * kFusedMaskWords];
+    __shared__ int s_wpre[kMaxRouteExperts * kFusedMaskWords];
+    __shared__ int s_cnt[kMaxRouteExperts], s_off[kMaxRouteExperts + 1];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int E = p.E, T = p.T, k = p.k, mw = p.mask_words, n = T * k;
+    for (int i = threadIdx.x; i < E * mw; i += blockDim.x) s_mask[i] = 0u;
+    __syncthreads();
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const int e = p.sel_idx[i], t = i / k;
+        if (e >= 0) atomicOr(&s_mask[e * mw + (t >> 5)], 1u << (t & 31));
+    }
+    __syncthreads();
+    for (int e = threadIdx.x; e < E; e += blockDim.x) {
+        int run = 0;
+        for (int w = 0; w < mw; w++) {
+            s_wpre[e * mw + w] = run;
+            run += __popc(s_mask[e * mw + w]);
+        }
+        s_cnt[e] = run;
+    }
+    __syncthreads();
+    if (warp == 0) {
+        const int chunk = (E + 31) / 32, b = lane * chunk;
+        int local = 0;
+        for (int i = 0; i < chunk; i++)
+            if (b + i < E) local += s_cnt[b + i];
+        int incl = local;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int v = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += v;
+        }
+        int run = incl - local;
+        for (int i = 0; i < chunk; i++) {
+            if (b + i < E) {
+                s_off[b + i] = run;
+                p.offsets[b + i] = run;
+                run += s_cnt[b + i];
+            }
+        }
+        if (lane == 31) {
+            s_off[E] = incl;
+            p.offsets[E] = incl;
+        }
+    }
+    __syncthreads();
+    if (warp == 1 || (blockDim.x == 32 && warp == 0)) {
+        int nact = 0;
+        for (int c = 0; c < E; c += 32) {
+            const int e = c + lane;
+            const bool act = e < E && s_cnt[e] > 0;
+            const uint32_t bal = __ballot_sync(0xffffffffu, act);
+            const int pos = nact + __popc(bal & ((1u << lane) - 1u));
+            if (act) p.problems[pos] = Problem{e, s_off[e], s_cnt[e], 0};
+            nact += __popc(bal);
+        }
+        if (lane == 0) {
+            *p.n_active = nact;
+            if (p.S > 0) p.problems[p.max_problems - 1] = Problem{0, T * k, T, 1};
+        }
+    }
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const int e = p.sel_idx[i], t = i / k;
+        int slot = -1;
+        if (e >= 0) {
+            const int w = e * mw + (t >> 5);
+            slot = s_off[e] + s_wpre[w] + __popc(s_mask[w] & ((1u << (t & 31)) - 1u));
+            p.perm_token[slot] = t;
+        }
+        p.slot_of[i] = slot;
+    }
+    if (p.S > 0)
+        for (int i = threadIdx.x; i < T; i += blockDim.x) p.perm_token[(size_t)T * k + i] = i;
+    if (threadIdx.x == 0) *p.sync = 0;   // ticket ready for the next selection
+}
 
-// One warp per token. With FUSE_SCAN (1024-thread CTAs) the last CTA to
-// finish (a fence and a ticket on p.sync, which the forward clears with the
-// masks) also builds the dispatch permutation with all of its 32 warps, so
-// small batches need no separate scan launch.
+// Routing of a small batch (T <= 256) in one kernel. Logits in the canonical
+// order of router_kernel, with the token tile staged in shared memory and each
+// warp's router row held in registers 2048 values at a time (one DRAM round
+// trip per 2048 values). The last CTA of a token tile to finish (ticket
+// sync[1 + tile]) selects its TT tokens, one warp each; the last token tile
+// (ticket sync[0]) builds the dispatch permutation. Tickets return to zero.
+template <int TT, int NL>
+__global__ void __launch_bounds__(128) router_small_kernel(FwdParams p)
+{
+    static_assert(TT == 4, "one selecting warp per token of the tile");
+    extern __shared__ float4 xs4[];   // [TT][H/4]
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int e = blockIdx.x * 4 + warp;
+    const int t0 = blockIdx.y * TT;
+    const int H = p.H, E = p.E, n4 = H >> 2;
+    const int ntok = min(TT, p.T - t0);
+    const float4 zero4 = make_float4(0.f, 0.f, 0.f, 0.f);
+    const float4 *wr = reinterpret_cast<const float4 *>(p.router + (size_t)min(e, E - 1) * H);
+
+    // issue the first row chunk before staging the tile, so both loads overlap
+    float4 w[16];
+#pragma unroll
+    for (int i = 0; i < 16; i++) {
+        const int h4 = lane + 32 * i;
+        w[i] = h4 < n4 ? __ldg(wr + h4) : zero4;
+    }
+    for (int i = threadIdx.x; i < TT * n4; i += blockDim.x) {
+        const int t = i / n4, c = i - t * n4;
+        xs4[i] = t < ntok ? __ldg(reinterpret_cast<const float4 *>(p.x + (size_t)(t0 + t) * H) + c) : zero4;
+    }
+    __syncthreads();
+
+    float acc[TT];
+#pragma unroll
+    for (int t = 0; t < TT; t++) acc[t] = 0.0f;
+    for (int base = 0; base < n4; base += 512) {
+        if (base > 0) {
+#pragma unroll
+            for (int i = 0; i < 16; i++) {
+                const int h4 = base + lane + 32 * i;
+                w[i] = h4 < n4 ? __ldg(wr + h4) : zero4;
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < 16; i++) {
+            const int h4 = base + lane + 32 * i;
+            if (h4 < n4) {
+#pragma unroll
+                for (int t = 0; t < TT; t++) {
+                    const float4 xv = xs4[t * n4 + h4];
+                    acc[t] = __fmaf_rn(w[i].x, xv.x, acc[t]);
+                    acc[t] = __fmaf_rn(w[i].y, xv.y, acc[t]);
+                    acc[t] = __fmaf_rn(w[i].z, xv.z, acc[t]);
+                    acc[t] = __fmaf_rn(w[i].w, xv.w, acc[t]);
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (int t = 0; t < TT; t++) {
+        float v = acc[t];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
+        if (lane == 0 && t < ntok && e < E) {
+            if (p.logit_bias) v = __fadd_rn(v, p.logit_bias[e]);
+            p.logits[(size_t)(t0 + t) * E + e] = v;
+        }
+    }
+    if (p.quant_x) quantize_tile(p, t0, ntok, blockIdx.x * 4 + warp, gridDim.x * 4, lane);
+
+    __shared__ int s_flag;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        s_flag = atomicAdd(&p.sync[1 + blockIdx.y], 1) == (int)gridDim.x - 1;
+    }
+    __syncthreads();
+    if (!s_flag) return;
+    __threadfence();   // the tile's logits from every CTA are visible
+    if (t0 + warp < p.T) select_token<NL>(p, t0 + warp, lane);
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        p.sync[1 + blockIdx.y] = 0;
+        __threadfence();
+        s_flag = atomicAdd(&p.sync[0], 1) == (int)gridDim.y - 1;
+    }
+    __syncthreads();
+    if (!s_flag) return;
+    __threadfence();
+    build_permutation_small(p);
+}
+
+// One warp per token. With FUSE_SCAN (1024-thread CTAs, T <= 256) the last
+// CTA to finish (a fence and a ticket on p.sync) also builds the dispatch
+// permutation, so small batches need no separate scan launch; that CTA sets
+// the ticket back to zero. Without it the selections go to the global masks
+// for scan_kernel.
 template <bool FUSE_SCAN, int NL>
 __global__ void __launch_bounds__(FUSE_SCAN ? 1024 : 128, 1) select_kernel(FwdParams p)
 {
@@ -446,7 +567,6 @@ __global__ void __launch_bounds__(FUSE_SCAN ? 1024 : 128, 1) select_kernel(FwdPa
     const int t = blockIdx.x * (blockDim.x >> 5) + warp;
     if (t < p.T) select_token<NL>(p, t, lane);
     if (!FUSE_SCAN) return;
-    __shared__ int s_scan[2 * kMaxRouteExperts + 1];
     __shared__ int s_last;
     __syncthreads();
     if (threadIdx.x == 0) {
@@ -456,7 +576,7 @@ __global__ void __launch_bounds__(FUSE_SCAN ? 1024 : 128, 1) select_kernel(FwdPa
     __syncthreads();
     if (!s_last) return;
     __threadfence();
-    build_permutation(p, s_scan, s_scan + p.E);
+    build_permutation_small(p);
 }
 
 __global__ void __launch_bounds__(1024) scan_kernel(FwdParams p)
@@ -496,21 +616,9 @@ __global__ void block_dots_kernel(DevMatrix m, const int8_t *xq, int n, int32_t 
     }
 }
 
-}  // namespace
-
 cudaError_t launch_router(const FwdParams &p, cudaStream_t st)
 {
-    if (p.T <= 256 && (p.H & 3) == 0 && p.H <= 12288) {   // token tile fits in shared memory
-        constexpr int TT = 4;
-        const size_t smem = (size_t)TT * p.H * 4;
-        if (smem > 48 * 1024) {
-            cudaError_t e = cudaFuncSetAttribute(router_small_kernel<TT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                 (int)smem);
-            if (e != cudaSuccess) return e;
-        }
-        dim3 grid((p.E + 3) / 4, (p.T + TT - 1) / TT);
-        router_small_kernel<TT><<<grid, 128, smem, st>>>(p);
-    } else if (p.T <= 256) {
+    if (p.T <= 256) {
         dim3 grid((p.E + 3) / 4, (p.T + 3) / 4);
         router_kernel<4, 1><<<grid, 128, 0, st>>>(p);
     } else {
@@ -522,8 +630,10 @@ cudaError_t launch_router(const FwdParams &p, cudaStream_t st)
 
 cudaError_t clear_routing_state(const FwdParams &p, cudaStream_t st)
 {
-    // the selection ticket (16 bytes) and the expert masks are one region
-    return cudaMemsetAsync(p.sync, 0, 16 + sizeof(uint32_t) * (size_t)p.E * p.mask_words, st);
+    // small batches keep their masks in shared memory and reset their own
+    // tickets; larger ones need zeroed global masks (tickets included)
+    if (p.T <= kFusedScanMaxT) return cudaSuccess;
+    return cudaMemsetAsync(p.sync, 0, kRoutingTicketBytes + sizeof(uint32_t) * (size_t)p.E * p.mask_words, st);
 }
 
 cudaError_t launch_select(const FwdParams &p, cudaStream_t st)
@@ -541,6 +651,48 @@ cudaError_t launch_select(const FwdParams &p, cudaStream_t st)
     if (e != cudaSuccess) return e;
     scan_kernel<<<1, 1024, sizeof(int) * (2 * (size_t)p.E + 1), st>>>(p);
     return cudaGetLastError();
+}
+
+template <int NL>
+cudaError_t launch_routing_small(const FwdParams &p, cudaStream_t st)
+{
+    constexpr int TT = 4;
+    const size_t smem = (size_t)TT * p.H * 4;
+    // the kernel also has static shared memory (the permutation), so the dynamic
+    // part needs the opt-in attribute; set once per device and size
+    static size_t opted[64] = {};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= 64 || opted[dev] < smem) {
+        e = cudaFuncSetAttribute(router_small_kernel<TT, NL>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+        if (dev >= 0 && dev < 64) opted[dev] = smem;
+    }
+    dim3 grid((p.E + 3) / 4, (p.T + TT - 1) / TT);
+    router_small_kernel<TT, NL><<<grid, 128, smem, st>>>(p);
+    return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t launch_routing(const FwdParams &p, cudaStream_t st, const Marker &mk)
+{
+    cudaError_t e;
+    if (p.E > kMaxRouteExperts) return cudaErrorInvalidValue;
+    // one kernel when the token tile fits in shared memory and the tile tickets in their region
+    if (p.T <= kFusedScanMaxT && (p.H & 3) == 0 && p.H <= 12288 && 4 * (1 + (p.T + 3) / 4) <= kRoutingTicketBytes) {
+        e = p.E <= 128 ? launch_routing_small<4>(p, st) : launch_routing_small<8>(p, st);
+        if (e != cudaSuccess) return e;
+        mk.mark("routing");
+        return cudaSuccess;
+    }
+    if ((e = clear_routing_state(p, st)) != cudaSuccess) return e;
+    if ((e = launch_router(p, st)) != cudaSuccess) return e;
+    mk.mark("router");
+    if ((e = launch_select(p, st)) != cudaSuccess) return e;
+    mk.mark("select");
+    return cudaSuccess;
 }
 
 int launch_quantize_rows(const float *x, int n, int cols, int8_t *xq, float *xd, float *xs, void *stream)
