@@ -413,9 +413,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 } else {
                     tmem_ld_wait();
                     const size_t s0 = (size_t)x.slot + 32 * cc;
+                    if (p.y_rows) {   // expert parallel: the output row of each slot is its received row
 #pragma unroll
-                    for (int i = 0; i < 32; i++)
-                        if (i < n_here) p.y[(size_t)y_row(p, s0 + i) * p.H + f] = __uint_as_float(g[i]);
+                        for (int i = 0; i < 32; i++)
+                            if (i < n_here) p.y[(size_t)p.y_rows[s0 + i] * p.H + f] = __uint_as_float(g[i]);
+                    } else {
+                        float *dst = p.y + s0 * p.H + f;
+#pragma unroll
+                        for (int i = 0; i < 32; i++)
+                            if (i < n_here) dst[(size_t)i * p.H] = __uint_as_float(g[i]);
+                    }
                 }
             }
             tc_fence_before();
