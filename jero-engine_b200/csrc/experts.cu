@@ -557,21 +557,55 @@ __global__ void __launch_bounds__(256) combine_kernel(FwdParams p)
 {
     __shared__ long long s_pos[kMaxK];
     __shared__ float s_w[kMaxK];
-    const int t = blockIdx.y, k = p.k;
-    if (threadIdx.x < k) {
-        const int r = threadIdx.x;
-        s_pos[r] = p.slot_of[(size_t)t * k + r];
-        s_w[r] = p.sel_w[(size_t)t * k + r];
-    }
-    __syncthreads();
-    const int H = p.H;
-    const size_t shared_row = (size_t)p.T * k + t;
-    for (int h = blockIdx.x * blockDim.x + threadIdx.x; h < H; h += gridDim.x * blockDim.x) {
-        float v = 0.0f;
-        if (p.S > 0) v = __fadd_rn(v, p.y[shared_row * H + h]);
-        for (int r = 0; r < k; r++)
-            if (s_pos[r] >= 0) v = __fadd_rn(v, __fmul_rn(s_w[r], p.y[(size_t)s_pos[r] * H + h]));
-        p.out[(size_t)t * H + h] = v;
+    const int k = p.k, H = p.H, mw = p.mask_words;
+    for (int t = blockIdx.y; t < p.T; t += gridDim.y) {
+        if (threadIdx.x < k) {
+            const int r = threadIdx.x;
+            long long pos;
+            if (p.T <= kFusedRoutingMaxT) {   // the routing kernel wrote the slot of each choice
+                pos = p.slot_of[(size_t)t * k + r];
+            } else {                          // slot from the expert masks
+                const int e = p.sel_idx[(size_t)t * k + r];
+                pos = -1;
+                if (e >= 0) {
+                    const uint32_t m = p.mask[(size_t)e * mw + (t >> 5)];
+                    pos = p.offsets[e] + p.wprefix[(size_t)e * mw + (t >> 5)] + __popc(m & ((1u << (t & 31)) - 1u));
+                }
+            }
+            s_pos[r] = pos;
+            s_w[r] = p.sel_w[(size_t)t * k + r];
+        }
+        __syncthreads();
+        const size_t shared_row = (size_t)p.T * k + t;
+        if ((H & 3) == 0) {   // four values per thread, same operation order per value
+            const int H4 = H >> 2;
+            for (int h4 = blockIdx.x * blockDim.x + threadIdx.x; h4 < H4; h4 += gridDim.x * blockDim.x) {
+                float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (p.S > 0) {
+                    const float4 s = reinterpret_cast<const float4 *>(p.y + shared_row * H)[h4];
+                    v = make_float4(__fadd_rn(v.x, s.x), __fadd_rn(v.y, s.y), __fadd_rn(v.z, s.z), __fadd_rn(v.w, s.w));
+                }
+                for (int r = 0; r < k; r++) {
+                    if (s_pos[r] < 0) continue;
+                    const float w = s_w[r];
+                    const float4 y = reinterpret_cast<const float4 *>(p.y + (size_t)s_pos[r] * H)[h4];
+                    v.x = __fadd_rn(v.x, __fmul_rn(w, y.x));
+                    v.y = __fadd_rn(v.y, __fmul_rn(w, y.y));
+                    v.z = __fadd_rn(v.z, __fmul_rn(w, y.z));
+                    v.w = __fadd_rn(v.w, __fmul_rn(w, y.w));
+                }
+                reinterpret_cast<float4 *>(p.out + (size_t)t * H)[h4] = v;
+            }
+        } else {
+            for (int h = blockIdx.x * blockDim.x + threadIdx.x; h < H; h += gridDim.x * blockDim.x) {
+                float v = 0.0f;
+                if (p.S > 0) v = __fadd_rn(v, p.y[shared_row * H + h]);
+                for (int r = 0; r < k; r++)
+                    if (s_pos[r] >= 0) v = __fadd_rn(v, __fmul_rn(s_w[r], p.y[(size_t)s_pos[r] * H + h]));
+                p.out[(size_t)t * H + h] = v;
+            }
+        }
+        __syncthreads();
     }
 }
 
@@ -672,7 +706,8 @@ cudaError_t launch_down(const FwdParams &p, const LayerDev &L, const LayerMaps &
 
 cudaError_t launch_combine(const FwdParams &p, cudaStream_t st)
 {
-    dim3 grid((p.H + 255) / 256 < 8 ? (p.H + 255) / 256 : 8, p.T);
+    const int per = (p.H & 3) == 0 ? p.H / 4 : p.H;
+    dim3 grid((per + 255) / 256 < 8 ? (per + 255) / 256 : 8, p.T < 65535 ? p.T : 65535);
     combine_kernel<<<grid, 256, 0, st>>>(p);
     return cudaGetLastError();
 }

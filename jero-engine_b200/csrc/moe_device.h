@@ -48,6 +48,10 @@ struct LayerMaps {
     MatMaps gate_tc, up_tc, down_tc, sh_gate_tc, sh_up_tc, sh_down_tc;  // tensor-core path: 128-row boxes per 256 values
 };
 
+// Batches up to this many tokens route in one kernel and get the slot of each
+// choice in FwdParams::slot_of; larger ones leave the global expert masks.
+constexpr int kFusedRoutingMaxT = 256;
+
 // Bytes of the routing tickets in front of the expert masks: [0] the last
 // token tile, [1 + j] the CTAs of token tile j (fused routing, T <= 256).
 constexpr int kRoutingTicketBytes = 1024;

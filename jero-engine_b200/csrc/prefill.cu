@@ -441,26 +441,42 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 }
 
 // B operand of the gate/up GEMM: slot s holds f16(xq * d) of its token (the
-// activation blocks the decode path uses), 8 values per thread, each group of
-// four in the order (0, 2, 1, 3).
-__global__ void gather_act_f16_kernel(FwdParams p, int n_slots)
+// activation blocks the decode path uses), each group of four values in the
+// order (0, 2, 1, 3). One warp per slot row, 16 values per lane: bytes go to
+// f32 exactly with a byte permute and one add (2^23 + 128 + q - (2^23 + 128)),
+// then f32(q) * d and one f16 rounding per value, as (float)q * d would.
+__device__ __forceinline__ float q8_to_f32(uint32_t flipped, int byte_idx)
 {
-    const int per_row = p.H >> 3;
-    const long long total = (long long)n_slots * per_row;
-    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
-        const int s = (int)(i / per_row), c = (int)(i % per_row);
-        const int tok = p.perm_token[s];
-        const uint2 q = *reinterpret_cast<const uint2 *>(p.xq + (size_t)tok * p.H + 8 * c);
-        const float d = p.xd[(size_t)tok * (p.H >> 5) + (c >> 2)];
-        const int8_t *qb = reinterpret_cast<const int8_t *>(&q);
-        uint32_t h[4];
+    const uint32_t b = __byte_perm(flipped, 0x4B000000u, 0x7540u | (uint32_t)byte_idx);
+    return __int_as_float((int)b) - 8388736.0f;   // 2^23 + 128
+}
+
+__global__ void __launch_bounds__(256) gather_act_f16_kernel(FwdParams p, int n_slots)
+{
+    const int H = p.H, chunks = H >> 4;
+    const int lane = threadIdx.x & 31;
+    const int warp = (int)((blockIdx.x * (size_t)blockDim.x + threadIdx.x) >> 5);
+    const int n_warps = (int)((gridDim.x * (size_t)blockDim.x) >> 5);
+    __half *a16 = static_cast<__half *>(p.a16);
+    for (int s = warp; s < n_slots; s += n_warps) {
+        const size_t tok = (size_t)p.perm_token[s];
+        const int8_t *xr = p.xq + tok * H;
+        const float *dr = p.xd + tok * (H >> 5);
+        __half *dst = a16 + (size_t)s * p.a16_stride;
+        for (int c = lane; c < chunks; c += 32) {
+            const uint4 q = *reinterpret_cast<const uint4 *>(xr + 16 * c);
+            const float d = dr[c >> 1];
+            const uint32_t w[4] = {q.x ^ 0x80808080u, q.y ^ 0x80808080u, q.z ^ 0x80808080u, q.w ^ 0x80808080u};
+            uint32_t h[8];
 #pragma unroll
-        for (int k = 0; k < 2; k++) {
-            h[2 * k] = h2_bits(__floats2half2_rn((float)qb[4 * k] * d, (float)qb[4 * k + 2] * d));
-            h[2 * k + 1] = h2_bits(__floats2half2_rn((float)qb[4 * k + 1] * d, (float)qb[4 * k + 3] * d));
+            for (int i = 0; i < 4; i++) {
+                h[2 * i] = h2_bits(__floats2half2_rn(q8_to_f32(w[i], 0) * d, q8_to_f32(w[i], 2) * d));
+                h[2 * i + 1] = h2_bits(__floats2half2_rn(q8_to_f32(w[i], 1) * d, q8_to_f32(w[i], 3) * d));
+            }
+            uint4 *o = reinterpret_cast<uint4 *>(dst + 16 * c);
+            o[0] = make_uint4(h[0], h[1], h[2], h[3]);
+            o[1] = make_uint4(h[4], h[5], h[6], h[7]);
         }
-        *reinterpret_cast<uint4 *>(static_cast<__half *>(p.a16) + (size_t)s * p.a16_stride + 8 * c) =
-            make_uint4(h[0], h[1], h[2], h[3]);
     }
 }
 
@@ -549,7 +565,7 @@ cudaError_t launch_prefill(const FwdParams &p, const LayerDev &L, const LayerMap
 {
     cudaError_t e;
     const int n_slots = p.T * p.k + (p.S > 0 ? p.T : 0);
-    gather_act_f16_kernel<<<num_sms * 4, 256, 0, st>>>(p, n_slots);
+    gather_act_f16_kernel<<<num_sms * 8, 256, 0, st>>>(p, n_slots);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     tile_plan_kernel<<<1, 32, 0, st>>>(p, L.gate.rows, p.S > 0 ? L.sh_gate.rows : 0, p.H);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;

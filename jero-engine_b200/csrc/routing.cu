@@ -11,7 +11,7 @@ namespace {
 
 // Batches up to this many tokens build the dispatch permutation inside the
 // selection kernel (shared-memory masks); larger ones use scan_kernel.
-constexpr int kFusedScanMaxT = 256;
+constexpr int kFusedScanMaxT = kFusedRoutingMaxT;
 constexpr int kFusedMaskWords = kFusedScanMaxT / 32;
 
 // Quantises the activation blocks of tokens [t0, t0 + ntok): eight lanes per
@@ -369,16 +369,6 @@ __device__ void build_permutation(const FwdParams &p, int *s_count, int *s_off)
     }
     if (p.S > 0)
         for (int i = threadIdx.x; i < p.T; i += blockDim.x) p.perm_token[(size_t)p.T * p.k + i] = i;
-    // slot of each (token, rank) choice, for the combine
-    for (int i = threadIdx.x; i < p.T * p.k; i += blockDim.x) {
-        const int t = i / p.k, e = p.sel_idx[i];
-        int slot = -1;
-        if (e >= 0) {
-            const uint32_t m = p.mask[(size_t)e * mw + (t >> 5)];
-            slot = s_off[e] + p.wprefix[(size_t)e * mw + (t >> 5)] + __popc(m & ((1u << (t & 31)) - 1u));
-        }
-        p.slot_of[i] = slot;
-    }
 }
 
 // The same permutation for T <= 256 by the last CTA of the selection, in
