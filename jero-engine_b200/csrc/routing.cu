@@ -453,6 +453,109 @@ __device__ void build_permutation_small(const FwdParams &p)
     if (threadIdx.x == 0) *p.sync = 0;   // ticket ready for the next selection
 }
 
+// Large batches: the router as a tiled f32 GEMM in the same canonical order.
+// A CTA (16 warps) covers 32 tokens x 32 experts; warp (tg, eg) owns 8 tokens
+// x 8 experts, lane l holding the partials of h4 = l (mod 32) for all 64, so
+// every logit is still lane fmaf chains in increasing h plus the xor
+// butterfly. Token and router rows are staged in shared memory 256 values at a
+// time (cp.async, double-buffered), which cuts the L2 re-reads of the router
+// rows by 4x and of the token rows by 2x against per-warp global loads.
+constexpr int kRtTok = 32, kRtExp = 32, kRtChunk4 = 64;   // chunk: 64 float4 = 256 values
+
+__device__ __forceinline__ void cp_async16(void *smem, const void *gmem, bool valid)
+{
+    const uint32_t s = (uint32_t)__cvta_generic_to_shared(smem);
+    const int n = valid ? 16 : 0;   // 0: zero fill, nothing read
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(s), "l"(gmem), "r"(n) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+__global__ void __launch_bounds__(512, 1) router_tiled_kernel(FwdParams p)
+{
+    extern __shared__ float4 rt_smem[];   // [2][kRtTok + kRtExp][kRtChunk4]
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int tg = warp & 3, eg = warp >> 2;
+    const int t_base = blockIdx.y * kRtTok, e_base = blockIdx.x * kRtExp;
+    const int H = p.H, E = p.E, T = p.T, n4 = H >> 2;
+    const int nchunks = (n4 + kRtChunk4 - 1) / kRtChunk4;
+    constexpr int kRows = kRtTok + kRtExp;
+
+    auto stage = [&](int c, int buf) {
+        float4 *dst = rt_smem + (size_t)buf * kRows * kRtChunk4;
+        for (int i = threadIdx.x; i < kRows * kRtChunk4; i += blockDim.x) {
+            const int r = i / kRtChunk4, c4 = i - r * kRtChunk4;
+            const int h4 = c * kRtChunk4 + c4;
+            const bool tok_row = r < kRtTok;
+            const int g = tok_row ? t_base + r : e_base + (r - kRtTok);
+            const bool valid = h4 < n4 && (tok_row ? g < T : g < E);
+            const float *src = tok_row ? p.x + (size_t)(valid ? g : 0) * H : p.router + (size_t)(valid ? g : 0) * H;
+            cp_async16(dst + i, reinterpret_cast<const float4 *>(src) + (valid ? h4 : 0), valid);
+        }
+        cp_async_commit();
+    };
+
+    float acc[8][8];
+#pragma unroll
+    for (int t = 0; t < 8; t++)
+#pragma unroll
+        for (int e = 0; e < 8; e++) acc[t][e] = 0.0f;
+
+    stage(0, 0);
+    for (int c = 0; c < nchunks; c++) {
+        if (c + 1 < nchunks) {
+            stage(c + 1, (c + 1) & 1);
+            cp_async_wait<1>();
+        } else {
+            cp_async_wait<0>();
+        }
+        __syncthreads();
+        const float4 *xs = rt_smem + (size_t)(c & 1) * kRows * kRtChunk4;
+        const float4 *ws = xs + kRtTok * kRtChunk4;
+#pragma unroll
+        for (int j = 0; j < kRtChunk4 / 32; j++) {
+            const int c4 = lane + 32 * j;
+            if (c * kRtChunk4 + c4 < n4) {
+                float4 w[8];
+#pragma unroll
+                for (int e = 0; e < 8; e++) w[e] = ws[(eg * 8 + e) * kRtChunk4 + c4];
+#pragma unroll
+                for (int t = 0; t < 8; t++) {
+                    const float4 xv = xs[(tg * 8 + t) * kRtChunk4 + c4];
+#pragma unroll
+                    for (int e = 0; e < 8; e++) {
+                        acc[t][e] = __fmaf_rn(w[e].x, xv.x, acc[t][e]);
+                        acc[t][e] = __fmaf_rn(w[e].y, xv.y, acc[t][e]);
+                        acc[t][e] = __fmaf_rn(w[e].z, xv.z, acc[t][e]);
+                        acc[t][e] = __fmaf_rn(w[e].w, xv.w, acc[t][e]);
+                    }
+                }
+            }
+        }
+        __syncthreads();   // the buffer is refilled by the next iteration's stage
+    }
+#pragma unroll
+    for (int t = 0; t < 8; t++) {
+#pragma unroll
+        for (int e = 0; e < 8; e++) {
+            float v = acc[t][e];
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
+            const int tok = t_base + tg * 8 + t, ex = e_base + eg * 8 + e;
+            if (lane == ((t * 8 + e) & 31) && tok < T && ex < E) {
+                if (p.logit_bias) v = __fadd_rn(v, p.logit_bias[ex]);
+                p.logits[(size_t)tok * E + ex] = v;
+            }
+        }
+    }
+    // activation blocks of this CTA's tokens, shared over the expert tiles
+    if (p.quant_x) {
+        const int ntok = min(kRtTok, T - t_base);
+        if (ntok > 0) quantize_tile(p, t_base, ntok, blockIdx.x * 16 + warp, gridDim.x * 16, lane);
+    }
+}
+
 // Routing of a small batch (T <= 256) in one kernel. Logits in the canonical
 // order of router_kernel, with the token tile staged in shared memory and each
 // warp's router row held in registers 2048 values at a time (one DRAM round
@@ -611,6 +714,19 @@ cudaError_t launch_router(const FwdParams &p, cudaStream_t st)
     if (p.T <= 256) {
         dim3 grid((p.E + 3) / 4, (p.T + 3) / 4);
         router_kernel<4, 1><<<grid, 128, 0, st>>>(p);
+    } else if ((p.H & 3) == 0) {
+        const size_t smem = 2 * (size_t)(kRtTok + kRtExp) * kRtChunk4 * sizeof(float4);
+        static size_t opted[64] = {};
+        int dev = 0;
+        cudaError_t e = cudaGetDevice(&dev);
+        if (e != cudaSuccess) return e;
+        if (dev < 0 || dev >= 64 || opted[dev] < smem) {
+            e = cudaFuncSetAttribute(router_tiled_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+            if (e != cudaSuccess) return e;
+            if (dev >= 0 && dev < 64) opted[dev] = smem;
+        }
+        dim3 grid((p.E + kRtExp - 1) / kRtExp, (p.T + kRtTok - 1) / kRtTok);
+        router_tiled_kernel<<<grid, 512, smem, st>>>(p);
     } else {
         dim3 grid((p.E + 15) / 16, (p.T + 7) / 8);
         router_kernel<8, 4><<<grid, 128, 0, st>>>(p);
