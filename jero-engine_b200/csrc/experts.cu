@@ -71,10 +71,22 @@ struct Smem {
     volatile int *abort_flag;
 };
 
+// Staged activation blocks, unit-major: block u of token t, half h (16 bytes)
+// at u * kUnitStride + t * 32 + h * 16; its (d, d*sum q) pair at
+// u * kDsStride + t * 8. The 16- and 8-byte pads put the eight lanes of a row
+// (eight consecutive units) on distinct banks, and every token offset is a
+// compile-time immediate in the dot loop.
+constexpr int kUnitStride = kTT * 32 + 16;
+constexpr int kDsStride = kTT * 8 + 8;
+
+// Bytes of the (d, d*sum q) region, rounded up to 16 so that the int4 problem
+// table after the g/u buffers stays 16-byte aligned for any block count.
+__host__ __device__ inline size_t ds_region_bytes(size_t nu) { return (nu * kDsStride + 15) / 16 * 16; }
+
 __host__ __device__ inline size_t smem_bytes(const StreamCfg &c)
 {
     const size_t nu = (size_t)c.act_k / 32;
-    return (size_t)c.stages * c.stage_bytes + (size_t)kTT * nu * 32 + (size_t)kTT * nu * 8 + 2 * (size_t)kTT * 32 * 4 +
+    return (size_t)c.stages * c.stage_bytes + nu * kUnitStride + ds_region_bytes(nu) + 2 * (size_t)kTT * 32 * 4 +
            16 * (size_t)c.max_q + 8 * ((size_t)c.max_q + 1) + 16 * (size_t)c.stages + 16;
 }
 
@@ -124,8 +136,8 @@ __device__ __forceinline__ Smem carve(uint8_t *base, const StreamCfg &c)
     Smem s;
     s.ring = base;
     s.xq = reinterpret_cast<int4 *>(base + (size_t)c.stages * c.stage_bytes);
-    s.xds = reinterpret_cast<float2 *>(s.xq + (size_t)kTT * 2 * nu);
-    s.g = reinterpret_cast<float *>(s.xds + (size_t)kTT * nu);
+    s.xds = reinterpret_cast<float2 *>(reinterpret_cast<uint8_t *>(s.xq) + (size_t)nu * kUnitStride);
+    s.g = reinterpret_cast<float *>(reinterpret_cast<uint8_t *>(s.xds) + ds_region_bytes(nu));
     s.u = s.g + kTT * 32;
     s.prob = reinterpret_cast<int4 *>(s.u + kTT * 32);
     s.cpre = reinterpret_cast<long long *>(s.prob + c.max_q);
@@ -159,24 +171,26 @@ __device__ __forceinline__ void drain(const Smem &s, int stages, uint32_t g)
     }
 }
 
-// Stages the activation blocks of nt rows: xq as [t][half][unit] 16-byte
-// halves (so eight lanes reading eight consecutive units touch 128 contiguous
-// bytes) and (d, d*sum q) pairs as [t][unit]. Rows are token ids from perm,
-// or consecutive slots from row0 when perm is null.
-__device__ __forceinline__ void stage_act(const Smem &s, int nu_s, const int8_t *gq, const float *gd, const float *gs,
+// Stages the activation blocks of nt rows in the unit-major layout above.
+// Rows are token ids from perm, or consecutive slots from row0 when perm is null.
+__device__ __forceinline__ void stage_act(const Smem &s, const int8_t *gq, const float *gd, const float *gs,
                                           size_t q_stride, size_t d_stride, const int32_t *perm, int row0, int nt,
                                           int K)
 {
     const int nu = K >> 5;
+    uint8_t *xq = reinterpret_cast<uint8_t *>(s.xq);
+    uint8_t *xds = reinterpret_cast<uint8_t *>(s.xds);
     for (int v = threadIdx.x; v < nt * nu * 2; v += kConsumers) {
-        const int i = v / (2 * nu), rem = v % (2 * nu), u = rem >> 1, h = rem & 1;
+        const int i = v / (2 * nu), rem = v - i * 2 * nu, u = rem >> 1, h = rem & 1;
         const size_t row = perm ? (size_t)perm[row0 + i] : (size_t)(row0 + i);
-        s.xq[((size_t)i * 2 + h) * nu_s + u] = __ldg(reinterpret_cast<const int4 *>(gq + row * q_stride) + 2 * u + h);
+        *reinterpret_cast<int4 *>(xq + (size_t)u * kUnitStride + i * 32 + h * 16) =
+            __ldg(reinterpret_cast<const int4 *>(gq + row * q_stride) + 2 * u + h);
     }
     for (int v = threadIdx.x; v < nt * nu; v += kConsumers) {
-        const int i = v / nu, u = v % nu;
+        const int i = v / nu, u = v - i * nu;
         const size_t row = perm ? (size_t)perm[row0 + i] : (size_t)(row0 + i);
-        s.xds[(size_t)i * nu_s + u] = make_float2(__ldg(gd + row * d_stride + u), __ldg(gs + row * d_stride + u));
+        *reinterpret_cast<float2 *>(xds + (size_t)u * kDsStride + i * 8) =
+            make_float2(__ldg(gd + row * d_stride + u), __ldg(gs + row * d_stride + u));
     }
 }
 
@@ -202,30 +216,36 @@ template <int FMT, int NMAT, int NT>
 __device__ __forceinline__ void consume_chunk(const Smem &s, const StreamCfg &c, const uint8_t *stage, int rw, int l8,
                                               int nu_slice, int ubase, int nu_s, float (&acc)[NMAT][NT])
 {
-    // 32-bit shared addresses throughout the loop
+    // 32-bit shared addresses, advanced by constants each iteration
     const uint32_t st = smem_addr(stage);
     const uint32_t mat_stride = (uint32_t)kRows * (c.qs_row + c.meta_row);
     const uint32_t q0a = st + (uint32_t)rw * c.qs_row;
     const uint32_t m0a = st + (uint32_t)kRows * c.qs_row + (uint32_t)rw * c.meta_row;
-    const uint32_t xa = smem_addr(s.xq), xda = smem_addr(s.xds);
-    const uint32_t xh_stride = (uint32_t)nu_s * 16;   // bytes between the two halves of a token's blocks
+    uint32_t qa[NMAT], ma[NMAT];
+#pragma unroll
+    for (int m = 0; m < NMAT; m++) {
+        qa[m] = q0a + m * mat_stride + (FMT == FMT_Q4_K ? 16 : 32) * l8;
+        ma[m] = m0a + m * mat_stride + (FMT == FMT_Q4_K ? 0 : 2 * l8);
+    }
+    uint32_t xu = smem_addr(s.xq) + (uint32_t)(ubase + l8) * kUnitStride;
+    uint32_t du = smem_addr(s.xds) + (uint32_t)(ubase + l8) * kDsStride;
 #pragma unroll 1
     for (int u = l8; u < nu_slice; u += 8) {
-        const uint32_t ug = (uint32_t)(ubase + u);
         if (FMT == FMT_Q4_K) {
             Q4Nib nb[NMAT];
             float2 sc[NMAT];
 #pragma unroll
             for (int m = 0; m < NMAT; m++) {
-                nb[m] = q4_nibbles(lds128(q0a + m * mat_stride + 16 * u));
-                sc[m] = q4_scales(lds128(m0a + m * mat_stride + 16 * (u >> 3)), l8);
+                nb[m] = q4_nibbles(lds128(qa[m]));
+                sc[m] = q4_scales(lds128(ma[m]), l8);   // super-block u / 8 (u % 8 == l8)
+                qa[m] += 128;
+                ma[m] += 16;
             }
 #pragma unroll
             for (int t = 0; t < NT; t++) {
-                const uint32_t xt = xa + (uint32_t)t * 2 * xh_stride + 16 * ug;
-                const int4 a = lds128i(xt);
-                const int4 b = lds128i(xt + xh_stride);
-                const float2 ds = lds64f(xda + 8 * ((uint32_t)t * nu_s + ug));
+                const int4 a = lds128i(xu + t * 32);
+                const int4 b = lds128i(xu + t * 32 + 16);
+                const float2 ds = lds64f(du + t * 8);
 #pragma unroll
                 for (int m = 0; m < NMAT; m++) {
                     const float f = i2f_small(q4_isum16(nb[m], a, b));
@@ -238,21 +258,24 @@ __device__ __forceinline__ void consume_chunk(const Smem &s, const StreamCfg &c,
             float d[NMAT];
 #pragma unroll
             for (int m = 0; m < NMAT; m++) {
-                q0[m] = lds128(q0a + m * mat_stride + 32 * u);
-                q1[m] = lds128(q0a + m * mat_stride + 32 * u + 16);
-                d[m] = __half2float(__ushort_as_half((unsigned short)lds16(m0a + m * mat_stride + 2 * u)));
+                q0[m] = lds128(qa[m]);
+                q1[m] = lds128(qa[m] + 16);
+                d[m] = __half2float(__ushort_as_half((unsigned short)lds16(ma[m])));
+                qa[m] += 256;
+                ma[m] += 16;
             }
 #pragma unroll
             for (int t = 0; t < NT; t++) {
-                const uint32_t xt = xa + (uint32_t)t * 2 * xh_stride + 16 * ug;
-                const int4 a = lds128i(xt);
-                const int4 b = lds128i(xt + xh_stride);
-                const float xd = lds64f(xda + 8 * ((uint32_t)t * nu_s + ug)).x;
+                const int4 a = lds128i(xu + t * 32);
+                const int4 b = lds128i(xu + t * 32 + 16);
+                const float xd = lds64f(du + t * 8).x;
 #pragma unroll
                 for (int m = 0; m < NMAT; m++)
                     acc[m][t] = fmaf(i2f_small(q8_isum(q0[m], q1[m], a, b)), d[m] * xd, acc[m][t]);
             }
         }
+        xu += 8 * kUnitStride;
+        du += 8 * kDsStride;
     }
 }
 
@@ -419,10 +442,10 @@ __global__ void __launch_bounds__(kStreamThreads, 2)
             if (staged_slot != x.pr.slot0 || staged_tile != tt) {
                 named_bar(1, kConsumers);
                 if (NMAT == 2)
-                    stage_act(s, nu_s, p.xq, p.xd, p.xs, (size_t)p.H, (size_t)(p.H >> 5), p.perm_token,
+                    stage_act(s, p.xq, p.xd, p.xs, (size_t)p.H, (size_t)(p.H >> 5), p.perm_token,
                               x.pr.slot0 + t0, nt, K);
                 else
-                    stage_act(s, nu_s, p.aq, p.ad, p.as, (size_t)p.W, (size_t)(p.W >> 5), nullptr, x.pr.slot0 + t0, nt,
+                    stage_act(s, p.aq, p.ad, p.as, (size_t)p.W, (size_t)(p.W >> 5), nullptr, x.pr.slot0 + t0, nt,
                               K);
                 named_bar(1, kConsumers);
                 staged_slot = x.pr.slot0;
