@@ -108,6 +108,9 @@ typedef struct moe_device_spec {
  * kernels; these flags force one path for every forward of the context. */
 #define MOE_FLAG_TENSOR_CORES_ALWAYS 1
 #define MOE_FLAG_TENSOR_CORES_NEVER 2
+/* Expert parallelism: exchange through NCCL even for batches that would use
+ * the peer-memory exchange (see moe_forward_ep). */
+#define MOE_FLAG_EP_NCCL_ONLY 4
 #define MOE_TENSOR_CORE_MIN_TOKENS 256
 
 /* Memory the admission check compares against. The real inspector reads

@@ -12,6 +12,7 @@
 #include <vector>
 
 #include "../../include/jeromoe.h"
+#include "ep_p2p.h"
 #include "ep_plan.h"
 #include "kernels.h"
 #include "layout.h"
@@ -134,6 +135,13 @@ struct EpState {
     int32_t *h_off = nullptr;     // pinned: all-gathered offsets
     uint8_t *h_plan = nullptr;    // pinned: plan upload staging
     size_t h_off_bytes = 0, h_plan_bytes = 0;
+    uint8_t *small = nullptr;     // device: set-up all-gathers (flags, IPC handles)
+    // exchange over peer memory (batches up to kEpP2PMaxTokens per rank)
+    int p2p_state = 0;            // 0 not set up, 1 ready, -1 off for the current dims
+    EpP2PLayout p2p{};
+    uint8_t *p2p_arena = nullptr;
+    uint8_t *p2p_peer[kEpMaxRanks] = {};
+    uint32_t p2p_epoch = 0;
 };
 
 }  // namespace
@@ -593,6 +601,18 @@ void shared_mark_cb(void *user, const char *kernel)
     inner->mark(name);
 }
 
+// Unmaps the peers' arenas and frees this rank's (every rank is idle here).
+void ep_p2p_release(EpState &ep)
+{
+    for (int g = 0; g < kEpMaxRanks; g++) {
+        if (ep.p2p_peer[g] && ep.p2p_peer[g] != ep.p2p_arena) cudaIpcCloseMemHandle(ep.p2p_peer[g]);
+        ep.p2p_peer[g] = nullptr;
+    }
+    if (ep.p2p_arena) cudaFree(ep.p2p_arena);
+    ep.p2p_arena = nullptr;
+    ep.p2p_state = 0;
+}
+
 int nccl_fail(moe_ctx *ctx, const NcclApi *nc, ncclResult_t r, const char *what)
 {
     return fail(ctx, MOE_ERR_NCCL, "%s: %s", what, nc ? nc->GetErrorString(r) : "NCCL unavailable");
@@ -603,6 +623,97 @@ int nccl_fail(moe_ctx *ctx, const NcclApi *nc, ncclResult_t r, const char *what)
         ncclResult_t r_ = (call);                                  \
         if (r_ != ncclSuccess) return nccl_fail(ctx, nc, r_, what); \
     } while (0)
+
+// Every rank's int v, all-gathered through NCCL (set-up only; synchronises).
+int ep_allgather_int(moe_ctx *ctx, const NcclApi *nc, int v, int *out)
+{
+    EpState &ep = ctx->ep;
+    cudaStream_t st = ctx->stream;
+    int32_t *d = reinterpret_cast<int32_t *>(ep.small);
+    CUDA_TRY(ctx, cudaMemcpyAsync(d, &v, 4, cudaMemcpyHostToDevice, st), "copy");
+    NCCL_TRY(ctx, nc, nc->AllGather(d, d + 16, 1, ncclInt32, ep.comm, st), "ncclAllGather");
+    CUDA_TRY(ctx, cudaMemcpyAsync(out, d + 16, (size_t)ep.world * 4, cudaMemcpyDeviceToHost, st), "copy");
+    CUDA_TRY(ctx, cudaStreamSynchronize(st), "set-up");
+    return MOE_OK;
+}
+
+// Decides, collectively, whether this layer's forward uses the exchange over
+// peer memory, and (re)builds the arenas and their mappings when it does and
+// the current ones do not fit. Every rank reaches this at the same forward.
+int ep_p2p_prepare(moe_ctx *ctx, const LayerStore &L, bool *use)
+{
+    EpState &ep = ctx->ep;
+    const NcclApi *nc = nccl_api();
+    *use = false;
+    const int G = ep.world, me = ep.rank;
+    const int W = std::max(L.I, L.S), cap = ctx->spec.max_tokens * L.k, slots_y = cap + ctx->spec.max_tokens;
+    const bool fits = ep.p2p_state == 1 && ep.p2p.world == G && ep.p2p.E == L.E && ep.p2p.H == L.H &&
+                      ep.p2p.W >= W && ep.p2p.cap >= cap && ep.p2p.slots_y >= slots_y;
+    if (fits) { *use = true; return MOE_OK; }
+    if (ep.p2p_state == -1 && ep.p2p.world == G && ep.p2p.E == L.E && ep.p2p.H == L.H && ep.p2p.cap >= cap)
+        return MOE_OK;   // already decided against for these dims
+    const bool want = !(ctx->spec.flags & MOE_FLAG_EP_NCCL_ONLY) && G <= kEpMaxRanks &&
+                      ctx->spec.max_tokens <= kEpP2PMaxTokens && L.H % 64 == 0 && L.E % G == 0 &&
+                      L.E <= 256;
+    int all[kEpMaxRanks * 2] = {};
+    int rc;
+    if (G > kEpMaxRanks) {
+        ep.p2p_state = -1;
+        return MOE_OK;
+    }
+    // the arenas must have one layout on every rank: same max_tokens everywhere
+    if ((rc = ep_allgather_int(ctx, nc, want ? ctx->spec.max_tokens : 0, all))) return rc;
+    bool agree = true;
+    for (int g = 0; g < G; g++) agree = agree && all[g] == ctx->spec.max_tokens && all[g] > 0;
+    // every rank is past its previous forwards here (the all-gather ran on every stream)
+    ep_p2p_release(ep);
+    ep.p2p = ep_p2p_layout(G, L.E, L.H, W, cap, slots_y);
+    if (!agree) {
+        ep.p2p_state = -1;
+        return MOE_OK;
+    }
+    void *arena = nullptr;
+    CUDA_TRY(ctx, cudaMalloc(&arena, ep.p2p.bytes), "cudaMalloc(peer-exchange arena)");
+    ep.p2p_arena = static_cast<uint8_t *>(arena);
+    CUDA_TRY(ctx, cudaMemset(arena, 0, ep.p2p.bytes), "cudaMemset(peer-exchange arena)");
+    ep.p2p_peer[me] = ep.p2p_arena;
+    int ok = 1;
+    if (G > 1) {
+        cudaIpcMemHandle_t h;
+        CUDA_TRY(ctx, cudaIpcGetMemHandle(&h, arena), "cudaIpcGetMemHandle");
+        static_assert(sizeof(cudaIpcMemHandle_t) == 64, "IPC handle size");
+        uint8_t *d = ep.small;
+        cudaStream_t st = ctx->stream;
+        CUDA_TRY(ctx, cudaMemcpyAsync(d, &h, 64, cudaMemcpyHostToDevice, st), "copy");
+        NCCL_TRY(ctx, nc, nc->AllGather(d, d + 1024, 64, ncclUint8, ep.comm, st), "ncclAllGather");
+        cudaIpcMemHandle_t hs[kEpMaxRanks];
+        CUDA_TRY(ctx, cudaMemcpyAsync(hs, d + 1024, (size_t)G * 64, cudaMemcpyDeviceToHost, st), "copy");
+        CUDA_TRY(ctx, cudaStreamSynchronize(st), "set-up");
+        for (int g = 0; g < G && ok; g++) {
+            if (g == me) continue;
+            void *ptr = nullptr;
+            if (cudaIpcOpenMemHandle(&ptr, hs[g], cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+                cudaGetLastError();
+                ok = 0;
+            } else {
+                ep.p2p_peer[g] = static_cast<uint8_t *>(ptr);
+            }
+        }
+        if ((rc = ep_allgather_int(ctx, nc, ok, all))) return rc;
+        for (int g = 0; g < G; g++) ok = ok && all[g] == 1;
+    }
+    if (!ok) {   // some rank could not map a peer: every rank falls back together
+        ep_p2p_release(ep);
+        ep.p2p_state = -1;
+        return MOE_OK;
+    }
+    CUDA_TRY(ctx, cudaMemcpy(ep.p2p_arena + ep.p2p.o_peers, ep.p2p_peer, sizeof(ep.p2p_peer), cudaMemcpyHostToDevice),
+             "copy peer table");
+    ep.p2p_epoch = 0;
+    ep.p2p_state = 1;
+    *use = true;
+    return MOE_OK;
+}
 
 }  // namespace
 
@@ -651,7 +762,9 @@ int moe_ctx_destroy(moe_ctx *ctx)
     if (ep.comm) {
         if (const NcclApi *nc = nccl_api()) nc->CommDestroy(ep.comm);
     }
+    ep_p2p_release(ep);
     if (ep.arena) cudaFree(ep.arena);
+    if (ep.small) cudaFree(ep.small);
     if (ep.h_off) cudaFreeHost(ep.h_off);
     if (ep.h_plan) cudaFreeHost(ep.h_plan);
     if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
@@ -1085,6 +1198,9 @@ int moe_ep_init(moe_ctx *ctx, int32_t rank, int32_t world, const uint8_t *id)
     ctx->ep.comm = comm;
     ctx->ep.rank = rank;
     ctx->ep.world = world;
+    void *small = nullptr;
+    CUDA_TRY(ctx, cudaMalloc(&small, 8192), "cudaMalloc(expert-parallel set-up buffer)");
+    ctx->ep.small = static_cast<uint8_t *>(small);
     return MOE_OK;
 }
 
@@ -1124,6 +1240,118 @@ int moe_ep_plan(int32_t rank, int32_t world, int32_t E, const int32_t *all_offse
 // that owns its expert, run the local experts over the received rows (outputs
 // written at their received row), send the outputs back, then the local
 // shared expert and the combine.
+// The rest of an expert-parallel forward through peer memory, after local
+// routing: plan (offsets exchanged by the ranks' kernels), dispatch of the
+// routed rows into their owners' inboxes, the local experts reading the
+// received rows in place, return of the outputs into the sources' output
+// inboxes, the replicated shared expert and the combine. No host
+// synchronisation; every cross-GPU wait is a bounded spin in a kernel.
+static int ep_forward_p2p(moe_ctx *ctx, LayerStore &L, FwdParams p, int T, int ptr_kind, float *out,
+                          int32_t *sel_idx, float *sel_w, const Marker &mk, int layer)
+{
+    EpState &ep = ctx->ep;
+    Scratch &s = ctx->scratch;
+    cudaStream_t st = ctx->stream;
+    const EpP2PLayout &l = ep.p2p;
+    uint8_t *A = ep.p2p_arena;
+    const int G = ep.world, me = ep.rank, E = L.E, El = E / G, H = L.H;
+    cudaError_t ce;
+    ep.p2p_epoch++;
+    EpP2PArgs a{};
+    a.peers = reinterpret_cast<uint8_t *const *>(A + l.o_peers);
+    a.own = A;
+    a.rank = me; a.world = G; a.E = E; a.El = El; a.e0 = me * El; a.H = H; a.cap = l.cap;
+    a.rb = l.rb; a.o_flags = l.o_flags; a.o_off = l.o_off; a.o_xin = l.o_xin; a.o_yin = l.o_yin;
+    a.epoch = ep.p2p_epoch;
+    a.err = s.err;
+    int32_t *misc = reinterpret_cast<int32_t *>(A + l.o_misc);
+    a.ticket = misc;
+    a.n_active = misc + 4;
+    a.total = misc + 8;
+    a.problems = reinterpret_cast<Problem *>(A + l.o_prob);
+    a.perm = reinterpret_cast<int32_t *>(A + l.o_perm);
+    a.ret = reinterpret_cast<int2 *>(A + l.o_ret);
+    a.offsets = s.offsets; a.perm_token = p.perm_token; a.xq = p.xq; a.xd = p.xd; a.xs = p.xs;
+    a.n_slots = T * L.k;
+    a.y = reinterpret_cast<const float *>(A + l.o_y);
+
+    if ((ce = launch_ep_p2p_plan(a, st)) != cudaSuccess) return cuda_fail(ctx, ce, "ep plan");
+    mk.mark("ep_plan");
+    if ((ce = launch_ep_p2p_dispatch(a, ctx->num_sms, st)) != cudaSuccess) return cuda_fail(ctx, ce, "ep dispatch");
+    if ((ce = launch_ep_p2p_wait(a, 1, st)) != cudaSuccess) return cuda_fail(ctx, ce, "ep wait");
+    mk.mark("ep_dispatch");
+
+    // the local experts over the received rows, read in place from the row inbox
+    FwdParams pe{};
+    pe.T = G * l.cap; pe.H = H; pe.E = El; pe.k = 1; pe.I = L.I; pe.S = 0;
+    pe.quant_x = 1;
+    pe.max_problems = std::max(El, 1);
+    pe.xq = reinterpret_cast<int8_t *>(A + l.o_xin);
+    pe.xd = reinterpret_cast<float *>(A + l.o_xin + H);
+    pe.xs = pe.xd + H / 32;
+    pe.x_qstride = (int)l.rb;
+    pe.x_dstride = (int)(l.rb / 4);
+    pe.perm_token = a.perm; pe.problems = a.problems; pe.n_active = a.n_active;
+    pe.aq = reinterpret_cast<int8_t *>(A + l.o_aq);
+    pe.ad = reinterpret_cast<float *>(A + l.o_ad);
+    pe.as = reinterpret_cast<float *>(A + l.o_as);
+    pe.af = nullptr; pe.W = l.W;
+    pe.y = reinterpret_cast<float *>(A + l.o_y); pe.y_rows = nullptr;
+    pe.err = s.err;
+    pe.use_tc = 0;
+    if ((ce = launch_gate_up(pe, L.dev, L.maps, 0, ctx->num_sms, st)) != cudaSuccess) return cuda_fail(ctx, ce, "gate_up");
+    mk.mark("gate_up");
+    if ((ce = launch_down(pe, L.dev, L.maps, 0, ctx->num_sms, st)) != cudaSuccess) return cuda_fail(ctx, ce, "down");
+    mk.mark("down");
+    if ((ce = launch_ep_p2p_return(a, ctx->num_sms, st)) != cudaSuccess) return cuda_fail(ctx, ce, "ep return");
+    mk.mark("ep_return");
+
+    p.y = reinterpret_cast<float *>(A + l.o_yin);   // routed outputs arrive here; shared rows follow
+    if (T > 0 && L.S > 0) {
+        if (p.use_tc) {
+            FwdParams ps = p;
+            ps.n_active = misc + 12;   // a zero word: no routed problems in this pass
+            if ((ce = launch_prefill(ps, L.dev, L.maps, ctx->num_sms, mk, st)) != cudaSuccess)
+                return cuda_fail(ctx, ce, "shared expert (tensor cores)");
+        } else {
+            if ((ce = launch_gate_up(p, L.dev, L.maps, 1, ctx->num_sms, st)) != cudaSuccess)
+                return cuda_fail(ctx, ce, "shared gate_up");
+            if ((ce = launch_down(p, L.dev, L.maps, 1, ctx->num_sms, st)) != cudaSuccess)
+                return cuda_fail(ctx, ce, "shared down");
+        }
+        mk.mark("shared");
+    }
+    if ((ce = launch_ep_p2p_wait(a, 2, st)) != cudaSuccess) return cuda_fail(ctx, ce, "ep wait");
+    mk.mark("ep_wait");
+    if (T > 0) {
+        if ((ce = launch_combine(p, st)) != cudaSuccess) return cuda_fail(ctx, ce, "combine");
+        mk.mark("combine");
+    }
+    ctx->last_layer = layer;
+    ctx->last_T = T;
+    if (ptr_kind == MOE_PTR_HOST) {
+        if (T > 0) {
+            CUDA_TRY(ctx, cudaMemcpyAsync(out, s.out, (size_t)T * H * 4, cudaMemcpyDeviceToHost, st), "copy out");
+            if (sel_idx)
+                CUDA_TRY(ctx, cudaMemcpyAsync(sel_idx, s.sel_idx, (size_t)T * L.k * 4, cudaMemcpyDeviceToHost, st),
+                         "copy sel_idx");
+            if (sel_w)
+                CUDA_TRY(ctx, cudaMemcpyAsync(sel_w, s.sel_w, (size_t)T * L.k * 4, cudaMemcpyDeviceToHost, st),
+                         "copy sel_w");
+        }
+        CUDA_TRY(ctx, cudaMemcpyAsync(ctx->status_host, s.err, sizeof(int), cudaMemcpyDeviceToHost, st),
+                 "copy status");
+        CUDA_TRY(ctx, cudaStreamSynchronize(st), "forward");
+        if (*ctx->status_host) {
+            const int code = *ctx->status_host;
+            cudaMemsetAsync(s.err, 0, sizeof(int), st);
+            return fail(ctx, MOE_ERR_TIMEOUT, "a bounded %s wait ran out in layer %d (status %d)",
+                        code == kErrEpTimeout ? "peer-rank" : "device", layer, code);
+        }
+    }
+    return MOE_OK;
+}
+
 int moe_forward_ep(moe_ctx *ctx, int32_t layer, int32_t T, const float *x, float *out, int32_t *sel_idx,
                    float *sel_w, int32_t ptr_kind)
 {
@@ -1155,9 +1383,11 @@ int moe_forward_ep(moe_ctx *ctx, int32_t layer, int32_t T, const float *x, float
         mk = Marker{&Profiler::mark_cb, &ctx->prof};
     }
     int rc;
+    bool p2p = false;   // small batches: exchange over peer memory, no host synchronisation
+    if ((rc = ep_p2p_prepare(ctx, L, &p2p))) return rc;
     // the arena's all-gather buffer and pinned staging (rows and sends sized below)
     EpDims dims{G, E, H, std::max(L.I, s.W), 1, std::max(T * L.k, 1), tc_possible(ctx->spec)};
-    if ((rc = ep_reserve(ctx, dims))) return rc;
+    if (!p2p && (rc = ep_reserve(ctx, dims))) return rc;
 
     mk.mark(nullptr);
     cudaError_t ce;
@@ -1168,6 +1398,7 @@ int moe_forward_ep(moe_ctx *ctx, int32_t layer, int32_t T, const float *x, float
     } else {
         CUDA_TRY(ctx, cudaMemsetAsync(s.offsets, 0, (size_t)(E + 1) * 4, st), "memset");
     }
+    if (p2p) return ep_forward_p2p(ctx, L, p, T, ptr_kind, out, sel_idx, sel_w, mk, layer);
 
     // exchange sizes: every rank's slot offsets by expert
     NCCL_TRY(ctx, nc, nc->AllGather(s.offsets, ep.all_off, (size_t)E + 1, ncclInt32, ep.comm, st), "ncclAllGather");

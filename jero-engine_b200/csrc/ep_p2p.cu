@@ -1,0 +1,230 @@
+// ep_p2p.cu -- kernels of the expert-parallel exchange over peer memory.
+// Peer arenas are written with plain stores from this GPU; nothing reads a
+// peer's memory. Every wait on a peer's flag is bounded (about 2 s at 2 GHz)
+// and records kErrEpTimeout in the status word instead of waiting on.
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "common.cuh"
+#include "ep_p2p.h"
+
+namespace jmoe {
+namespace {
+
+constexpr long long kEpWaitCycles = 4000000000LL;
+
+__device__ __forceinline__ uint32_t *ep_flag(uint8_t *arena, size_t o_flags, int phase, int src)
+{
+    return reinterpret_cast<uint32_t *>(arena + o_flags) + phase * kEpMaxRanks + src;
+}
+
+__device__ __forceinline__ void st_release_sys(uint32_t *p, uint32_t v)
+{
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t *p)
+{
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Waits until flag >= epoch (wrap-safe); false after kEpWaitCycles.
+__device__ __forceinline__ bool wait_epoch(const uint32_t *flag, uint32_t epoch)
+{
+    const long long t0 = clock64();
+    while ((int32_t)(ld_acquire_sys(flag) - epoch) < 0) {
+        if (clock64() - t0 > kEpWaitCycles) return false;
+        __nanosleep(256);
+    }
+    return true;
+}
+
+// Raises this rank's flag of `phase` in every rank's arena, once all warps of
+// the grid have passed their system-scope fence (last-warp ticket).
+__device__ __forceinline__ void signal_when_done(const EpP2PArgs &a, int *ticket, int phase)
+{
+    __threadfence_system();
+    __syncwarp();
+    if ((threadIdx.x & 31) == 0) {
+        const int nwarps = (int)((gridDim.x * blockDim.x) >> 5);
+        if (atomicAdd(ticket, 1) == nwarps - 1) {
+            atomicExch(ticket, 0);   // ready for the next forward
+            __threadfence_system();
+            for (int g = 0; g < a.world; g++) st_release_sys(ep_flag(a.peers[g], a.o_flags, phase, a.rank), a.epoch);
+        }
+    }
+}
+
+// One CTA: publish my slot offsets to every rank, wait for every rank's, then
+// the plan of the rows I receive: my experts in order, each with its rows in
+// (source rank, source slot) order -- the global canonical order restricted
+// to my experts. perm[slot] = received row, ret[slot] = (source, source slot).
+__global__ void __launch_bounds__(256) ep_p2p_plan_kernel(EpP2PArgs a)
+{
+    __shared__ int s_off[kEpMaxRanks * (kMaxRouteExperts + 1)];
+    __shared__ int s_cnt[kMaxRouteExperts], s_slot0[kMaxRouteExperts];
+    __shared__ int s_ok;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
+    const int E = a.E, G = a.world, El = a.El;
+    for (int g = 0; g < G; g++) {
+        int32_t *dst = reinterpret_cast<int32_t *>(a.peers[g] + a.o_off) + (size_t)a.rank * (E + 1);
+        for (int i = tid; i <= E; i += blockDim.x) dst[i] = a.offsets[i];
+    }
+    __threadfence_system();
+    if (tid == 0) s_ok = 1;
+    __syncthreads();
+    if (tid < G) st_release_sys(ep_flag(a.peers[tid], a.o_flags, 0, a.rank), a.epoch);
+    if (tid < G && !wait_epoch(ep_flag(a.own, a.o_flags, 0, tid), a.epoch)) {
+        s_ok = 0;
+        atomicExch(a.err, kErrEpTimeout);
+    }
+    __syncthreads();
+    if (!s_ok) {
+        if (tid == 0) { *a.n_active = 0; *a.total = 0; }
+        return;
+    }
+    const int32_t *off = reinterpret_cast<const int32_t *>(a.own + a.o_off);
+    for (int i = tid; i < G * (E + 1); i += blockDim.x) s_off[i] = off[i];
+    __syncthreads();
+    for (int el = tid; el < El; el += blockDim.x) {
+        const int e = a.e0 + el;
+        int c = 0;
+        for (int s = 0; s < G; s++) c += s_off[s * (E + 1) + e + 1] - s_off[s * (E + 1) + e];
+        s_cnt[el] = c;
+    }
+    __syncthreads();
+    if (warp == 0) {
+        const int chunk = (El + 31) / 32, b = lane * chunk;
+        int local = 0;
+        for (int i = 0; i < chunk; i++)
+            if (b + i < El) local += s_cnt[b + i];
+        int incl = local;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int v = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += v;
+        }
+        int run = incl - local;
+        for (int i = 0; i < chunk; i++)
+            if (b + i < El) { s_slot0[b + i] = run; run += s_cnt[b + i]; }
+        if (lane == 31) *a.total = incl;
+        int nact = 0;
+        for (int c0 = 0; c0 < El; c0 += 32) {
+            const int el = c0 + lane;
+            const bool act = el < El && s_cnt[el] > 0;
+            const uint32_t bal = __ballot_sync(0xffffffffu, act);
+            __syncwarp();
+            const int pos = nact + __popc(bal & ((1u << lane) - 1u));
+            if (act) a.problems[pos] = Problem{el, s_slot0[el], s_cnt[el], 0};
+            nact += __popc(bal);
+        }
+        if (lane == 0) *a.n_active = nact;
+    }
+    __syncthreads();
+    for (int it = warp; it < El * G; it += nw) {
+        const int el = it / G, s = it - el * G, e = a.e0 + el;
+        const int *os = s_off + s * (E + 1);
+        const int c = os[e + 1] - os[e];
+        if (!c) continue;
+        int base = s_slot0[el];
+        for (int s2 = 0; s2 < s; s2++) base += s_off[s2 * (E + 1) + e + 1] - s_off[s2 * (E + 1) + e];
+        const int row = s * a.cap + (os[e] - os[a.e0]);
+        for (int i = lane; i < c; i += 32) {
+            a.perm[base + i] = row + i;
+            a.ret[base + i] = make_int2(s, os[e] + i);
+        }
+    }
+}
+
+// My routed rows, packed [H int8 | H/32 d | H/32 s], into the row inbox of the
+// rank that owns each row's expert, at (my rank, position among my rows for
+// that rank). One warp per row.
+__global__ void __launch_bounds__(256) ep_p2p_dispatch_kernel(EpP2PArgs a)
+{
+    const int lane = threadIdx.x & 31;
+    const int warp = (int)((blockIdx.x * (size_t)blockDim.x + threadIdx.x) >> 5);
+    const int nwarps = (int)((gridDim.x * (size_t)blockDim.x) >> 5);
+    const int H = a.H, chunks = H >> 4, nd = H >> 5;
+    for (int s = warp; s < a.n_slots; s += nwarps) {
+        int lo = 0, hi = a.E - 1;   // the expert of slot s: last e with offsets[e] <= s
+        while (lo < hi) {
+            const int mid = (lo + hi + 1) >> 1;
+            if (a.offsets[mid] <= s) lo = mid;
+            else hi = mid - 1;
+        }
+        const int dest = lo / a.El;
+        const int r = s - a.offsets[dest * a.El];
+        const size_t tok = (size_t)a.perm_token[s];
+        uint8_t *row = a.peers[dest] + a.o_xin + ((size_t)a.rank * a.cap + r) * a.rb;
+        const int4 *q = reinterpret_cast<const int4 *>(a.xq + tok * H);
+        for (int c = lane; c < chunks; c += 32) reinterpret_cast<int4 *>(row)[c] = q[c];
+        float *rd = reinterpret_cast<float *>(row + H);
+        for (int c = lane; c < nd; c += 32) {
+            rd[c] = a.xd[tok * nd + c];
+            rd[nd + c] = a.xs[tok * nd + c];
+        }
+    }
+    signal_when_done(a, a.ticket, 1);
+}
+
+// Expert outputs of the rows I received, by local slot, into each source's
+// output inbox at the source's own slot. One warp per row.
+__global__ void __launch_bounds__(256) ep_p2p_return_kernel(EpP2PArgs a)
+{
+    const int lane = threadIdx.x & 31;
+    const int warp = (int)((blockIdx.x * (size_t)blockDim.x + threadIdx.x) >> 5);
+    const int nwarps = (int)((gridDim.x * (size_t)blockDim.x) >> 5);
+    const int H = a.H, chunks = H >> 2;
+    const int total = *a.total;
+    for (int s = warp; s < total; s += nwarps) {
+        const int2 rr = a.ret[s];
+        float4 *dst = reinterpret_cast<float4 *>(a.peers[rr.x] + a.o_yin + (size_t)rr.y * H * 4);
+        const float4 *src = reinterpret_cast<const float4 *>(a.y + (size_t)s * H);
+        for (int c = lane; c < chunks; c += 32) dst[c] = src[c];
+    }
+    signal_when_done(a, a.ticket + 1, 2);
+}
+
+// Waits for every rank's flag of `phase` in this rank's arena.
+__global__ void ep_p2p_wait_kernel(EpP2PArgs a, int phase)
+{
+    const int lane = threadIdx.x;
+    if (lane < a.world && !wait_epoch(ep_flag(a.own, a.o_flags, phase, lane), a.epoch)) atomicExch(a.err, kErrEpTimeout);
+}
+
+int rows_grid(long long rows, int num_sms)
+{
+    const long long blocks = (rows + 7) / 8;   // 8 warps per block
+    const long long cap = 4LL * num_sms;
+    return (int)(blocks < 1 ? 1 : (blocks > cap ? cap : blocks));
+}
+
+}  // namespace
+
+cudaError_t launch_ep_p2p_plan(const EpP2PArgs &a, cudaStream_t st)
+{
+    ep_p2p_plan_kernel<<<1, 256, 0, st>>>(a);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_ep_p2p_dispatch(const EpP2PArgs &a, int num_sms, cudaStream_t st)
+{
+    ep_p2p_dispatch_kernel<<<rows_grid(a.n_slots, num_sms), 256, 0, st>>>(a);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_ep_p2p_return(const EpP2PArgs &a, int num_sms, cudaStream_t st)
+{
+    ep_p2p_return_kernel<<<rows_grid((long long)a.world * a.cap, num_sms), 256, 0, st>>>(a);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_ep_p2p_wait(const EpP2PArgs &a, int phase, cudaStream_t st)
+{
+    ep_p2p_wait_kernel<<<1, 32, 0, st>>>(a, phase);
+    return cudaGetLastError();
+}
+
+}  // namespace jmoe

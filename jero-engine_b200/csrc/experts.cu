@@ -442,7 +442,8 @@ __global__ void __launch_bounds__(kStreamThreads, 2)
             if (staged_slot != x.pr.slot0 || staged_tile != tt) {
                 named_bar(1, kConsumers);
                 if (NMAT == 2)
-                    stage_act(s, p.xq, p.xd, p.xs, (size_t)p.H, (size_t)(p.H >> 5), p.perm_token,
+                    stage_act(s, p.xq, p.xd, p.xs, (size_t)(p.x_qstride ? p.x_qstride : p.H),
+                              (size_t)(p.x_dstride ? p.x_dstride : (p.H >> 5)), p.perm_token,
                               x.pr.slot0 + t0, nt, K);
                 else
                     stage_act(s, p.aq, p.ad, p.as, (size_t)p.W, (size_t)(p.W >> 5), nullptr, x.pr.slot0 + t0, nt,

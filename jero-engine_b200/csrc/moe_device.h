@@ -82,7 +82,9 @@ struct FwdParams {
     const float *logit_bias;     // [E] or null
     const float *sel_bias;       // [E] or null
 
-    int8_t *xq;                  // [T][H]
+    int8_t *xq;                  // [T][H] (row stride x_qstride bytes when set)
+    int x_qstride, x_dstride;    // 0: H and H/32. Expert-parallel inbox rows are packed
+                                 // [H int8 | H/32 d | H/32 s], read in place with these strides
     float *xd;                   // [T][H/32] block scale
     float *xs;                   // [T][H/32] block scale * block sum of quants
     float *logits;               // [T][E]

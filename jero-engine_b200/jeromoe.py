@@ -39,6 +39,7 @@ QUANT_NAMES = {F32: "F32", Q8_0: "Q8_0", Q4_K: "Q4_K"}
 ROUTE_SOFTMAX_TOPK, ROUTE_GROUP_LIMITED = 0, 1
 PTR_HOST, PTR_DEVICE = 0, 1
 FLAG_TENSOR_CORES_ALWAYS, FLAG_TENSOR_CORES_NEVER = 1, 2
+FLAG_EP_NCCL_ONLY = 4   # expert parallelism: NCCL exchange for every batch size
 TENSOR_CORE_MIN_TOKENS = 256
 
 

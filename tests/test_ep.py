@@ -57,8 +57,11 @@ def _ep_layer(cfg_id, over, flags, T):
     return cfg, d, keep, x
 
 
+# max_tokens <= 256 uses the exchange over peer memory, larger the NCCL one;
+# FLAG_EP_NCCL_ONLY keeps the NCCL exchange covered for small batches too.
 EP1_CASES = {
     "cfg2_stream": (2, dict(E=16, I=256, H=512), jm.FLAG_TENSOR_CORES_NEVER, 40, True),
+    "cfg2_stream_nccl": (2, dict(E=16, I=256, H=512), jm.FLAG_TENSOR_CORES_NEVER | jm.FLAG_EP_NCCL_ONLY, 40, True),
     "cfg3_shared_stream": (3, dict(E=16, k=4, I=384, S=512, H=512), jm.FLAG_TENSOR_CORES_NEVER, 33, True),
     "cfg2_tensor_cores": (2, dict(E=16, I=256, H=512), jm.FLAG_TENSOR_CORES_ALWAYS, 300, False),
     "cfg5_groups_shared_tc": (5, dict(E=32, k=6, I=256, S=512, H=512, n_groups=8, topk_groups=3),
@@ -69,9 +72,9 @@ EP1_CASES = {
 @pytest.mark.gpu
 @pytest.mark.parametrize("name", list(EP1_CASES))
 def test_gpu_ep_world_of_one_matches_forward(name):
-    """A world of one rank runs every step of the expert-parallel forward
-    (pack, NCCL send/recv to itself, unpack, experts writing at received rows,
-    return exchange): same routing and output as moe_forward."""
+    """A world of one rank runs every step of the expert-parallel forward (the
+    peer-memory exchange with itself, or NCCL send/recv to itself): same
+    routing and output as moe_forward, also on a second call."""
     cid, over, flags, T, exact = EP1_CASES[name]
     cfg, d, keep, x = _ep_layer(cid, over, flags, T)
     uid = jm.ep_unique_id()
@@ -80,12 +83,14 @@ def test_gpu_ep_world_of_one_matches_forward(name):
         ep.upload(0, d)
         ref.upload(0, d)
         out, si, sw = ep.forward_ep(0, x)
+        out2, _, _ = ep.forward_ep(0, x)
         r_out, r_si, r_sw = ref.forward(0, x)
         empty, _, _ = ep.forward_ep(0, x[:0])
         assert empty.shape == (0, cfg.H)
         assert ep.device_status() == 0
     np.testing.assert_array_equal(si, r_si)
     np.testing.assert_array_equal(sw, r_sw)
+    np.testing.assert_array_equal(out, out2)
     if exact:
         np.testing.assert_array_equal(out, r_out)
     else:
@@ -105,10 +110,12 @@ def test_gpu_ep_requires_init_and_split():
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("flags,exact", [(jm.FLAG_TENSOR_CORES_NEVER, True), (jm.FLAG_TENSOR_CORES_ALWAYS, False)])
+@pytest.mark.parametrize("flags,exact", [(jm.FLAG_TENSOR_CORES_NEVER, True),
+                                         (jm.FLAG_TENSOR_CORES_NEVER | jm.FLAG_EP_NCCL_ONLY, True),
+                                         (jm.FLAG_TENSOR_CORES_ALWAYS, False)])
 def test_gpu_ep_two_ranks(flags, exact):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     over = dict(E=16, k=4, I=384, S=512, H=512)
-    T = 300 if flags == jm.FLAG_TENSOR_CORES_ALWAYS else 40
+    T = 300 if flags & jm.FLAG_TENSOR_CORES_ALWAYS else 40
     mp.spawn(gpu_worker, args=(2, free_port(), 3, over, T, flags, exact), nprocs=2, join=True)
