@@ -351,6 +351,8 @@ __global__ void __launch_bounds__(kStreamThreads, 2)
     extern __shared__ __align__(128) uint8_t smem_raw[];
     const Smem s = carve(smem_raw, c);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    pdl_wait();      // launched as a dependent: routing / gate_up output is complete
+    pdl_trigger();
     // the launch's problems (routed, then the shared expert) and their cost prefix
     const int with_sh = (c.mode != 0 && p.S > 0) ? 1 : 0;
     const int nr = min(c.mode == 1 ? 0 : *p.n_active, c.max_q - with_sh);
@@ -581,6 +583,8 @@ __global__ void __launch_bounds__(256) combine_kernel(FwdParams p)
 {
     __shared__ long long s_pos[kMaxK];
     __shared__ float s_w[kMaxK];
+    pdl_wait();
+    pdl_trigger();
     const int k = p.k, H = p.H, mw = p.mask_words;
     for (int t = blockIdx.y; t < p.T; t += gridDim.y) {
         if (threadIdx.x < k) {
@@ -655,8 +659,7 @@ cudaError_t launch_stream(Kern kern, const FwdParams &p, const LayerDev &L, cons
         return err;
     if (per_sm < 1) return cudaErrorInvalidConfiguration;
     const int grid = upper < num_sms * per_sm ? upper : num_sms * per_sm;
-    kern<<<grid, kStreamThreads, sm, st>>>(p, L, c, maps);
-    return cudaGetLastError();
+    return launch_dependent(kern, dim3(grid), dim3(kStreamThreads), sm, st, p, L, c, maps);
 }
 
 // Ring geometry from the slice plan of the matrices the launch streams (the
@@ -732,7 +735,8 @@ cudaError_t launch_combine(const FwdParams &p, cudaStream_t st)
 {
     const int per = (p.H & 3) == 0 ? p.H / 4 : p.H;
     dim3 grid((per + 255) / 256 < 8 ? (per + 255) / 256 : 8, p.T < 65535 ? p.T : 65535);
-    combine_kernel<<<grid, 256, 0, st>>>(p);
+    cudaError_t e = launch_dependent(combine_kernel, grid, dim3(256), 0, st, p);
+    if (e != cudaSuccess) return e;
     return cudaGetLastError();
 }
 

@@ -26,6 +26,26 @@ struct StreamCfg {
 // (T <= 256) run it as one kernel; larger ones clear the expert masks, then
 // router, selection and scan kernels. Marks "routing" or "router"/"select".
 cudaError_t launch_routing(const FwdParams &p, cudaStream_t st, const Marker &mk);
+
+// Launch with programmatic stream serialization: the kernel may be scheduled
+// while its predecessor finishes, so it must call pdl_wait() before touching
+// memory (the decode-path kernels do so on entry).
+template <typename... KArgs, typename... Args>
+cudaError_t launch_dependent(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                             Args &&...args)
+{
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, static_cast<Args &&>(args)...);
+}
 // Routed and shared matrices can share one streaming launch when their slice plans match.
 bool stream_plans_match(const DevMatrix &a, const DevMatrix &b);
 cudaError_t launch_gate_up(const FwdParams &p, const LayerDev &L, const LayerMaps &maps, int mode, int num_sms,

@@ -62,6 +62,14 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t *bar, uint32_t pari
     return ok != 0;
 }
 
+// Programmatic dependent launch. A kernel launched with the programmatic
+// stream-serialization attribute may start while its predecessor in the stream
+// still runs: pdl_wait() returns once the predecessor grid has completed and
+// its memory is visible (at once when there is no such launch), and
+// pdl_trigger() lets the next such kernel start launching.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // Slot and phase of a ring of n stages. Consumers wait for the full barrier
 // of the slot with the phase's parity; producers wait for the empty barrier
 // with the opposite parity, which a fresh barrier reports complete, so the

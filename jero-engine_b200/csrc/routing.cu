@@ -5,6 +5,7 @@
 
 #include "common.cuh"
 #include "kernels.h"
+#include "ptx.cuh"
 
 namespace jmoe {
 namespace {
@@ -566,6 +567,8 @@ template <int TT, int NL>
 __global__ void __launch_bounds__(128) router_small_kernel(FwdParams p)
 {
     static_assert(TT == 4, "one selecting warp per token of the tile");
+    pdl_wait();      // launched as a dependent: the previous forward's last kernel is done
+    pdl_trigger();
     extern __shared__ float4 xs4[];   // [TT][H/4]
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int e = blockIdx.x * 4 + warp;
@@ -582,10 +585,15 @@ __global__ void __launch_bounds__(128) router_small_kernel(FwdParams p)
         const int h4 = lane + 32 * i;
         w[i] = h4 < n4 ? __ldg(wr + h4) : zero4;
     }
+    // the tile by asynchronous copies, all in flight at once (rows past the
+    // batch are zero-filled)
     for (int i = threadIdx.x; i < TT * n4; i += blockDim.x) {
         const int t = i / n4, c = i - t * n4;
-        xs4[i] = t < ntok ? __ldg(reinterpret_cast<const float4 *>(p.x + (size_t)(t0 + t) * H) + c) : zero4;
+        const bool ok = t < ntok;
+        cp_async16(xs4 + i, reinterpret_cast<const float4 *>(p.x + (size_t)(t0 + (ok ? t : 0)) * H) + c, ok);
     }
+    cp_async_commit();
+    cp_async_wait<0>();
     __syncthreads();
 
     float acc[TT];
@@ -776,8 +784,7 @@ cudaError_t launch_routing_small(const FwdParams &p, cudaStream_t st)
         if (dev >= 0 && dev < 64) opted[dev] = smem;
     }
     dim3 grid((p.E + 3) / 4, (p.T + TT - 1) / TT);
-    router_small_kernel<TT, NL><<<grid, 128, smem, st>>>(p);
-    return cudaGetLastError();
+    return launch_dependent(router_small_kernel<TT, NL>, grid, dim3(128), smem, st, p);
 }
 
 }  // namespace
