@@ -342,7 +342,8 @@ def run_ours(args):
     value = world * T * args.steps / (total_ms / 1e3)
     # the rank-0 kernels explain the rank-0 time; the slowest rank sets the value
     tc = "gate_up_tc" in prof
-    cands = ("gate_up_tc", "down_tc") if tc else ("gate_up", "down")
+    i8 = "gate_up_i8" in prof   # int8 tensor-core path: weight streaming at HBM rate, like the dp4a kernels
+    cands = ("gate_up_tc", "down_tc") if tc else (("gate_up_i8", "down_i8") if i8 else ("gate_up", "down"))
     rows_here = kb["routed_rows"]
     dom = max(cands, key=lambda k: prof.get(k, (0, 1))[0])
     dom_ms = prof[dom][0] / prof[dom][1]
@@ -356,11 +357,11 @@ def run_ours(args):
                     "peak_source": tpk_kind, "algorithmic_flops_per_launch": int(fl),
                     "operands": "f16 (weights dequantised from GGUF blocks in shared memory), f32 accumulate"}
     else:    # HBM-bound: algorithmic bytes of the dominant kernel per launch
-        achieved = kb[dom] / (dom_ms / 1e3) / 1e9
+        achieved = kb[dom.replace("_i8", "")] / (dom_ms / 1e3) / 1e9
         roofline = {"bound": "hbm", "kernel": dom, "achieved": round(achieved, 1), "peak": hbm,
                     "unit": "GB/s", "frac": round(achieved / hbm, 4),
                     "traffic": measured_traffic(f"{cfg.name} T={T}", dom),
-                    "peak_source": peak_kind, "algorithmic_bytes_per_launch": int(kb[dom])}
+                    "peak_source": peak_kind, "algorithmic_bytes_per_launch": int(kb[dom.replace("_i8", "")])}
     layer_ms = total_ms / args.steps
     kernels = {k: {"avg_us": round(1e3 * v[0] / v[1], 2), "launches": v[1]} for k, v in prof.items()}
     launches = sum(v[1] for v in prof.values())

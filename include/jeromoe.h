@@ -112,6 +112,16 @@ typedef struct moe_device_spec {
  * the peer-memory exchange (see moe_forward_ep). */
 #define MOE_FLAG_EP_NCCL_ONLY 4
 #define MOE_TENSOR_CORE_MIN_TOKENS 256
+/* Below MOE_TENSOR_CORE_MIN_TOKENS, forwards with at least
+ * MOE_INT8_TENSOR_CORE_MIN_TOKENS tokens run the experts on the tensor cores
+ * with integer operands (the GGUF quants and the int8 activation blocks,
+ * exact int32 block sums, f32 block scaling) when the layer has a shared
+ * expert, Q8_0 experts, or at least six routed rows per expert on average;
+ * other small batches run on the int8 weight-streaming kernels. These flags
+ * force one of the two. */
+#define MOE_FLAG_INT8_TENSOR_CORES_NEVER 8
+#define MOE_FLAG_INT8_TENSOR_CORES_ALWAYS 16
+#define MOE_INT8_TENSOR_CORE_MIN_TOKENS 16
 
 /* Memory the admission check compares against. The real inspector reads
  * cudaMemGetInfo on spec->device; tests pass a fixed one, as the reference's

@@ -446,6 +446,22 @@ bool tc_matrix_ok(const DevMatrix &m)
     return (m.type == FMT_Q4_K || m.type == FMT_Q8_0) && m.rows % 128 == 0 && m.cols % 64 == 0;
 }
 
+// Batches below the f16 tensor-core path: the int8 tensor-core path
+// (decode_tc.cu) from MOE_INT8_TENSOR_CORE_MIN_TOKENS tokens when the layer
+// has a shared expert (all T tokens on one expert, which the streaming kernels
+// re-stream per 8-token tile), Q8_0 experts, or at least six routed rows per
+// expert on average; the weight-streaming kernels otherwise. Measured on B200:
+// Qwen3-MoE Q4_K (E 128, top-8) streams faster up to 64 tokens (4 rows per
+// expert) and the tensor cores win from 128; Q8_0 and shared-expert layers
+// win on the tensor cores from 32 tokens.
+bool use_int8_tc(const moe_device_spec &spec, const LayerStore &L, int T, int rows)
+{
+    if (spec.flags & MOE_FLAG_INT8_TENSOR_CORES_NEVER) return false;
+    if (spec.flags & MOE_FLAG_INT8_TENSOR_CORES_ALWAYS) return true;
+    if (T < MOE_INT8_TENSOR_CORE_MIN_TOKENS) return false;
+    return L.S > 0 || L.dev.gate.type == FMT_Q8_0 || (int64_t)rows >= 6 * (int64_t)L.E;
+}
+
 bool use_tensor_cores(const moe_device_spec &spec, const LayerStore &L, const Scratch &s, int T)
 {
     if (!s.tc || (spec.flags & MOE_FLAG_TENSOR_CORES_NEVER)) return false;
@@ -491,6 +507,7 @@ FwdParams local_params(moe_ctx *ctx, const LayerStore &L, int T, int ptr_kind, c
     p.a16 = s.a16; p.a16dn = s.a16dn;
     p.a16_stride = s.H; p.a16dn_stride = s.W; p.slots_cap = s.slots_cap;
     p.use_tc = use_tensor_cores(ctx->spec, L, s, T);
+    p.use_dtc = !p.use_tc && use_int8_tc(ctx->spec, L, T, T * L.k) && decode_tc_ok(p, L.dev);
     return p;
 }
 
@@ -1299,10 +1316,17 @@ static int ep_forward_p2p(moe_ctx *ctx, LayerStore &L, FwdParams p, int T, int p
     pe.y = reinterpret_cast<float *>(A + l.o_y); pe.y_rows = nullptr;
     pe.err = s.err;
     pe.use_tc = 0;
-    if ((ce = launch_gate_up(pe, L.dev, L.maps, 0, ctx->num_sms, st)) != cudaSuccess) return cuda_fail(ctx, ce, "gate_up");
-    mk.mark("gate_up");
-    if ((ce = launch_down(pe, L.dev, L.maps, 0, ctx->num_sms, st)) != cudaSuccess) return cuda_fail(ctx, ce, "down");
-    mk.mark("down");
+    pe.use_dtc = use_int8_tc(ctx->spec, L, T, T * L.k) && decode_tc_ok(pe, L.dev);
+    if (pe.use_dtc) {
+        if ((ce = launch_decode_tc(pe, L.dev, L.maps, ctx->num_sms, mk, st)) != cudaSuccess)
+            return cuda_fail(ctx, ce, "experts (int8 tensor cores)");
+    } else {
+        if ((ce = launch_gate_up(pe, L.dev, L.maps, 0, ctx->num_sms, st)) != cudaSuccess)
+            return cuda_fail(ctx, ce, "gate_up");
+        mk.mark("gate_up");
+        if ((ce = launch_down(pe, L.dev, L.maps, 0, ctx->num_sms, st)) != cudaSuccess) return cuda_fail(ctx, ce, "down");
+        mk.mark("down");
+    }
     if ((ce = launch_ep_p2p_return(a, ctx->num_sms, st)) != cudaSuccess) return cuda_fail(ctx, ce, "ep return");
     mk.mark("ep_return");
 
@@ -1313,6 +1337,10 @@ static int ep_forward_p2p(moe_ctx *ctx, LayerStore &L, FwdParams p, int T, int p
             ps.n_active = misc + 12;   // a zero word: no routed problems in this pass
             if ((ce = launch_prefill(ps, L.dev, L.maps, ctx->num_sms, mk, st)) != cudaSuccess)
                 return cuda_fail(ctx, ce, "shared expert (tensor cores)");
+        } else if (p.use_dtc) {
+            if ((ce = launch_decode_tc(p, L.dev, L.maps, ctx->num_sms, Marker{nullptr, nullptr}, st, true)) !=
+                cudaSuccess)
+                return cuda_fail(ctx, ce, "shared expert (int8 tensor cores)");
         } else {
             if ((ce = launch_gate_up(p, L.dev, L.maps, 1, ctx->num_sms, st)) != cudaSuccess)
                 return cuda_fail(ctx, ce, "shared gate_up");
@@ -1468,9 +1496,13 @@ int moe_forward_ep(moe_ctx *ctx, int32_t layer, int32_t T, const float *x, float
         Scratch tcs{};
         tcs.tc = ep.tc;
         pe.use_tc = use_tensor_cores(ctx->spec, L, tcs, plan.n_recv);
+        pe.use_dtc = !pe.use_tc && use_int8_tc(ctx->spec, L, T, T * L.k) && decode_tc_ok(pe, L.dev);
         if (pe.use_tc) {
             if ((ce = launch_prefill(pe, L.dev, L.maps, ctx->num_sms, mk, st)) != cudaSuccess)
                 return cuda_fail(ctx, ce, "experts (tensor cores)");
+        } else if (pe.use_dtc) {
+            if ((ce = launch_decode_tc(pe, L.dev, L.maps, ctx->num_sms, mk, st)) != cudaSuccess)
+                return cuda_fail(ctx, ce, "experts (int8 tensor cores)");
         } else {
             if ((ce = launch_gate_up(pe, L.dev, L.maps, 0, ctx->num_sms, st)) != cudaSuccess)
                 return cuda_fail(ctx, ce, "gate_up");
@@ -1506,6 +1538,11 @@ int moe_forward_ep(moe_ctx *ctx, int32_t layer, int32_t T, const float *x, float
                 const Marker smk{mk.fn ? &shared_mark_cb : nullptr, const_cast<Marker *>(&mk)};
                 if ((ce = launch_prefill(ps, L.dev, L.maps, ctx->num_sms, smk, st)) != cudaSuccess)
                     return cuda_fail(ctx, ce, "shared expert (tensor cores)");
+            } else if (p.use_dtc) {
+                if ((ce = launch_decode_tc(p, L.dev, L.maps, ctx->num_sms, Marker{nullptr, nullptr}, st, true)) !=
+                    cudaSuccess)
+                    return cuda_fail(ctx, ce, "shared expert (int8 tensor cores)");
+                mk.mark("shared");
             } else {
                 if ((ce = launch_gate_up(p, L.dev, L.maps, 1, ctx->num_sms, st)) != cudaSuccess)
                     return cuda_fail(ctx, ce, "shared gate_up");

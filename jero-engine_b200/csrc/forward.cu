@@ -24,6 +24,12 @@ int launch_forward(const FwdParams &p, const LayerDev &L, const LayerMaps &maps,
         mk.mark("combine");
         return cudaSuccess;
     }
+    if (p.use_dtc) {
+        if ((err = launch_decode_tc(p, L, maps, num_sms, mk, st)) != cudaSuccess) return err;
+        if ((err = launch_combine(p, st)) != cudaSuccess) return err;
+        mk.mark("combine");
+        return cudaSuccess;
+    }
     const bool has_sh = p.S > 0;
     // one launch covers routed and shared problems when they share a format and slice plan
     const bool same_gu = has_sh && stream_plans_match(L.sh_gate, L.gate);

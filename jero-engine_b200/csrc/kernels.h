@@ -59,6 +59,14 @@ cudaError_t launch_combine(const FwdParams &p, cudaStream_t st);
 cudaError_t launch_prefill(const FwdParams &p, const LayerDev &L, const LayerMaps &maps, int num_sms,
                            const Marker &mk, cudaStream_t st);
 
+// Tensor-core expert path with integer operands for small batches: the gate/up
+// and down launches (routed problems, plus the shared expert when p.S > 0), or
+// the shared expert alone. decode_tc_ok: the layer's formats, shapes and
+// buffers suit it.
+bool decode_tc_ok(const FwdParams &p, const LayerDev &L);
+cudaError_t launch_decode_tc(const FwdParams &p, const LayerDev &L, const LayerMaps &maps, int num_sms,
+                             const Marker &mk, cudaStream_t st, bool shared_only = false);
+
 // Expert-parallel exchange (ep.cu): bytes of one packed token row, and the
 // pack / unpack / receive-plan kernels.
 size_t ep_row_bytes(int H);

@@ -75,7 +75,8 @@ struct FwdParams {
     int mask_words;              // ceil(T/32)
     int quant_x;                 // x needs int8 blocks (some gate/up matrix is quantised)
     int max_problems;            // grid.y of the expert kernels
-    int use_tc;                  // experts on the tensor-core path (prefill.cu)
+    int use_tc;                  // experts on the f16 tensor-core path (prefill.cu)
+    int use_dtc;                 // experts on the int8 tensor-core path (decode_tc.cu)
 
     const float *x;              // [T][H]
     const float *router;         // [E][H]

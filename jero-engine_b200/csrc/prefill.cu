@@ -26,6 +26,7 @@
 #include "common.cuh"
 #include "kernels.h"
 #include "ptx.cuh"
+#include "tc_common.cuh"
 
 namespace jmoe {
 namespace {
@@ -38,8 +39,6 @@ constexpr int kWarpTma = 0, kWarpMma = 1, kDeqWarp0 = 2, kDeqWarps = 8, kEpiWarp
 constexpr int kTcThreads = (kEpiWarp0 + kEpiWarps) * 32;
 constexpr int kMaxStages = 6;
 constexpr int kTmemCols = 512, kAccCols = 256;  // two accumulator buffers of 256 columns
-constexpr long long kWaitCycles = 4000000000LL;
-constexpr int kErrTimeout = 1;
 constexpr int kWTileBytes = kM * 128;           // dequantised weights: one matrix, one K step (16 KB)
 constexpr int kQuantBox = kM * 128;             // quants of one matrix per quantised stage (16 KB)
 constexpr int kQBytes = kQuantBox + kM * 16;    // + 16 bytes of scales per row (18 KB)
@@ -59,66 +58,6 @@ struct TcMaps {
     CUtensorMap sq[2], sm[2];             // shared expert weights
 };
 
-// Waiting warps sleep in try_wait (suspend hint) instead of spinning, so they
-// leave the issue slots to the dequant and epilogue warps; the abort flag and
-// the clock are checked only when a try_wait times out.
-constexpr uint32_t kSleepNs = 20000;
-
-__device__ __forceinline__ bool tc_wait(uint64_t *bar, uint32_t parity, volatile int *abort_flag, int *err)
-{
-    if (mbar_try_wait(bar, parity)) return true;
-    const long long t0 = clock64();
-    while (!mbar_try_wait_sleep(bar, parity, kSleepNs)) {
-        if (*abort_flag) return false;
-        if (clock64() - t0 > kWaitCycles) {
-            *abort_flag = 1;
-            atomicExch(err, kErrTimeout);
-            return false;
-        }
-    }
-    return true;
-}
-
-// Bounded wait used while draining after an abort (no error recorded).
-__device__ __forceinline__ void drain_wait(uint64_t *bar, uint32_t parity)
-{
-    const long long t0 = clock64();
-    while (!mbar_try_wait_sleep(bar, parity, kSleepNs) && clock64() - t0 < kWaitCycles) {}
-}
-
-struct TcItem {
-    int expert, slot, n, nt;   // n: slots of this item (1..cap)
-    bool shared;
-};
-
-// Slot chunks of a problem: ceil(count / cap) chunks of equal size rounded up
-// to 16 (the MMA's N granularity); the last one takes the remainder.
-__device__ __forceinline__ int chunk_count(int count, int cap) { return (count + cap - 1) / cap; }
-__device__ __forceinline__ int chunk_size(int count, int nch) { return (((count + nch - 1) / nch) + 15) & ~15; }
-
-// The item table lives in shared memory: s_off[0..nq] is the first item of
-// each problem of the launch (routed problems in list order, then the shared
-// expert), s_prob[q] = (expert, slot0, count, is_shared).
-__device__ __forceinline__ TcItem tc_item(const int *s_off, const int4 *s_prob, int nq, int cap, int it)
-{
-    int lo = 0, hi = nq - 1;
-    while (lo < hi) {
-        const int mid = (lo + hi + 1) >> 1;
-        if (s_off[mid] <= it) lo = mid;
-        else hi = mid - 1;
-    }
-    const int4 pr = s_prob[lo];
-    const int nch = chunk_count(pr.z, cap), base = chunk_size(pr.z, nch);
-    const int local = it - s_off[lo];
-    const int ch = local % nch;
-    TcItem x;
-    x.nt = local / nch;
-    x.expert = pr.x;
-    x.slot = pr.y + ch * base;
-    x.n = min(base, pr.z - ch * base);
-    x.shared = pr.w != 0;
-    return x;
-}
 
 // Output position of K index f within its group of four: (0, 2, 1, 3).
 __device__ __forceinline__ int k_perm(int f) { return (f & ~3) | ((f & 1) << 1) | ((f >> 1) & 1); }
@@ -158,11 +97,6 @@ __device__ __forceinline__ void q8_word_f16(uint32_t w, __half2 d, uint32_t &o0,
     o1 = h2_bits(__hmul2(o, d));
 }
 
-__device__ __forceinline__ void sts128(uint32_t a, uint4 v)
-{
-    asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
-                 : "memory");
-}
 
 template <int FMT, int NMAT>
 __global__ void __launch_bounds__(kTcThreads, 1)

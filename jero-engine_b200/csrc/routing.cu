@@ -463,15 +463,6 @@ __device__ void build_permutation_small(const FwdParams &p)
 // rows by 4x and of the token rows by 2x against per-warp global loads.
 constexpr int kRtTok = 32, kRtExp = 32, kRtChunk4 = 64;   // chunk: 64 float4 = 256 values
 
-__device__ __forceinline__ void cp_async16(void *smem, const void *gmem, bool valid)
-{
-    const uint32_t s = (uint32_t)__cvta_generic_to_shared(smem);
-    const int n = valid ? 16 : 0;   // 0: zero fill, nothing read
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(s), "l"(gmem), "r"(n) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
 __global__ void __launch_bounds__(512, 1) router_tiled_kernel(FwdParams p)
 {

@@ -40,6 +40,8 @@ ROUTE_SOFTMAX_TOPK, ROUTE_GROUP_LIMITED = 0, 1
 PTR_HOST, PTR_DEVICE = 0, 1
 FLAG_TENSOR_CORES_ALWAYS, FLAG_TENSOR_CORES_NEVER = 1, 2
 FLAG_EP_NCCL_ONLY = 4   # expert parallelism: NCCL exchange for every batch size
+# small batches: int8 weight-streaming kernels only / int8 tensor cores for every size below the f16 path
+FLAG_INT8_TENSOR_CORES_NEVER, FLAG_INT8_TENSOR_CORES_ALWAYS = 8, 16
 TENSOR_CORE_MIN_TOKENS = 256
 
 

@@ -209,6 +209,41 @@ def test_gpu_tensor_core_matches_streaming_path():
     assert row_rel_err(outs[0][0], outs[1][0]).max() <= OUT_TOL
 
 
+# ---------------------------------- int8 tensor-core path (small batches)
+
+@pytest.mark.parametrize("name", list(TC_CASES))
+@pytest.mark.parametrize("T", [1, 5, 33, 100])
+def test_gpu_int8_tensor_core_path(name, T):
+    """The same small layers forced onto the int8 tensor-core path (exact
+    int32 block sums from tcgen05 kind::i8, f32 block scaling) and onto the
+    dp4a streaming path: same routing, both within the contract tolerance of
+    the oracle, and the int8 path is the one that ran."""
+    cid, over = TC_CASES[name]
+    cfg = synth.CONFIGS[cid].scaled(**over)
+    w = synth.build_weights(cfg)
+    x = synth.gen_x(cfg, T)
+    ref = oracle_layer(w, cfg).forward(x, 8)
+    outs = []
+    for flags in (jm.FLAG_INT8_TENSOR_CORES_ALWAYS, jm.FLAG_INT8_TENSOR_CORES_NEVER):
+        with gpu_layer(w, cfg.E, cfg.k, cfg.I, cfg.S > 0, cfg.route, cfg.H, T, flags=flags) as ctx:
+            ctx.set_profiling(True)
+            outs.append(ctx.forward(0, x))
+            prof, _ = ctx.profile_read()
+            assert ctx.device_status() == 0
+        assert ("gate_up_i8" in prof) == (flags == jm.FLAG_INT8_TENSOR_CORES_ALWAYS), sorted(prof)
+        assert_parity(*outs[-1], *ref)
+    np.testing.assert_array_equal(outs[0][1], outs[1][1])
+    assert row_rel_err(outs[0][0], outs[1][0]).max() <= OUT_TOL
+
+
+@pytest.mark.parametrize("cid,T", [(3, 64), (5, 64), (1, 17)])
+def test_gpu_int8_tensor_core_full_size(cid, T):
+    """Full-size layers at decode batch sizes on the default path (the int8
+    tensor cores from MOE_INT8_TENSOR_CORE_MIN_TOKENS tokens): shared experts,
+    group-limited routing and Q8_0 weights."""
+    _full_size_parity(cid, T, sample=16)
+
+
 # ------------------------------------------------------------- edge cases
 
 def _small_cfg(**kw):
