@@ -613,14 +613,27 @@ __global__ void __launch_bounds__(256) combine_kernel(FwdParams p)
                     const float4 s = reinterpret_cast<const float4 *>(p.y + shared_row * H)[h4];
                     v = make_float4(__fadd_rn(v.x, s.x), __fadd_rn(v.y, s.y), __fadd_rn(v.z, s.z), __fadd_rn(v.w, s.w));
                 }
-                for (int r = 0; r < k; r++) {
-                    if (s_pos[r] < 0) continue;
-                    const float w = s_w[r];
-                    const float4 y = reinterpret_cast<const float4 *>(p.y + (size_t)s_pos[r] * H)[h4];
-                    v.x = __fadd_rn(v.x, __fmul_rn(w, y.x));
-                    v.y = __fadd_rn(v.y, __fmul_rn(w, y.y));
-                    v.z = __fadd_rn(v.z, __fmul_rn(w, y.z));
-                    v.w = __fadd_rn(v.w, __fmul_rn(w, y.w));
+                // all rows' loads in flight first (8 at a time), then the adds in rank order
+                for (int r0 = 0; r0 < k; r0 += 8) {
+                    float4 yv[8];
+#pragma unroll
+                    for (int i = 0; i < 8; i++) {
+                        const int r = r0 + i;
+                        yv[i] = (r < k && s_pos[r] >= 0)
+                                    ? reinterpret_cast<const float4 *>(p.y + (size_t)s_pos[r] * H)[h4]
+                                    : make_float4(0.f, 0.f, 0.f, 0.f);
+                    }
+#pragma unroll
+                    for (int i = 0; i < 8; i++) {
+                        const int r = r0 + i;
+                        if (r < k && s_pos[r] >= 0) {
+                            const float w = s_w[r];
+                            v.x = __fadd_rn(v.x, __fmul_rn(w, yv[i].x));
+                            v.y = __fadd_rn(v.y, __fmul_rn(w, yv[i].y));
+                            v.z = __fadd_rn(v.z, __fmul_rn(w, yv[i].z));
+                            v.w = __fadd_rn(v.w, __fmul_rn(w, yv[i].w));
+                        }
+                    }
                 }
                 reinterpret_cast<float4 *>(p.out + (size_t)t * H)[h4] = v;
             }

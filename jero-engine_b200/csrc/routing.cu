@@ -210,45 +210,37 @@ __device__ __forceinline__ void select_token(const FwdParams &p, int t, int lane
         k = min(k, p.topk_groups * gs);
     }
 
-    // rank of each candidate among the candidates
-    int32_t ckey[NL];
-    int rank[NL];
+    // k rounds of a warp argmax over the candidates. Each candidate is packed
+    // as (key in unsigned order) << 32 | (0xFFFFFFFF - expert), so the 64-bit
+    // maximum is the largest key with ties to the lower index; non-candidates
+    // are 0. Round r's winner is the r-th choice; its owner lane clears it.
+    uint64_t pk[NL];
 #pragma unroll
-    for (int i = 0; i < NL; i++) {
-        ckey[i] = cand[i] ? key[i] : INT32_MIN;   // below every candidate's key
-        rank[i] = 0;
-    }
-    const int nlane = (E + 31) >> 5;
-#pragma unroll
-    for (int j = 0; j < NL; j++) {
-        if (j >= nlane) break;
-#pragma unroll 4
-        for (int src = 0; src < 32; src++) {
-            const int32_t ok = __shfl_sync(0xffffffffu, ckey[j], src);
-            const int oe = src + 32 * j;
-#pragma unroll
-            for (int i = 0; i < NL; i++)
-                if (rank_before(ok, oe, ckey[i], lane + 32 * i)) rank[i]++;
-        }
-    }
-
-    // lane r collects the r-th choice
+    for (int i = 0; i < NL; i++)
+        pk[i] = cand[i] ? ((uint64_t)((uint32_t)key[i] ^ 0x80000000u) << 32) |
+                              (uint64_t)(0xFFFFFFFFu - (uint32_t)(lane + 32 * i))
+                        : 0ull;
     int my_e = -1;
     float my_w = 0.0f;
     int nsel = 0;
     for (int r = 0; r < k; r++) {
-        int has = -1;
+        uint64_t loc = pk[0];
+#pragma unroll
+        for (int i = 1; i < NL; i++) loc = pk[i] > loc ? pk[i] : loc;
+        const uint32_t hi = __reduce_max_sync(0xffffffffu, (uint32_t)(loc >> 32));
+        const uint32_t lo = __reduce_max_sync(0xffffffffu, (uint32_t)(loc >> 32) == hi ? (uint32_t)loc : 0u);
+        if (hi == 0u && lo == 0u) break;   // fewer candidates than k
+        const int e = (int)(0xFFFFFFFFu - lo);
         float hp = 0.0f;
 #pragma unroll
         for (int i = 0; i < NL; i++)
-            if (cand[i] && rank[i] == r) { has = lane + 32 * i; hp = pv[i]; }
-        const uint32_t b = __ballot_sync(0xffffffffu, has >= 0);
-        if (!b) break;
-        const int src = __ffs(b) - 1;
-        const int bi = __shfl_sync(0xffffffffu, has, src);
-        const float bp = __shfl_sync(0xffffffffu, hp, src);
+            if (lane + 32 * i == e) {
+                pk[i] = 0ull;
+                hp = pv[i];
+            }
+        const float bp = __shfl_sync(0xffffffffu, hp, e & 31);
         if (lane == r) {
-            my_e = bi;
+            my_e = e;
             if (p.sel_bias) my_w = sum_ok ? __fdiv_rn(bp, psum) : 0.0f;
             else my_w = sum_ok ? __fdiv_rn(bp, psum) : __fdiv_rn(1.0f, (float)E);
         }
