@@ -59,10 +59,18 @@ def _ep_layer(cfg_id, over, flags, T):
 
 # max_tokens <= 256 uses the exchange over peer memory, larger the NCCL one;
 # FLAG_EP_NCCL_ONLY keeps the NCCL exchange covered for small batches too.
+# STREAM / INT8 pin the expert path of small batches (streaming kernels or
+# int8 tensor cores); both are deterministic, so EP equals moe_forward bit
+# for bit on them.
+STREAM = jm.FLAG_TENSOR_CORES_NEVER | jm.FLAG_INT8_TENSOR_CORES_NEVER
+INT8 = jm.FLAG_TENSOR_CORES_NEVER | jm.FLAG_INT8_TENSOR_CORES_ALWAYS
 EP1_CASES = {
-    "cfg2_stream": (2, dict(E=16, I=256, H=512), jm.FLAG_TENSOR_CORES_NEVER, 40, True),
-    "cfg2_stream_nccl": (2, dict(E=16, I=256, H=512), jm.FLAG_TENSOR_CORES_NEVER | jm.FLAG_EP_NCCL_ONLY, 40, True),
-    "cfg3_shared_stream": (3, dict(E=16, k=4, I=384, S=512, H=512), jm.FLAG_TENSOR_CORES_NEVER, 33, True),
+    "cfg2_stream": (2, dict(E=16, I=256, H=512), STREAM, 40, True),
+    "cfg2_stream_nccl": (2, dict(E=16, I=256, H=512), STREAM | jm.FLAG_EP_NCCL_ONLY, 40, True),
+    "cfg3_shared_stream": (3, dict(E=16, k=4, I=384, S=512, H=512), STREAM, 33, True),
+    "cfg2_int8": (2, dict(E=16, I=256, H=512), INT8, 40, True),
+    "cfg3_shared_int8_nccl": (3, dict(E=16, k=4, I=384, S=512, H=512), INT8 | jm.FLAG_EP_NCCL_ONLY, 33, True),
+    "cfg5_groups_shared_int8": (5, dict(E=32, k=6, I=256, S=512, H=512, n_groups=8, topk_groups=3), INT8, 64, True),
     "cfg2_tensor_cores": (2, dict(E=16, I=256, H=512), jm.FLAG_TENSOR_CORES_ALWAYS, 300, False),
     "cfg5_groups_shared_tc": (5, dict(E=32, k=6, I=256, S=512, H=512, n_groups=8, topk_groups=3),
                               jm.FLAG_TENSOR_CORES_ALWAYS, 260, False),
@@ -110,8 +118,9 @@ def test_gpu_ep_requires_init_and_split():
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("flags,exact", [(jm.FLAG_TENSOR_CORES_NEVER, True),
-                                         (jm.FLAG_TENSOR_CORES_NEVER | jm.FLAG_EP_NCCL_ONLY, True),
+@pytest.mark.parametrize("flags,exact", [(STREAM, True),
+                                         (STREAM | jm.FLAG_EP_NCCL_ONLY, True),
+                                         (INT8, True),
                                          (jm.FLAG_TENSOR_CORES_ALWAYS, False)])
 def test_gpu_ep_two_ranks(flags, exact):
     if torch.cuda.device_count() < 2:

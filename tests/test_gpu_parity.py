@@ -202,7 +202,7 @@ def test_gpu_tensor_core_matches_streaming_path():
     w = synth.build_weights(cfg)
     x = synth.gen_x(cfg, 200)
     outs = []
-    for flags in (jm.FLAG_TENSOR_CORES_ALWAYS, jm.FLAG_TENSOR_CORES_NEVER):
+    for flags in (jm.FLAG_TENSOR_CORES_ALWAYS, jm.FLAG_TENSOR_CORES_NEVER | jm.FLAG_INT8_TENSOR_CORES_NEVER):
         with gpu_layer(w, cfg.E, cfg.k, cfg.I, False, cfg.route, cfg.H, 200, flags=flags) as ctx:
             outs.append(ctx.forward(0, x))
     np.testing.assert_array_equal(outs[0][1], outs[1][1])
