@@ -24,16 +24,16 @@
 //   1       MMA issue (one thread); owns the 512 TMEM columns
 //   2..5    helpers, thread = weight row (its TMEM lane): Q4_K nibbles -> u8
 //           A operand, block scales decoded to f32, and chunks of the slot
-//           rows of the activation operand (cp.async, two K steps ahead)
+//           rows of the activation operand (cp.async, six K steps ahead)
 //   6..13   epilogue, thread = TMEM lane = weight row, in two warpgroups:
 //           gate/up: one matrix each, the up sums handed to the gate group
 //           for SwiGLU; down: two blocks of each K step each, the partial
 //           sums of the second group added by the first
 // Rings: quant stages (TMA -> helpers, and for Q8_0 the MMA operand itself),
-// A stages in TMEM (helpers -> MMA, Q4_K), activation + scales (helpers -> MMA
-// and epilogue, freed by the epilogue), accumulator stages in TMEM (MMA ->
-// epilogue). Every wait is bounded; a timeout sets the context's error word
-// and the CTA drains.
+// A stages in TMEM (helpers -> MMA, Q4_K), activation rows + their scales
+// (helpers -> MMA and epilogue), weight scales (helpers -> epilogue), both
+// freed by the epilogue, accumulator stages in TMEM (MMA -> epilogue). Every
+// wait is bounded; a timeout sets the context's error word and the CTA drains.
 //
 // Semantics followed: the per-token expert FFN of dispatch_qwen3_moe_ffn
 // (src/qwen_deepseek.rs:847-951) over GGUF Q4_K / Q8_0 weights, with the
