@@ -187,6 +187,24 @@ int moe_layer_upload(moe_ctx *ctx, int32_t layer, const moe_layer_desc *desc);
 int moe_forward(moe_ctx *ctx, int32_t layer, int32_t T, const float *x, float *out,
                 int32_t *sel_idx, float *sel_w, int32_t ptr_kind);
 
+/* The FFN pre-norm of an uploaded layer for moe_forward_block: the RMSNorm
+ * weight [H] f32 in host memory (blk.L.ffn_norm.weight) and eps. NULL weight,
+ * or a non-finite entry, reads as 1.0, as read_f32_weight_or_default does
+ * (src/qwen_deepseek.rs:491-519, used at :1279-1284). A re-upload of the layer
+ * drops the norm. */
+int moe_layer_set_ffn_norm(moe_ctx *ctx, int32_t layer, const float *weight, float eps);
+
+/* The FFN sublayer around the MoE block for T tokens of the residual stream:
+ * out = hidden + MoE(rmsnorm(hidden, ffn_norm, eps)), the reference's
+ * src/qwen_deepseek.rs:1279-1306 (rmsnorm_standard, dispatch_qwen3_moe_ffn,
+ * hidden += ffn_out) for a MoE layer, without the host round trip between
+ * the norm, the block and the residual add. out may equal hidden. The norm
+ * uses a fixed f32 order (lane partials (h/4) mod 32 of x*x as fmaf chains,
+ * xor butterfly, mean, + eps, 1/sqrt, x * inv * w), the same in the oracle;
+ * the reference kernel's order is not visible. Needs moe_layer_set_ffn_norm. */
+int moe_forward_block(moe_ctx *ctx, int32_t layer, int32_t T, const float *hidden, float *out,
+                      int32_t *sel_idx, float *sel_w, int32_t ptr_kind);
+
 int moe_residency_summary(const moe_ctx *ctx, moe_residency *out);
 
 /* Reads and clears the device status word of ctx (synchronises the context

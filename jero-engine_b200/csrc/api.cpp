@@ -9,6 +9,7 @@
 #include <memory>
 #include <mutex>
 #include <string>
+#include <cmath>
 #include <vector>
 
 #include "../../include/jeromoe.h"
@@ -37,6 +38,8 @@ struct LayerStore {
     void *block = nullptr;          // one cudaMalloc for the whole layer
     size_t block_bytes = 0, gguf_bytes = 0;
     const float *router = nullptr, *logit_bias = nullptr, *sel_bias = nullptr;
+    float *ffn_norm = nullptr;      // moe_layer_set_ffn_norm: RMSNorm weight [H] (own allocation)
+    float norm_eps = 0.0f;
     LayerDev dev{};
     LayerMaps maps{};
 };
@@ -475,6 +478,7 @@ bool use_tensor_cores(const moe_device_spec &spec, const LayerStore &L, const Sc
 void free_layer(LayerStore &L)
 {
     if (L.block) cudaFree(L.block);
+    if (L.ffn_norm) cudaFree(L.ffn_norm);
     L = LayerStore{};
 }
 
@@ -989,8 +993,9 @@ int moe_layer_upload(moe_ctx *ctx, int32_t layer, const moe_layer_desc *desc)
     return MOE_OK;
 }
 
-int moe_forward(moe_ctx *ctx, int32_t layer, int32_t T, const float *x, float *out, int32_t *sel_idx,
-                float *sel_w, int32_t ptr_kind)
+// moe_forward, and with block = true moe_forward_block: out = x + block(rmsnorm(x)).
+static int forward_impl(moe_ctx *ctx, int32_t layer, int32_t T, const float *x, float *out, int32_t *sel_idx,
+                        float *sel_w, int32_t ptr_kind, bool block)
 {
     if (!ctx) return fail(nullptr, MOE_ERR_INVALID_ARGS, "null context");
     if (layer < 0 || layer >= (int)ctx->layers.size())
@@ -1006,13 +1011,31 @@ int moe_forward(moe_ctx *ctx, int32_t layer, int32_t T, const float *x, float *o
     if (!x || !out) return fail(ctx, MOE_ERR_INVALID_ARGS, "null x or out");
     if (ptr_kind == MOE_PTR_DEVICE && (((uintptr_t)x | (uintptr_t)out) & 15))
         return fail(ctx, MOE_ERR_INVALID_ARGS, "device x and out must be 16-byte aligned");
+    if (block && !L.ffn_norm)
+        return fail(ctx, MOE_ERR_INVALID_ARGS, "layer %d has no ffn_norm (moe_layer_set_ffn_norm)", layer);
     CUDA_TRY(ctx, cudaSetDevice(ctx->spec.device), "cudaSetDevice");
     Scratch &s = ctx->scratch;
     cudaStream_t st = ctx->stream;
     FwdParams p = local_params(ctx, L, T, ptr_kind, x, out, sel_idx, sel_w);
 
-    if (ptr_kind == MOE_PTR_HOST)
+    if (block) {
+        // host: the residual stream goes to s.out, which the combine updates in
+        // place; device: read from x, written to out (which may be x). The
+        // normalised tokens go to s.x, the routing's input.
+        const float *hidden = x;
+        if (ptr_kind == MOE_PTR_HOST) {
+            CUDA_TRY(ctx, cudaMemcpyAsync(s.out, x, (size_t)T * L.H * 4, cudaMemcpyHostToDevice, st), "copy hidden");
+            hidden = s.out;
+        }
+        p.norm_in = hidden;
+        p.norm_out = s.x;
+        p.norm_w = L.ffn_norm;
+        p.norm_eps = L.norm_eps;
+        p.residual = hidden;
+        p.x = s.x;
+    } else if (ptr_kind == MOE_PTR_HOST) {
         CUDA_TRY(ctx, cudaMemcpyAsync(s.x, x, (size_t)T * L.H * 4, cudaMemcpyHostToDevice, st), "copy x");
+    }
     Marker mk{nullptr, nullptr};
     if (ctx->prof.on) {
         ctx->prof.stream = st;
@@ -1039,6 +1062,38 @@ int moe_forward(moe_ctx *ctx, int32_t layer, int32_t T, const float *x, float *o
                         *ctx->status_host);
         }
     }
+    return MOE_OK;
+}
+
+int moe_forward(moe_ctx *ctx, int32_t layer, int32_t T, const float *x, float *out, int32_t *sel_idx,
+                float *sel_w, int32_t ptr_kind)
+{
+    return forward_impl(ctx, layer, T, x, out, sel_idx, sel_w, ptr_kind, false);
+}
+
+int moe_forward_block(moe_ctx *ctx, int32_t layer, int32_t T, const float *hidden, float *out, int32_t *sel_idx,
+                      float *sel_w, int32_t ptr_kind)
+{
+    return forward_impl(ctx, layer, T, hidden, out, sel_idx, sel_w, ptr_kind, true);
+}
+
+int moe_layer_set_ffn_norm(moe_ctx *ctx, int32_t layer, const float *weight, float eps)
+{
+    if (!ctx) return fail(nullptr, MOE_ERR_INVALID_ARGS, "null context");
+    if (layer < 0 || layer >= (int)ctx->layers.size())
+        return fail(ctx, MOE_ERR_INVALID_ARGS, "layer %d outside 0..%d", layer, (int)ctx->layers.size() - 1);
+    LayerStore &L = ctx->layers[layer];
+    if (!L.present) return fail(ctx, MOE_ERR_NOT_UPLOADED, "layer %d was never uploaded", layer);
+    if (!std::isfinite(eps) || eps < 0.0f) return fail(ctx, MOE_ERR_INVALID_ARGS, "eps must be finite and >= 0");
+    // missing or non-finite weights read as 1.0 (read_f32_weight_or_default)
+    std::vector<float> w((size_t)L.H, 1.0f);
+    if (weight)
+        for (int h = 0; h < L.H; h++)
+            if (std::isfinite(weight[h])) w[h] = weight[h];
+    CUDA_TRY(ctx, cudaSetDevice(ctx->spec.device), "cudaSetDevice");
+    if (!L.ffn_norm) CUDA_TRY(ctx, cudaMalloc(&L.ffn_norm, (size_t)L.H * 4), "ffn_norm allocation");
+    CUDA_TRY(ctx, cudaMemcpy(L.ffn_norm, w.data(), (size_t)L.H * 4, cudaMemcpyHostToDevice), "copy ffn_norm");
+    L.norm_eps = eps;
     return MOE_OK;
 }
 

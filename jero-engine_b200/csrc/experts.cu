@@ -635,6 +635,10 @@ __global__ void __launch_bounds__(256) combine_kernel(FwdParams p)
                         }
                     }
                 }
+                if (p.residual) {   // hidden += ffn_out (src/qwen_deepseek.rs:1304-1306)
+                    const float4 r = reinterpret_cast<const float4 *>(p.residual + (size_t)t * H)[h4];
+                    v = make_float4(__fadd_rn(r.x, v.x), __fadd_rn(r.y, v.y), __fadd_rn(r.z, v.z), __fadd_rn(r.w, v.w));
+                }
                 reinterpret_cast<float4 *>(p.out + (size_t)t * H)[h4] = v;
             }
         } else {
@@ -643,6 +647,7 @@ __global__ void __launch_bounds__(256) combine_kernel(FwdParams p)
                 if (p.S > 0) v = __fadd_rn(v, p.y[shared_row * H + h]);
                 for (int r = 0; r < k; r++)
                     if (s_pos[r] >= 0) v = __fadd_rn(v, __fmul_rn(s_w[r], p.y[(size_t)s_pos[r] * H + h]));
+                if (p.residual) v = __fadd_rn(p.residual[(size_t)t * H + h], v);
                 p.out[(size_t)t * H + h] = v;
             }
         }

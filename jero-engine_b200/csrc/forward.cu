@@ -16,6 +16,10 @@ int launch_forward(const FwdParams &p, const LayerDev &L, const LayerMaps &maps,
     cudaError_t err;
     if (p.T == 0) return cudaSuccess;
     mk.mark(nullptr);
+    if (p.norm_in) {
+        if ((err = launch_rmsnorm(p, st)) != cudaSuccess) return err;
+        mk.mark("ffn_norm");
+    }
     if ((err = launch_routing(p, st, mk)) != cudaSuccess) return err;
 
     if (p.use_tc) {

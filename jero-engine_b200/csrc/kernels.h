@@ -54,6 +54,9 @@ cudaError_t launch_down(const FwdParams &p, const LayerDev &L, const LayerMaps &
                         cudaStream_t st);
 cudaError_t launch_combine(const FwdParams &p, cudaStream_t st);
 
+// RMSNorm of the T rows of p.norm_in into p.norm_out (moe_forward_block).
+cudaError_t launch_rmsnorm(const FwdParams &p, cudaStream_t st);
+
 // Tensor-core expert path (gather of the f16 operand, item plan, gate/up and
 // down GEMMs); replaces launch_gate_up / launch_down for large token counts.
 cudaError_t launch_prefill(const FwdParams &p, const LayerDev &L, const LayerMaps &maps, int num_sms,

@@ -111,6 +111,15 @@ struct FwdParams {
     float *out;                  // [T][H]
     int *err;                    // device status word: 0 ok, 1 a bounded wait ran out
 
+    // FFN sublayer (moe_forward_block): norm_out = rmsnorm(norm_in, norm_w,
+    // norm_eps) before the routing (x = norm_out), and out = residual + block
+    // in the combine. null norm_in / residual: plain moe_forward.
+    const float *norm_in;
+    float *norm_out;
+    const float *norm_w;
+    float norm_eps;
+    const float *residual;
+
     // tensor-core (prefill) path
     void *a16;                   // [slots_cap][a16_stride] f16: gate/up operand (activation blocks dequantised)
     void *a16dn;                 // [slots_cap][a16dn_stride] f16: down operand (quantised SwiGLU output)

@@ -143,9 +143,9 @@ __global__ void __launch_bounds__(128) router_kernel(FwdParams p)
 // top-k on the total_cmp key with ties to the lower index, the weights, and
 // the token's bit in each chosen expert's mask. Semantics of
 // select_top_k_experts and select_experts_with_optional_bias
-// (src/gemma.rs:362-442, src/qwen_deepseek.rs:773-831). Each candidate's rank
-// is the number of candidates ranking before it (one pass of shuffles, no
-// sequential rounds); rank r < k is the r-th choice.
+// (src/gemma.rs:362-442, src/qwen_deepseek.rs:773-831). The r-th choice is
+// the winner of the r-th round of a warp-wide 64-bit argmax over the
+// candidates not chosen yet.
 template <int NL>   // experts per lane: E <= 32 * NL
 __device__ __forceinline__ void select_token(const FwdParams &p, int t, int lane)
 {
@@ -807,6 +807,48 @@ int launch_block_dots(const DevMatrix &m, const int8_t *xq, int n, int32_t *isum
     else
         block_dots_kernel<FMT_Q8_0><<<(tot + 255) / 256, 256, 0, st>>>(m, xq, n, isum);
     return cudaGetLastError();
+}
+
+}  // namespace jmoe
+
+// ------------------------------------------------------------ FFN pre-norm
+
+namespace jmoe {
+namespace {
+
+// RMSNorm of one token per warp in the fixed order shared with the oracle
+// (orc_rmsnorm): element h feeds lane partial (h/4) mod 32 as x*x fmaf chains
+// in increasing h, the xor butterfly 16..1 adds the partials, then
+// mean = sum / H, inv = 1 / sqrt(mean + eps), y = (x * inv) * w, each step
+// rounded once. Semantics of rmsnorm_standard (src/qwen_deepseek.rs:521-528),
+// whose kernel (jero-kernels-rvv) fixes no order.
+__global__ void __launch_bounds__(128) rmsnorm_kernel(FwdParams p)
+{
+    pdl_wait();   // the previous sublayer may still be writing the residual stream
+    pdl_trigger();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int t = blockIdx.x * 4 + warp;
+    if (t >= p.T) return;
+    const int H = p.H;
+    const float *x = p.norm_in + (size_t)t * H;
+    float *y = p.norm_out + (size_t)t * H;
+    float acc = 0.0f;
+    for (int hb = 4 * lane; hb < H; hb += 128)
+#pragma unroll
+        for (int c = 0; c < 4; c++)
+            if (hb + c < H) acc = __fmaf_rn(x[hb + c], x[hb + c], acc);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, o));
+    const float mean = __fdiv_rn(acc, (float)H);
+    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, p.norm_eps)));
+    for (int h = lane; h < H; h += 32) y[h] = __fmul_rn(__fmul_rn(x[h], inv), p.norm_w[h]);
+}
+
+}  // namespace
+
+cudaError_t launch_rmsnorm(const FwdParams &p, cudaStream_t st)
+{
+    return launch_dependent(rmsnorm_kernel, dim3((p.T + 3) / 4), dim3(128), 0, st, p);
 }
 
 }  // namespace jmoe

@@ -134,6 +134,9 @@ EXPORTS = {
     "moe_layer_upload": (C.c_int, [C.c_void_p, C.c_int32, C.POINTER(moe_layer_desc)]),
     "moe_forward": (C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.c_void_p, C.c_void_p, C.c_void_p,
                               C.c_void_p, C.c_int32]),
+    "moe_layer_set_ffn_norm": (C.c_int, [C.c_void_p, C.c_int32, C.c_void_p, C.c_float]),
+    "moe_forward_block": (C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.c_void_p, C.c_void_p, C.c_void_p,
+                                    C.c_void_p, C.c_int32]),
     "moe_residency_summary": (C.c_int, [C.c_void_p, C.POINTER(moe_residency)]),
     "moe_device_status": (C.c_int, [C.c_void_p, C.POINTER(C.c_int32)]),
     "moe_ctx_set_profiling": (C.c_int, [C.c_void_p, C.c_int32]),
@@ -366,6 +369,32 @@ class Context:
                      ptr_kind: int = PTR_DEVICE):
         _check(lib.moe_forward(self.h, layer, T, C.c_void_p(x_ptr), C.c_void_p(out_ptr),
                                C.c_void_p(sel_idx_ptr or None), C.c_void_p(sel_w_ptr or None), ptr_kind), self.h)
+
+    # ---- the FFN sublayer (moe_layer_set_ffn_norm / moe_forward_block)
+
+    def set_ffn_norm(self, layer: int, weight, eps: float):
+        """RMSNorm weight [H] (None: ones) and eps of the layer's FFN pre-norm."""
+        w = None if weight is None else np.ascontiguousarray(weight, dtype=np.float32)
+        _check(lib.moe_layer_set_ffn_norm(self.h, layer, _ptr(w) if w is not None else None, C.c_float(eps)), self.h)
+        self._keep_norm = w
+
+    def forward_block(self, layer: int, hidden: np.ndarray, want_selection: bool = True):
+        """hidden [T, H] -> (hidden + MoE(rmsnorm(hidden)), sel_idx, sel_w), host arrays."""
+        hidden = np.ascontiguousarray(hidden, dtype=np.float32)
+        T, H = hidden.shape
+        k = self.layers.get(layer, {"k": 1})["k"]
+        out = np.empty((T, H), dtype=np.float32)
+        si = np.empty((T, k), dtype=np.int32) if want_selection else None
+        sw = np.empty((T, k), dtype=np.float32) if want_selection else None
+        _check(lib.moe_forward_block(self.h, layer, T, _ptr(hidden), _ptr(out), _ptr(si), _ptr(sw), PTR_HOST),
+               self.h)
+        return out, si, sw
+
+    def forward_block_ptrs(self, layer: int, T: int, hidden_ptr: int, out_ptr: int, sel_idx_ptr: int = 0,
+                           sel_w_ptr: int = 0, ptr_kind: int = PTR_DEVICE):
+        _check(lib.moe_forward_block(self.h, layer, T, C.c_void_p(hidden_ptr), C.c_void_p(out_ptr),
+                                     C.c_void_p(sel_idx_ptr or None), C.c_void_p(sel_w_ptr or None), ptr_kind),
+               self.h)
 
     # ---- expert parallelism (moe_ep_init / moe_forward_ep)
 

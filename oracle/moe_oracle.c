@@ -236,6 +236,33 @@ void orc_router_logits(const float *w, const float *x, int E, int H, float *logi
     }
 }
 
+/* RMSNorm of one row in the build's fixed f32 order (the reference's
+ * rmsnorm_standard, src/qwen_deepseek.rs:521-528, calls a kernel of the
+ * un-vendored jero-kernels-rvv crate whose order is not visible): element h
+ * goes to partial (h/4) mod 32 as x*x fmaf chains in increasing h, the 32
+ * partials are combined by the xor butterfly 16..1, then mean = sum / H,
+ * inv = 1 / sqrt(mean + eps) and out = (x * inv) * w, each rounded once.
+ * w NULL: ones. Same order as the library's rmsnorm_kernel. */
+void orc_rmsnorm(const float *x, const float *w, int H, float eps, float *out)
+{
+    float p[32], q[32];
+    for (int l = 0; l < 32; l++) p[l] = 0.0f;
+    for (int h = 0; h < H; h++) {
+        int l = (h >> 2) & 31;
+        p[l] = fmaf(x[h], x[h], p[l]);
+    }
+    for (int off = 16; off >= 1; off >>= 1) {
+        for (int l = 0; l < 32; l++) q[l] = p[l] + p[l ^ off];
+        memcpy(p, q, sizeof p);
+    }
+    const float mean = p[0] / (float)H;
+    const float inv = 1.0f / sqrtf(mean + eps);
+    for (int h = 0; h < H; h++) {
+        const float y = x[h] * inv;
+        out[h] = w ? y * w[h] : y;
+    }
+}
+
 /* Rust f32::total_cmp as a signed-integer key (src/gemma.rs:417). */
 static inline int32_t total_key(float f)
 {

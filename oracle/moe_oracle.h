@@ -87,6 +87,7 @@ float orc_row_dot_q(int type, const uint8_t *wrow, const int8_t *xq, const float
 
 /* ---- router ---- */
 void orc_router_logits(const float *w, const float *x, int E, int H, float *logits);
+void orc_rmsnorm(const float *x, const float *w, int H, float eps, float *out);
 int  orc_select(const orc_layer *L, const float *logits, int32_t *idx, float *w);
 
 /* ---- the layer ---- */

@@ -48,6 +48,7 @@ def _load():
         "orc_block_dots": (C.c_int, [C.c_int, C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_void_p]),
         "orc_row_dot_q": (C.c_float, [C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int]),
         "orc_router_logits": (None, [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p]),
+        "orc_rmsnorm": (None, [C.c_void_p, C.c_void_p, C.c_int, C.c_float, C.c_void_p]),
         "orc_select": (C.c_int, [C.POINTER(orc_layer), C.c_void_p, C.c_void_p, C.c_void_p]),
         "orc_moe_forward": (C.c_int, [C.POINTER(orc_layer), C.c_int, C.c_void_p, C.c_void_p, C.c_void_p,
                                       C.c_void_p, C.c_int]),
@@ -105,6 +106,17 @@ def router_logits(w: np.ndarray, x: np.ndarray) -> np.ndarray:
     E, H = w.shape
     out = np.empty(E, dtype=np.float32)
     lib.orc_router_logits(_p(w), _p(x), E, H, _p(out))
+    return out
+
+
+def rmsnorm(x: np.ndarray, w, eps: float) -> np.ndarray:
+    """Rows of x [T, H] through orc_rmsnorm (w None: ones)."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    T, H = x.shape
+    wv = None if w is None else np.ascontiguousarray(w, dtype=np.float32)
+    out = np.empty_like(x)
+    for t in range(T):
+        lib.orc_rmsnorm(_p(x[t]), _p(wv) if wv is not None else None, H, C.c_float(eps), _p(out[t]))
     return out
 
 

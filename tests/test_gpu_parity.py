@@ -244,6 +244,57 @@ def test_gpu_int8_tensor_core_full_size(cid, T):
     _full_size_parity(cid, T, sample=16)
 
 
+# ------------------------------------------------ FFN sublayer (pre-norm + residual)
+
+@pytest.mark.parametrize("cid,over,T", [(2, dict(E=32, I=256, H=512), 5),
+                                        (3, dict(E=16, k=4, I=384, S=512, H=512), 40),
+                                        (2, {}, 64)])
+def test_gpu_forward_block_is_norm_block_residual(cid, over, T):
+    """moe_forward_block(hidden) == hidden + moe_forward(rmsnorm(hidden)) bit for
+    bit, with the norm taken by the oracle's fixed-order restatement (so the
+    device norm equals it bit for bit too); and within the contract tolerance of
+    the oracle's whole sublayer. Non-finite norm weights read as 1.0. Host and
+    device pointers, the device call in place (out = hidden)."""
+    import torch
+    cfg = synth.CONFIGS[cid].scaled(**over) if over else synth.CONFIGS[cid]
+    w = synth.build_weights(cfg)
+    rng = np.random.default_rng(7)
+    hidden = (synth.gen_x(cfg, T) * 3.0).astype(np.float32)
+    nw = rng.uniform(0.5, 1.5, cfg.H).astype(np.float32)
+    nw[3] = np.nan
+    nw[7] = np.inf
+    nw_eff = nw.copy()
+    nw_eff[[3, 7]] = 1.0
+    eps = 1e-6
+    xn = orc.rmsnorm(hidden, nw_eff, eps)
+    with gpu_layer(w, cfg.E, cfg.k, cfg.I, cfg.S > 0, cfg.route, cfg.H, T) as ctx:
+        ctx.set_ffn_norm(0, nw, eps)
+        out_b, si_b, sw_b = ctx.forward_block(0, hidden)
+        out_f, si_f, sw_f = ctx.forward(0, xn)
+        dev = torch.from_numpy(hidden.copy()).cuda()
+        ctx.forward_block_ptrs(0, T, dev.data_ptr(), dev.data_ptr())
+        torch.cuda.synchronize()
+        out_d = dev.cpu().numpy()
+        assert ctx.device_status() == 0
+    np.testing.assert_array_equal(si_b, si_f)
+    np.testing.assert_array_equal(sw_b, sw_f)
+    np.testing.assert_array_equal(out_b, hidden + out_f)
+    np.testing.assert_array_equal(out_d, out_b)
+    rows = np.arange(T) if T <= 16 else np.arange(0, T, T // 16)
+    r_out, r_si, r_sw = oracle_layer(w, cfg).forward(xn[rows], 8)
+    assert_parity(out_b[rows], si_b[rows], sw_b[rows], hidden[rows] + r_out, r_si, r_sw)
+
+
+def test_gpu_forward_block_needs_norm():
+    cfg = synth.CONFIGS[2].scaled(E=32, I=256, H=512)
+    w = synth.build_weights(cfg)
+    with gpu_layer(w, cfg.E, cfg.k, cfg.I, False, cfg.route, cfg.H, 4) as ctx:
+        with pytest.raises(jm.MoeError):
+            ctx.forward_block(0, synth.gen_x(cfg, 2))
+        with pytest.raises(jm.MoeError):
+            ctx.set_ffn_norm(0, None, float("nan"))
+
+
 # ------------------------------------------------------------- edge cases
 
 def _small_cfg(**kw):

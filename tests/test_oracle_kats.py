@@ -77,3 +77,19 @@ def test_oracle_threads_do_not_change_results():
     b = L.forward(x, 5)
     for u, v in zip(a, b):
         np.testing.assert_array_equal(u, v)
+
+
+def test_oracle_rmsnorm_matches_float64_and_defaults():
+    """orc_rmsnorm (the fixed-order restatement of rmsnorm_standard) against a
+    float64 RMSNorm, a NULL weight as all ones, and a zero row staying zero."""
+    rng = np.random.default_rng(5)
+    x = rng.standard_normal((4, 2048)).astype(np.float32) * np.array([[1.0], [1e-3], [1e3], [0.0]], np.float32)
+    w = rng.uniform(0.5, 1.5, 2048).astype(np.float32)
+    eps = 1e-6
+    y = orc.rmsnorm(x, w, eps)
+    x64 = x.astype(np.float64)
+    ref = x64 / np.sqrt((x64 ** 2).mean(axis=1, keepdims=True) + eps) * w
+    for t in range(3):
+        assert np.abs(y[t] - ref[t]).max() <= 1e-6 * np.abs(ref[t]).max()
+    assert np.all(y[3] == 0.0)
+    np.testing.assert_array_equal(orc.rmsnorm(x, None, eps), orc.rmsnorm(x, np.ones(2048, np.float32), eps))
