@@ -7,6 +7,8 @@
 
 #include "common.cuh"
 #include "ep_p2p.h"
+#include "kernels.h"
+#include "ptx.cuh"
 
 namespace jmoe {
 namespace {
@@ -66,6 +68,8 @@ __global__ void __launch_bounds__(256) ep_p2p_plan_kernel(EpP2PArgs a)
     __shared__ int s_off[kEpMaxRanks * (kMaxRouteExperts + 1)];
     __shared__ int s_cnt[kMaxRouteExperts], s_slot0[kMaxRouteExperts];
     __shared__ int s_ok;
+    pdl_wait();   // launched as a dependent: the routing is complete
+    pdl_trigger();
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
     const int E = a.E, G = a.world, El = a.El;
     for (int g = 0; g < G; g++) {
@@ -143,19 +147,24 @@ __global__ void __launch_bounds__(256) ep_p2p_plan_kernel(EpP2PArgs a)
 // that rank). One warp per row.
 __global__ void __launch_bounds__(256) ep_p2p_dispatch_kernel(EpP2PArgs a)
 {
+    __shared__ int s_off[kMaxRouteExperts + 1];
+    pdl_wait();
+    pdl_trigger();
     const int lane = threadIdx.x & 31;
     const int warp = (int)((blockIdx.x * (size_t)blockDim.x + threadIdx.x) >> 5);
     const int nwarps = (int)((gridDim.x * (size_t)blockDim.x) >> 5);
     const int H = a.H, chunks = H >> 4, nd = H >> 5;
+    for (int i = threadIdx.x; i <= a.E; i += blockDim.x) s_off[i] = a.offsets[i];
+    __syncthreads();
     for (int s = warp; s < a.n_slots; s += nwarps) {
         int lo = 0, hi = a.E - 1;   // the expert of slot s: last e with offsets[e] <= s
         while (lo < hi) {
             const int mid = (lo + hi + 1) >> 1;
-            if (a.offsets[mid] <= s) lo = mid;
+            if (s_off[mid] <= s) lo = mid;
             else hi = mid - 1;
         }
         const int dest = lo / a.El;
-        const int r = s - a.offsets[dest * a.El];
+        const int r = s - s_off[dest * a.El];
         const size_t tok = (size_t)a.perm_token[s];
         uint8_t *row = a.peers[dest] + a.o_xin + ((size_t)a.rank * a.cap + r) * a.rb;
         const int4 *q = reinterpret_cast<const int4 *>(a.xq + tok * H);
@@ -173,6 +182,8 @@ __global__ void __launch_bounds__(256) ep_p2p_dispatch_kernel(EpP2PArgs a)
 // output inbox at the source's own slot. One warp per row.
 __global__ void __launch_bounds__(256) ep_p2p_return_kernel(EpP2PArgs a)
 {
+    pdl_wait();   // the down projection's outputs are complete
+    pdl_trigger();
     const int lane = threadIdx.x & 31;
     const int warp = (int)((blockIdx.x * (size_t)blockDim.x + threadIdx.x) >> 5);
     const int nwarps = (int)((gridDim.x * (size_t)blockDim.x) >> 5);
@@ -190,6 +201,8 @@ __global__ void __launch_bounds__(256) ep_p2p_return_kernel(EpP2PArgs a)
 // Waits for every rank's flag of `phase` in this rank's arena.
 __global__ void ep_p2p_wait_kernel(EpP2PArgs a, int phase)
 {
+    pdl_wait();
+    pdl_trigger();
     const int lane = threadIdx.x;
     if (lane < a.world && !wait_epoch(ep_flag(a.own, a.o_flags, phase, lane), a.epoch)) atomicExch(a.err, kErrEpTimeout);
 }
@@ -205,26 +218,23 @@ int rows_grid(long long rows, int num_sms)
 
 cudaError_t launch_ep_p2p_plan(const EpP2PArgs &a, cudaStream_t st)
 {
-    ep_p2p_plan_kernel<<<1, 256, 0, st>>>(a);
-    return cudaGetLastError();
+    return launch_dependent(ep_p2p_plan_kernel, dim3(1), dim3(256), 0, st, a);
 }
 
 cudaError_t launch_ep_p2p_dispatch(const EpP2PArgs &a, int num_sms, cudaStream_t st)
 {
-    ep_p2p_dispatch_kernel<<<rows_grid(a.n_slots, num_sms), 256, 0, st>>>(a);
-    return cudaGetLastError();
+    return launch_dependent(ep_p2p_dispatch_kernel, dim3(rows_grid(a.n_slots, num_sms)), dim3(256), 0, st, a);
 }
 
 cudaError_t launch_ep_p2p_return(const EpP2PArgs &a, int num_sms, cudaStream_t st)
 {
-    ep_p2p_return_kernel<<<rows_grid((long long)a.world * a.cap, num_sms), 256, 0, st>>>(a);
-    return cudaGetLastError();
+    return launch_dependent(ep_p2p_return_kernel, dim3(rows_grid((long long)a.world * a.cap, num_sms)), dim3(256), 0,
+                            st, a);
 }
 
 cudaError_t launch_ep_p2p_wait(const EpP2PArgs &a, int phase, cudaStream_t st)
 {
-    ep_p2p_wait_kernel<<<1, 32, 0, st>>>(a, phase);
-    return cudaGetLastError();
+    return launch_dependent(ep_p2p_wait_kernel, dim3(1), dim3(32), 0, st, a, phase);
 }
 
 }  // namespace jmoe
