@@ -43,15 +43,16 @@ __device__ __forceinline__ bool wait_epoch(const uint32_t *flag, uint32_t epoch)
     return true;
 }
 
-// Raises this rank's flag of `phase` in every rank's arena, once all warps of
-// the grid have passed their system-scope fence (last-warp ticket).
+// Raises this rank's flag of `phase` in every rank's arena once every CTA of
+// the grid has finished its stores: a CTA barrier, then one system-scope fence
+// and one ticket per CTA (the fence is cumulative over the barrier); the last
+// CTA raises the flags.
 __device__ __forceinline__ void signal_when_done(const EpP2PArgs &a, int *ticket, int phase)
 {
-    __threadfence_system();
-    __syncwarp();
-    if ((threadIdx.x & 31) == 0) {
-        const int nwarps = (int)((gridDim.x * blockDim.x) >> 5);
-        if (atomicAdd(ticket, 1) == nwarps - 1) {
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence_system();
+        if (atomicAdd(ticket, 1) == (int)gridDim.x - 1) {
             atomicExch(ticket, 0);   // ready for the next forward
             __threadfence_system();
             for (int g = 0; g < a.world; g++) st_release_sys(ep_flag(a.peers[g], a.o_flags, phase, a.rank), a.epoch);
@@ -228,8 +229,10 @@ cudaError_t launch_ep_p2p_dispatch(const EpP2PArgs &a, int num_sms, cudaStream_t
 
 cudaError_t launch_ep_p2p_return(const EpP2PArgs &a, int num_sms, cudaStream_t st)
 {
-    return launch_dependent(ep_p2p_return_kernel, dim3(rows_grid((long long)a.world * a.cap, num_sms)), dim3(256), 0,
-                            st, a);
+    // the received rows are counted on the device: one CTA per SM covers them
+    // with a grid-stride loop (capacity world * cap would mostly idle)
+    const int g = rows_grid((long long)a.world * a.cap, num_sms);
+    return launch_dependent(ep_p2p_return_kernel, dim3(g < num_sms ? g : num_sms), dim3(256), 0, st, a);
 }
 
 cudaError_t launch_ep_p2p_wait(const EpP2PArgs &a, int phase, cudaStream_t st)
