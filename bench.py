@@ -343,7 +343,9 @@ def run_ours(args):
     # the rank-0 kernels explain the rank-0 time; the slowest rank sets the value
     tc = "gate_up_tc" in prof
     i8 = "gate_up_i8" in prof   # int8 tensor-core path: weight streaming at HBM rate, like the dp4a kernels
-    cands = ("gate_up_tc", "down_tc") if tc else (("gate_up_i8", "down_i8") if i8 else ("gate_up", "down"))
+    kb["experts_tc"] = kb["gate_up"] + kb["down"]   # the fused launch streams both
+    cands = ("gate_up_tc", "down_tc") if tc else (("gate_up_i8", "down_i8") if i8 else
+                                                  (("experts_tc",) if "experts_tc" in prof else ("gate_up", "down")))
     rows_here = kb["routed_rows"]
     dom = max(cands, key=lambda k: prof.get(k, (0, 1))[0])
     dom_ms = prof[dom][0] / prof[dom][1]

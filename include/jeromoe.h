@@ -122,6 +122,13 @@ typedef struct moe_device_spec {
 #define MOE_FLAG_INT8_TENSOR_CORES_NEVER 8
 #define MOE_FLAG_INT8_TENSOR_CORES_ALWAYS 16
 #define MOE_INT8_TENSOR_CORE_MIN_TOKENS 16
+/* By default, forwards below MOE_TENSOR_CORE_MIN_TOKENS run the whole expert
+ * FFN (gate/up, SwiGLU, down) as one launch on the tensor cores with f16
+ * operands: each weight value is expanded from its GGUF block once, the block
+ * scales folded in, and accumulated over the whole K in f32. This flag turns
+ * that off (the int8 paths above then apply); the two MOE_FLAG_INT8_* flags
+ * also select the int8 paths. */
+#define MOE_FLAG_FUSED_TC_NEVER 32
 
 /* Memory the admission check compares against. The real inspector reads
  * cudaMemGetInfo on spec->device; tests pass a fixed one, as the reference's
@@ -246,6 +253,19 @@ int moe_debug_permutation(moe_ctx *ctx, int32_t *offsets, int32_t *perm_token, i
  * xq [n x cols] and xd [n x cols/32] receive the quantised activations. */
 int moe_debug_block_dots(int32_t device, int32_t quant, const void *w, const float *x, int32_t n,
                          int32_t cols, int32_t *isum, int8_t *xq, float *xd);
+
+/* Tensor-core throughput probe (measurement support): n_mma back-to-back
+ * tcgen05.mma of one shape on every SM of `device`, operands in shared memory
+ * (a_tmem = 1: A in TMEM, m = 128 only), issued by n_acc warps (1..4) of
+ * each CTA, each into its own accumulator (n_acc * n <= 256); kind 0 = f16 inputs with f32 accumulation
+ * (K = 16 per MMA), kind 1 = int8 (s8 x s8, s32 accumulation, K = 32).
+ * *tops: dense tera-operations per second over the whole launch (2*m*n*K per
+ * MMA); *cycles_per_mma: SM clock cycles per MMA of one issuing warp on the
+ * slowest SM. m = 64 or
+ * 128, n = 16..256 in steps of 16. No counterpart in the reference; it
+ * measures the peaks the expert GEMMs are held against. */
+int moe_probe_tensor(int32_t device, int32_t kind, int32_t m, int32_t n, int32_t a_tmem, int32_t n_acc,
+                     int32_t ctas_per_sm, int32_t n_mma, double *tops, double *cycles_per_mma);
 
 /* ---- routing without allocation ----
  * No counterpart in the reference. For callers that cannot allocate device

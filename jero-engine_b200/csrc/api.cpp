@@ -63,6 +63,9 @@ struct Scratch {
     int *err = nullptr;
     int32_t *tile_off = nullptr;
     void *a16 = nullptr, *a16dn = nullptr;   // tensor-core path operands (f16)
+    void *x16 = nullptr;                     // fused small-batch launch: f16 token rows
+    int32_t *dep = nullptr;                  // fused expert launch: chunk counters, then the CTA ticket
+    int dep_cap = 0;
     bool tc = false;
     int slots_cap = 0;
 };
@@ -381,7 +384,13 @@ size_t carve_scratch(const ScratchDims &d, uint8_t *base, Scratch *s)
     t.err = (int *)take(4);
     t.tile_off = (int32_t *)take(4 * (size_t)kTileOffStride * 4);
     t.a16 = d.tc ? take(slots * H * 2) : nullptr;
-    t.a16dn = d.tc ? take(slots * W * 2) : nullptr;
+    // f16 operands: the down operand of both tensor-core paths, and the token
+    // rows of the fused small-batch launch (batches below the prefill path)
+    const size_t Tx = std::min<size_t>(Tm, MOE_TENSOR_CORE_MIN_TOKENS - 1), slots_x = Tx * k + Tx;
+    t.a16dn = take((d.tc ? slots : slots_x) * W * 2);
+    t.x16 = take(Tx * H * 2);
+    t.dep_cap = dep_entries((int)Tm, (int)k, (int)E);
+    t.dep = (int32_t *)take(((size_t)t.dep_cap + 1) * 4);
     if (s && base) {
         void *blk = s->block;
         *s = t;
@@ -465,6 +474,15 @@ bool use_int8_tc(const moe_device_spec &spec, const LayerStore &L, int T, int ro
     return L.S > 0 || L.dev.gate.type == FMT_Q8_0 || (int64_t)rows >= 6 * (int64_t)L.E;
 }
 
+// Batches below the f16 prefill path run the experts as one fused f16
+// tensor-core launch (experts_tc.cu) unless a flag forces the int8 paths.
+bool use_fused_tc(const moe_device_spec &spec, int T)
+{
+    if (spec.flags & (MOE_FLAG_FUSED_TC_NEVER | MOE_FLAG_INT8_TENSOR_CORES_NEVER | MOE_FLAG_INT8_TENSOR_CORES_ALWAYS))
+        return false;
+    return T < MOE_TENSOR_CORE_MIN_TOKENS;
+}
+
 bool use_tensor_cores(const moe_device_spec &spec, const LayerStore &L, const Scratch &s, int T)
 {
     if (!s.tc || (spec.flags & MOE_FLAG_TENSOR_CORES_NEVER)) return false;
@@ -510,8 +528,14 @@ FwdParams local_params(moe_ctx *ctx, const LayerStore &L, int T, int ptr_kind, c
     p.tile_off = s.tile_off;
     p.a16 = s.a16; p.a16dn = s.a16dn;
     p.a16_stride = s.H; p.a16dn_stride = s.W; p.slots_cap = s.slots_cap;
+    p.dep = s.dep;
+    p.dep_done = s.dep ? s.dep + s.dep_cap : nullptr;
+    p.dep_cap = s.dep_cap;
+    p.x16 = T < MOE_TENSOR_CORE_MIN_TOKENS ? s.x16 : nullptr;
     p.use_tc = use_tensor_cores(ctx->spec, L, s, T);
-    p.use_dtc = !p.use_tc && use_int8_tc(ctx->spec, L, T, T * L.k) && decode_tc_ok(p, L.dev);
+    p.use_xtc = !p.use_tc && use_fused_tc(ctx->spec, T) && fused_experts_ok(p, L.dev);
+    if (!p.use_xtc) p.x16 = nullptr;   // the routing writes the f16 rows only for the fused launch
+    p.use_dtc = !p.use_tc && !p.use_xtc && use_int8_tc(ctx->spec, L, T, T * L.k) && decode_tc_ok(p, L.dev);
     return p;
 }
 
@@ -934,6 +958,8 @@ int moe_layer_upload(moe_ctx *ctx, int32_t layer, const moe_layer_desc *desc)
         carve_scratch(sd, static_cast<uint8_t *>(blk), &ctx->scratch);
         CUDA_TRY(ctx, cudaMemset(ctx->scratch.err, 0, sizeof(int)), "cudaMemset(status)");
         CUDA_TRY(ctx, cudaMemset(ctx->scratch.sync, 0, kRoutingTicketBytes), "cudaMemset(routing tickets)");
+        CUDA_TRY(ctx, cudaMemset(ctx->scratch.dep, 0, ((size_t)ctx->scratch.dep_cap + 1) * 4),
+                 "cudaMemset(chunk counters)");
     }
     LayerStore &L = ctx->layers[layer];
     void *blk = nullptr;

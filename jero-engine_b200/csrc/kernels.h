@@ -70,6 +70,15 @@ bool decode_tc_ok(const FwdParams &p, const LayerDev &L);
 cudaError_t launch_decode_tc(const FwdParams &p, const LayerDev &L, const LayerMaps &maps, int num_sms,
                              const Marker &mk, cudaStream_t st, bool shared_only = false);
 
+// The expert FFN of small batches as one persistent launch on the tensor
+// cores with f16 operands (experts_tc.cu): gate/up + SwiGLU and down, the
+// down items of a slot chunk waiting for its gate/up tiles. mode: 0 routed
+// problems, 1 the shared expert only, 2 both. fused_experts_ok: the layer's
+// formats, shapes and buffers suit it.
+bool fused_experts_ok(const FwdParams &p, const LayerDev &L);
+cudaError_t launch_fused_experts(const FwdParams &p, const LayerDev &L, const LayerMaps &maps, int mode, int num_sms,
+                                 cudaStream_t st);
+
 // Expert-parallel exchange (ep.cu): bytes of one packed token row, and the
 // pack / unpack / receive-plan kernels.
 size_t ep_row_bytes(int H);

@@ -77,6 +77,7 @@ struct FwdParams {
     int max_problems;            // grid.y of the expert kernels
     int use_tc;                  // experts on the f16 tensor-core path (prefill.cu)
     int use_dtc;                 // experts on the int8 tensor-core path (decode_tc.cu)
+    int use_xtc;                 // experts in one fused f16 tensor-core launch (experts_tc.cu)
 
     const float *x;              // [T][H]
     const float *router;         // [E][H]
@@ -87,6 +88,8 @@ struct FwdParams {
     int x_qstride, x_dstride;    // 0: H and H/32. Expert-parallel inbox rows are packed
                                  // [H int8 | H/32 d | H/32 s], read in place with these strides
     float *xd;                   // [T][H/32] block scale
+    void *x16;                   // null, or [T][H] f16(q * d) of the activation blocks, each aligned group
+                                 // of four values in the order (0, 2, 1, 3) (fused tensor-core launch)
     float *xs;                   // [T][H/32] block scale * block sum of quants
     float *logits;               // [T][E]
     int32_t *sel_idx;            // [T][k]
@@ -125,7 +128,19 @@ struct FwdParams {
     void *a16dn;                 // [slots_cap][a16dn_stride] f16: down operand (quantised SwiGLU output)
     int a16_stride, a16dn_stride, slots_cap;
     int32_t *tile_off;           // [4][kTileOffStride] work-item offsets of the tensor-core launches
+
+    // fused expert launch (experts_tc.cu): per slot chunk, the number of
+    // gate/up epilogue warps that have stored their SwiGLU rows (the down
+    // items of that chunk wait for all of them), and a ticket of finished
+    // CTAs; the last CTA returns both to zero. dep_cap entries.
+    int32_t *dep;
+    int32_t *dep_done;
+    int dep_cap;
 };
+
+// Entries of FwdParams::dep a forward over T tokens may use: one per slot
+// chunk of up to 32 slots of every problem.
+inline int dep_entries(int T, int k, int E) { return (T * k + T) / 32 + (E < T * k ? E : T * k) + 2; }
 
 struct LayerDev {
     DevMatrix gate, up, down;

@@ -1,4 +1,5 @@
 // routing.cu -- router logits, top-k selection and the dispatch permutation.
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <math.h>
 #include <stdint.h>
@@ -46,10 +47,16 @@ __device__ __forceinline__ void quantize_tile(const FwdParams &p, int t0, int nt
             const uint32_t packed = (uint32_t)(q0 & 0xFF) | ((uint32_t)(q1 & 0xFF) << 8) |
                                     ((uint32_t)(q2 & 0xFF) << 16) | ((uint32_t)(q3 & 0xFF) << 24);
             *reinterpret_cast<uint32_t *>(p.xq + (size_t)t * H + 32 * b + 4 * l8) = packed;
+            const float d = __fdiv_rn(amax, 127.0f);
             if (l8 == 0) {
-                const float d = __fdiv_rn(amax, 127.0f);
                 p.xd[(size_t)t * nb + b] = d;
                 p.xs[(size_t)t * nb + b] = d * (float)qs;
+            }
+            if (p.x16) {   // f16(q * d) in the tensor-core operand order (0, 2, 1, 3)
+                const __half2 a = __floats2half2_rn((float)q0 * d, (float)q2 * d);
+                const __half2 c = __floats2half2_rn((float)q1 * d, (float)q3 * d);
+                *reinterpret_cast<uint2 *>(static_cast<__half *>(p.x16) + (size_t)t * H + 32 * b + 4 * l8) =
+                    make_uint2(*reinterpret_cast<const uint32_t *>(&a), *reinterpret_cast<const uint32_t *>(&c));
             }
         }
     }

@@ -42,6 +42,7 @@ FLAG_TENSOR_CORES_ALWAYS, FLAG_TENSOR_CORES_NEVER = 1, 2
 FLAG_EP_NCCL_ONLY = 4   # expert parallelism: NCCL exchange for every batch size
 # small batches: int8 weight-streaming kernels only / int8 tensor cores for every size below the f16 path
 FLAG_INT8_TENSOR_CORES_NEVER, FLAG_INT8_TENSOR_CORES_ALWAYS = 8, 16
+FLAG_FUSED_TC_NEVER = 32   # small batches: no fused f16 tensor-core expert launch
 TENSOR_CORE_MIN_TOKENS = 256
 
 
@@ -149,6 +150,8 @@ EXPORTS = {
     "moe_route_noalloc": (C.c_int, [C.c_int32, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int32,
                                     C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_float, C.c_int32, C.c_int32,
                                     C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]),
+    "moe_probe_tensor": (C.c_int, [C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int32,
+                                   C.c_int32, C.POINTER(C.c_double), C.POINTER(C.c_double)]),
     "moe_ep_unique_id": (C.c_int, [C.c_void_p]),
     "moe_ep_init": (C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.c_void_p]),
     "moe_forward_ep": (C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
@@ -493,6 +496,17 @@ def admission_check(device: int, max_tokens: int, descs: Sequence[moe_layer_desc
         insp = C.byref(moe_mem_inspector(free_bytes, total_bytes or free_bytes))
     _check(lib.moe_admission_check(C.byref(spec), arr, len(descs), insp, C.byref(fp)))
     return fp
+
+
+def probe_tensor(device: int, kind: int, m: int, n: int, a_tmem: bool = False, n_acc: int = 1, ctas_per_sm: int = 1,
+                 n_mma: int = 4096):
+    """Tensor-core throughput probe: (dense TOPS, cycles per MMA) of n_mma
+    back-to-back MMAs of one shape on every SM (kind 0 f16, 1 int8) over
+    n_acc independent accumulators, from ctas_per_sm issuing CTAs per SM."""
+    tops, cyc = C.c_double(), C.c_double()
+    _check(lib.moe_probe_tensor(device, kind, m, n, int(bool(a_tmem)), n_acc, ctas_per_sm, n_mma, C.byref(tops),
+                                C.byref(cyc)))
+    return tops.value, cyc.value
 
 
 def debug_block_dots(device: int, quant: int, w_rows: np.ndarray, x: np.ndarray):

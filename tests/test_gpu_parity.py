@@ -209,6 +209,37 @@ def test_gpu_tensor_core_matches_streaming_path():
     assert row_rel_err(outs[0][0], outs[1][0]).max() <= OUT_TOL
 
 
+# ------------------------- fused f16 tensor-core expert launch (small batches)
+
+@pytest.mark.parametrize("name", list(TC_CASES))
+@pytest.mark.parametrize("T", [1, 5, 33, 100, 255])
+def test_gpu_fused_tensor_core_path(name, T):
+    """The default path below 256 tokens: gate/up, SwiGLU and down in one
+    tensor-core launch (f16 weights expanded from the GGUF blocks, f32
+    accumulation over the whole K). Same routing as the oracle, outputs within
+    the contract tolerance of it and of the int8 streaming path, and the fused
+    launch is the one that ran. Run twice to cover the chunk counters' reset."""
+    cid, over = TC_CASES[name]
+    cfg = synth.CONFIGS[cid].scaled(**over)
+    w = synth.build_weights(cfg)
+    x = synth.gen_x(cfg, T)
+    ref = oracle_layer(w, cfg).forward(x, 8)
+    with gpu_layer(w, cfg.E, cfg.k, cfg.I, cfg.S > 0, cfg.route, cfg.H, T) as ctx:
+        ctx.set_profiling(True)
+        first = ctx.forward(0, x)
+        second = ctx.forward(0, x)
+        prof, _ = ctx.profile_read()
+        assert ctx.device_status() == 0
+    assert "experts_tc" in prof, sorted(prof)
+    assert_parity(*first, *ref)
+    np.testing.assert_array_equal(first[0], second[0])
+    with gpu_layer(w, cfg.E, cfg.k, cfg.I, cfg.S > 0, cfg.route, cfg.H, T,
+                   flags=jm.FLAG_INT8_TENSOR_CORES_NEVER) as ctx:
+        stream = ctx.forward(0, x)
+    np.testing.assert_array_equal(first[1], stream[1])
+    assert row_rel_err(first[0], stream[0]).max() <= OUT_TOL
+
+
 # ---------------------------------- int8 tensor-core path (small batches)
 
 @pytest.mark.parametrize("name", list(TC_CASES))
