@@ -257,7 +257,8 @@ int moe_debug_block_dots(int32_t device, int32_t quant, const void *w, const flo
 /* Tensor-core throughput probe (measurement support): n_mma back-to-back
  * tcgen05.mma of one shape on every SM of `device`, operands in shared memory
  * (a_tmem = 1: A in TMEM, m = 128 only), issued by n_acc warps (1..4) of
- * each CTA, each into its own accumulator (n_acc * n <= 256); kind 0 = f16 inputs with f32 accumulation
+ * each CTA, or for n_acc < 0 by lanes 0..-n_acc-1 (up to 8) of one warp, each
+ * issuer into its own accumulator (|n_acc| * n <= 256); kind 0 = f16 inputs with f32 accumulation
  * (K = 16 per MMA), kind 1 = int8 (s8 x s8, s32 accumulation, K = 32).
  * *tops: dense tera-operations per second over the whole launch (2*m*n*K per
  * MMA); *cycles_per_mma: SM clock cycles per MMA of one issuing warp on the

@@ -192,10 +192,13 @@ __device__ __forceinline__ void q4_scales_all(const uint4 &m, float (&sc)[8], fl
     }
 }
 
+// Every role waits suspended in try_wait (the warp issues nothing until the
+// phase completes): spinning waiters measurably took issue slots from the
+// dequant warps, which are issue-bound.
 template <bool SPIN>
 __device__ __forceinline__ bool xwait(uint64_t *bar, uint32_t parity, volatile int *abort_flag, int *err)
 {
-    return SPIN ? tc_spin_wait(bar, parity, abort_flag, err) : tc_wait(bar, parity, abort_flag, err);
+    return tc_wait(bar, parity, abort_flag, err);
 }
 
 __global__ void __launch_bounds__(kXThreads, 1)
@@ -444,8 +447,8 @@ __global__ void __launch_bounds__(kXThreads, 1)
                     q4_scales_all(meta, s8, m8);
 #pragma unroll
                     for (int kq = 0; kq < 4; kq++) {
-                        if (!xwait<true>(&a_empty[ar.slot], ar.phase ^ 1u, abort_flag, p.err)) { ok = false; break; }
-                        tc_fence_after();   // the MMAs that read this A stage have completed
+                        // expand first, then wait for the A stage: the expansion
+                        // overlaps the MMAs that still read the stage
                         uint32_t v[32];
 #pragma unroll
                         for (int h = 0; h < 2; h++) {
@@ -458,6 +461,8 @@ __global__ void __launch_bounds__(kXThreads, 1)
                             q4w(q.z, dsc, ndmn, o[4], o[5], o[12], o[13]);
                             q4w(q.w, dsc, ndmn, o[6], o[7], o[14], o[15]);
                         }
+                        if (!xwait<true>(&a_empty[ar.slot], ar.phase ^ 1u, abort_flag, p.err)) { ok = false; break; }
+                        tc_fence_after();   // the MMAs that read this A stage have completed
                         tmem_st32(arow + (uint32_t)(ar.slot * 64), v);
                         tmem_st_wait();
                         tc_fence_before();
@@ -470,8 +475,6 @@ __global__ void __launch_bounds__(kXThreads, 1)
                     const uint32_t dw[2] = {(qs & 1) ? meta.z : meta.x, (qs & 1) ? meta.w : meta.y};
 #pragma unroll
                     for (int kq = 0; kq < 2; kq++) {
-                        if (!xwait<true>(&a_empty[ar.slot], ar.phase ^ 1u, abort_flag, p.err)) { ok = false; break; }
-                        tc_fence_after();
                         uint32_t v[32];
                         const uint32_t dpair = dw[kq];   // f16 d of blocks 2 kq, 2 kq + 1 of the stage
                         const __half2 d0 = __low2half2(bits_h2(dpair)), d1 = __high2half2(bits_h2(dpair));
@@ -484,6 +487,8 @@ __global__ void __launch_bounds__(kXThreads, 1)
                             q8w(q.z, d, v[8 * cc + 4], v[8 * cc + 5]);
                             q8w(q.w, d, v[8 * cc + 6], v[8 * cc + 7]);
                         }
+                        if (!xwait<true>(&a_empty[ar.slot], ar.phase ^ 1u, abort_flag, p.err)) { ok = false; break; }
+                        tc_fence_after();
                         tmem_st32(arow + (uint32_t)(ar.slot * 64), v);
                         tmem_st_wait();
                         tc_fence_before();

@@ -30,14 +30,14 @@ __global__ void __launch_bounds__(128)
     uint8_t *base = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     uint8_t *sa = base, *sb = base + 16384;
     const int bytes = cols == 512 ? 65536 : 49152;
-    uint64_t *bar = reinterpret_cast<uint64_t *>(base + bytes - 64);   // one per issuing warp (<= 4)
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bar + 4);
+    uint64_t *bar = reinterpret_cast<uint64_t *>(base + bytes - 128);   // one per issuer (<= 8)
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bar + 8);
     const int warp = threadIdx.x >> 5;
     // zero operands: every product is 0, no special values
-    for (int i = threadIdx.x; i < (bytes - 64) / 16; i += blockDim.x)
+    for (int i = threadIdx.x; i < (bytes - 128) / 16; i += blockDim.x)
         reinterpret_cast<uint4 *>(base)[i] = make_uint4(0u, 0u, 0u, 0u);
     if (threadIdx.x == 0) {
-        for (int i = 0; i < 4; i++) mbar_init(&bar[i], 1);
+        for (int i = 0; i < 8; i++) mbar_init(&bar[i], 1);
         fence_barrier_init();
     }
     if (warp == 0) tmem_alloc(tmem_slot, (uint32_t)cols);
@@ -60,13 +60,17 @@ __global__ void __launch_bounds__(128)
     tc_fence_after();
     // issuers = n_acc: lane 0 of warp w issues every MMA into accumulator w
     // (columns [w N, (w + 1) N)), one independent K loop per issuing warp
-    if ((threadIdx.x & 31) == 0 && warp < n_acc) {
+    // n_acc > 0: issuer w = lane 0 of warp w; n_acc < 0: issuers = lanes 0..-n_acc-1 of warp 0
+    const bool lanes = n_acc < 0;
+    const int n_iss = lanes ? -n_acc : n_acc;
+    const int iss = lanes ? (threadIdx.x & 31) : warp;
+    if (lanes ? (warp == 0 && (threadIdx.x & 31) < n_iss) : ((threadIdx.x & 31) == 0 && warp < n_iss)) {
         const uint64_t ad = umma_desc_sw128(smem_addr(sa)), bd = umma_desc_sw128(smem_addr(sb));
         // D f32 (f16 kind) or s32 (i8 kind, s8 x s8), both K-major
         const uint32_t idesc = kind == 0 ? ((1u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24))
                                          : ((2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) |
                                             ((uint32_t)(M >> 4) << 24));
-        const uint32_t d = tmem + (uint32_t)(warp * N);
+        const uint32_t d = tmem + (uint32_t)(iss * N);
         const long long t0 = clock64();
         for (int i = 0; i < n_mma; i++) {
             const uint32_t acc = i > 0 ? 1u : 0u;
@@ -79,10 +83,10 @@ __global__ void __launch_bounds__(128)
                 else tc_mma_i8(d, ad, bd, idesc, acc);
             }
         }
-        tc_commit(&bar[warp]);
+        tc_commit(&bar[iss]);
         volatile int never = 0;
-        tc_wait(&bar[warp], 0, &never, err);
-        if (warp == 0) cycles[blockIdx.x] = clock64() - t0;
+        tc_wait(&bar[iss], 0, &never, err);
+        if (iss == 0) cycles[blockIdx.x] = clock64() - t0;
     }
     tc_fence_before();
     __syncthreads();
@@ -100,7 +104,8 @@ extern "C" int moe_probe_tensor(int32_t device, int32_t kind, int32_t m, int32_t
 {
     using namespace jmoe;
     if ((kind != 0 && kind != 1) || (m != 64 && m != 128) || n < 16 || n > 256 || n % 16 || n_mma < 4 ||
-        n_acc < 1 || n_acc > 4 || (ctas_per_sm != 1 && ctas_per_sm != 2) || n_acc * n > 256 / ctas_per_sm ||
+        n_acc == 0 || n_acc > 4 || n_acc < -8 || (ctas_per_sm != 1 && ctas_per_sm != 2) ||
+        (n_acc < 0 ? -n_acc : n_acc) * n > 256 / ctas_per_sm ||
         (ctas_per_sm == 2 && n > 128) || !tops || !cycles_per_mma)
         return MOE_ERR_INVALID_ARGS;
     if (m == 64 && a_tmem) return MOE_ERR_INVALID_ARGS;   // A from TMEM: M = 128 only here
@@ -157,7 +162,7 @@ extern "C" int moe_probe_tensor(int32_t device, int32_t kind, int32_t m, int32_t
     }
     if (rc == MOE_OK) {
         const double k = kind == 0 ? 16.0 : 32.0;
-        *tops = 2.0 * m * n * k * (double)n_mma * n_acc * grid / (ms * 1e-3) / 1e12;
+        *tops = 2.0 * m * n * k * (double)n_mma * (n_acc < 0 ? -n_acc : n_acc) * grid / (ms * 1e-3) / 1e12;
         long long mx = 0;
         for (long long c : hc) mx = c > mx ? c : mx;
         *cycles_per_mma = (double)mx / n_mma;
