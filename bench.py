@@ -2,19 +2,23 @@
 """Benchmark of the MoE FFN hot path on B200.
 
 Metric: MoE-layer tokens/s (one step = one forward of one MoE layer over T
-tokens), with the HBM-roofline fraction of the dominant kernel. Default
+tokens), with the roofline fraction of the dominant kernel. Default
 workload: config 2 of the benchmark set (Qwen3-MoE layer, hidden 2048, 128
 experts, top-8, intermediate 768, Q4_K weights), decode batch T=64, seeded
-synthetic inputs; the T=1..64 sweep is reported beside it.
+synthetic inputs; the T=1..32 sweep and one entry per other configuration
+(config 1 T=32, config 3 T=2048, config 4 T=512 and 4096, config 5 T=8192)
+are reported beside it.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
 --impl reference times the CPU restatement of the reference MoE path (the
 reference is Rust and cannot be built here) on this host's cores, on the same
-workload. Under torchrun with N>1 the layer runs expert-parallel: rank g holds
-experts [g*E/N, (g+1)*E/N), routes its own T tokens and exchanges the routed
-rows over NCCL (moe_forward_ep); value = N*T tokens per step over the slowest
-rank's time (weak scaling). --strong splits T over the ranks instead.
+workload, with layers built by the restatement's own generator and quantiser
+(the product library is not loaded). Under torchrun with N>1 the layer runs
+expert-parallel: rank g holds experts [g*E/N, (g+1)*E/N), routes its own T
+tokens and exchanges the routed rows with the owning ranks
+(moe_forward_ep); value = N*T tokens per step over the slowest rank's time
+(weak scaling). --strong splits T over the ranks instead.
 """
 import argparse
 import json
@@ -30,6 +34,11 @@ sys.path.insert(0, os.path.join(ROOT, "jero-engine_b200"))
 
 FLUSH_BYTES = 256 << 20   # > 126 MB L2
 FALLBACK_HBM_GBS = 6650.0
+FALLBACK_BF16_TFLOPS = 1590.0
+METRIC, UNIT = "MoE-layer tokens/s", "tokens/s"
+# the other configurations, one timed entry each (N = 1 only)
+EXTRA_CONFIGS = ((1, 32), (3, 2048), (4, 512), (4, 4096), (5, 8192))
+PARITY_ROWS = 16
 
 
 def parse():
@@ -42,6 +51,7 @@ def parse():
     ap.add_argument("--tokens", type=int, default=0, help="T of the headline workload (default: largest of the config)")
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-configs", action="store_true", help="skip the entries of the other configurations")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--strong", action="store_true", help="with N>1: T is the global batch, split over the ranks")
     ap.add_argument("--flags", type=int, default=0, help="MOE_FLAG_* bits of the context (e.g. 1: tensor cores always)")
@@ -61,13 +71,9 @@ def measured_traffic(workload, kernel):
         return None
 
 
-FALLBACK_BF16_TFLOPS = 1590.0
-
-
 def peaks():
-    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     try:
-        with open(p) as f:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
             d = json.load(f)
         return float(d["hbm_gbs"]), "measured"
     except Exception:
@@ -83,6 +89,14 @@ def tensor_peak():
         return float(d.get("bf16_tflops_sustained", d["bf16_tflops"])), "measured (sustained)"
     except Exception:
         return FALLBACK_BF16_TFLOPS, "fallback"
+
+
+def workload_config(cfg, T, world, strong, U):
+    """The workload both arms report (no timing method, no model keys)."""
+    return {"workload": f"{cfg.name} T={T}", "T": T, "H": cfg.H, "E": cfg.E, "k": cfg.k, "I": cfg.I, "S": cfg.S,
+            "quant": "Q4_K" if cfg.quant == 12 else "Q8_0", "experts_routed": int(U),
+            "global_batch": int(world * T),
+            "parallelism": f"ep{world}" if world > 1 else "single"}
 
 
 def kernel_flops(cfg, T, routed_rows=None):
@@ -181,7 +195,58 @@ def kernel_bytes(cfg, weights, sel_idx, T, expert_range=None, routed_rows=None):
     layer = (U * sum(per.values()) + sum(sh.values()) + cfg.E * cfg.H * 4 + 2 * T * cfg.H * 4 + T * cfg.k * 8)
     if expert_range is not None:   # activation rows out and expert outputs back through the exchange
         layer += routed * cfg.H * 1.25 + routed * cfg.H * 4
-    return {"gate_up": gate_up, "down": down, "layer": layer, "U": U, "routed_rows": routed}
+    # the fused small-batch launch streams both projections
+    return {"gate_up": gate_up, "down": down, "experts_tc": gate_up + down, "layer": layer, "U": U,
+            "routed_rows": routed}
+
+
+def roofline_of(cfg, T, prof, kb, workload, rows_here=None, ep=False, tensor_peaks=None):
+    """Roofline of the dominant expert kernel of one forward from the per-stage
+    profile: HBM-bound paths by algorithmic bytes, the prefill tensor-core path
+    by algorithmic FLOPs (against the sustained bf16 peak, with the fraction of
+    this run's own f16 and int8 probe peaks beside it)."""
+    tc = "gate_up_tc" in prof
+    i8 = "gate_up_i8" in prof
+    cands = ("gate_up_tc", "down_tc") if tc else (("gate_up_i8", "down_i8") if i8 else
+                                                  (("experts_tc",) if "experts_tc" in prof else ("gate_up", "down")))
+    dom = max(cands, key=lambda k: prof.get(k, (0, 1))[0])
+    dom_ms = prof[dom][0] / prof[dom][1]
+    traffic = None if ep else measured_traffic(workload, dom)   # captures are single-GPU workloads
+    if tc:
+        fl = kernel_flops(cfg, T, rows_here)[dom]
+        tpk, tpk_kind = tensor_peak()
+        ach = fl / (dom_ms / 1e3) / 1e12
+        r = {"bound": "tensor", "kernel": dom, "achieved": round(ach, 1), "peak": tpk, "unit": "TFLOP/s",
+             "frac": round(ach / tpk, 4), "traffic": traffic, "peak_source": tpk_kind,
+             "algorithmic_flops_per_launch": int(fl),
+             "operands": "f16 (weights dequantised from GGUF blocks in shared memory), f32 accumulate"}
+        if tensor_peaks:
+            r["frac_of_probe_f16"] = round(ach / tensor_peaks["f16_tflops"], 4)
+            r["frac_of_probe_int8"] = round(ach / tensor_peaks["int8_tops"], 4)
+        return r
+    hbm, peak_kind = peaks()
+    b = kb[dom.replace("_i8", "")]
+    ach = b / (dom_ms / 1e3) / 1e9
+    return {"bound": "hbm", "kernel": dom, "achieved": round(ach, 1), "peak": hbm, "unit": "GB/s",
+            "frac": round(ach / hbm, 4), "traffic": traffic, "peak_source": peak_kind,
+            "algorithmic_bytes_per_launch": int(b)}
+
+
+def row_rel_err(out, ref):
+    import numpy as np
+    return np.abs(out - ref).max(axis=1) / np.maximum(np.abs(ref).max(axis=1), 1e-30)
+
+
+def oracle_parity(cfg, weights, x_rows, out_rows, si_rows, threads):
+    """Rows of this run's output against the CPU oracle: routing bit-exact and
+    the max per-row relative error (the contract is 1e-2)."""
+    import numpy as np
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as orc
+    L = orc.Layer(weights, 0, cfg.E, cfg.k, cfg.S > 0, cfg.route, hidden=cfg.H)
+    ro, rsi, _ = L.forward(x_rows, threads)
+    return {"rows_checked": int(len(x_rows)), "routing_exact": bool(np.array_equal(si_rows, rsi)),
+            "max_row_rel_err": float(row_rel_err(out_rows, ro).max())}
 
 
 def cpu_baseline(cfg, weights, x, seconds, threads):
@@ -202,39 +267,142 @@ def cpu_baseline(cfg, weights, x, seconds, threads):
 
 
 def run_reference(args):
+    """The reference arm: the CPU restatement timed on this host's cores over
+    the same workload and configuration as our arm (the global batch at N>1),
+    each step a bounded sample of it. Rank 0 alone runs; the layer is built by
+    the restatement's own generator and quantiser (same bytes as the library's),
+    so the product library is never loaded."""
     rank, _, world = rank_info()
     if rank != 0:
         return
+    import numpy as np
     import synth
-    cfg = synth.CONFIGS[args.config]
-    T = args.tokens or max(cfg.tokens)
-    threads = os.cpu_count() or 1
-    weights = synth.build_weights(cfg)
-    x = synth.gen_x(cfg, T)
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle as orc
+    synth.use_backend(orc)
+    cfg = synth.CONFIGS[args.config]
+    T_arg = args.tokens or max(cfg.tokens)
+    ep = world > 1
+    T = T_arg // world if (ep and args.strong) else T_arg
+    glob = T * world
+    threads = os.cpu_count() or 1
+    weights = synth.build_weights(cfg)
+    x = synth.gen_x(cfg, glob)
     L = orc.Layer(weights, 0, cfg.E, cfg.k, cfg.S > 0, cfg.route, hidden=cfg.H)
+    sample = min(glob, 256)   # tokens per timed step
     for _ in range(args.warmup):
         L.forward(x[:1], threads)
-    times = []
-    for _ in range(args.steps):
+    times, sel = [], []
+    for i in range(args.steps):
+        lo = (i * sample) % glob
+        rows = x[lo:lo + sample] if lo + sample <= glob else np.concatenate([x[lo:], x[:lo + sample - glob]])
         t0 = time.perf_counter()
-        L.forward(x, threads)
+        _, si, _ = L.forward(rows, threads)
         times.append(time.perf_counter() - t0)
+        sel.append(si)
     total = sum(times)
-    value = T * args.steps / total
+    value = sample * args.steps / total
+    # experts routed by the whole global batch (the oracle's routing is the product's, bit for bit)
+    router = weights.tensor("blk.0.ffn_gate_inp.weight").data.reshape(cfg.E, cfg.H)
+    chosen = set()
+    for t in range(glob):
+        idx, _ = L.select(orc.router_logits(router, x[t]))
+        chosen.update(int(e) for e in idx)
     line = {
-        "impl": "reference", "metric": "MoE-layer tokens/s", "value": round(value, 3), "unit": "tokens/s",
-        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(1e3 * total / args.steps, 3), "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "int8", "data": "synthetic",
-        "config": {"workload": f"{cfg.name} T={T}", "T": T, "H": cfg.H, "E": cfg.E, "k": cfg.k, "I": cfg.I,
-                   "quant": "Q4_K" if cfg.quant == 12 else "Q8_0"},
-        "cpu_baseline": {"value": round(value, 3), "unit": "tokens/s", "cores": threads, "kind": "port",
-                         "sample": f"{T} tokens per step, {args.steps} steps, one token at a time"},
-        "e2e": {"value": round(value, 3), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": UNIT,
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(1e3 * total / args.steps, 3), "higher_is_better": True,
+        "scaling": "strong" if (ep and args.strong) else "weak",
+        "vs_baseline": None, "dtype": "int8", "data": "synthetic (seeded N(0,1) activations, N(0,0.02) weights "
+                                                     "quantised to GGUF blocks)",
+        "config": workload_config(cfg, T, world, args.strong, len(chosen)),
+        "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": threads, "kind": "port",
+                         "sample": f"{sample} of the {glob} tokens of the workload per step, {args.steps} steps, "
+                                   f"one token at a time (CPU restatement of the reference MoE path, "
+                                   f"oracle/moe_oracle.c)"},
+        "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
+
+
+class Timer:
+    """Forwards of one context timed with CUDA events on its stream, the L2
+    flushed (256 MiB write) before every step."""
+
+    def __init__(self, torch, ctx, stream, flush, step, barrier, world):
+        self.torch, self.ctx, self.stream, self.flush = torch, ctx, stream, flush
+        self.step, self.barrier, self.world = step, barrier, world
+
+    def run(self, t, steps, profile):
+        torch = self.torch
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+        self.barrier()
+        torch.cuda.synchronize()
+        if profile:
+            self.ctx.set_profiling(True)
+        for i in range(steps):
+            self.flush.fill_(i & 0xFF)
+            evs[i][0].record(self.stream)
+            self.step(t)
+            evs[i][1].record(self.stream)
+        torch.cuda.synchronize()
+        self.barrier()
+        prof = None
+        if profile:
+            prof = self.ctx.profile_read()
+            self.ctx.set_profiling(False)
+        return [a.elapsed_time(b) for a, b in evs], prof
+
+
+def probe_peaks(jm):
+    """This GPU's dense tensor peaks from the library's probe (one issuing warp
+    per SM, M = 128, N = 256, A in TMEM): f16 and int8."""
+    try:
+        f16, _ = jm.probe_tensor(0, 0, 128, 256, True, 1, 1, 8192)
+        i8, _ = jm.probe_tensor(0, 1, 128, 256, True, 1, 1, 8192)
+        return {"f16_tflops": round(f16, 1), "int8_tops": round(i8, 1),
+                "how": "moe_probe_tensor: 8192 back-to-back tcgen05.mma M128 N256 (A in TMEM) per SM, CUDA events"}
+    except Exception as e:   # the headline does not depend on it
+        return {"error": str(e)[:200]}
+
+
+def extra_config(torch, jm, synth, cid, T, stream, flush, tensor_peaks, steps=10):
+    """One timed entry of another configuration at N = 1: tokens/s, the
+    dominant kernel's roofline and a parity sample against the oracle."""
+    import numpy as np
+    cfg = synth.CONFIGS[cid]
+    weights = synth.build_weights(cfg)
+    x = synth.gen_x(cfg, T)
+    ctx = jm.Context(0, T, 1)
+    try:
+        ctx.set_stream(stream.cuda_stream)
+        d, keep = synth.desc_for(cfg, weights)
+        ctx.upload(0, d)
+        x_dev = torch.from_numpy(x).cuda()
+        out_dev = torch.empty_like(x_dev)
+        si_dev = torch.empty((T, cfg.k), dtype=torch.int32, device="cuda")
+        sw_dev = torch.empty((T, cfg.k), dtype=torch.float32, device="cuda")
+
+        def step(t):
+            ctx.forward_ptrs(0, t, x_dev.data_ptr(), out_dev.data_ptr(), si_dev.data_ptr(), sw_dev.data_ptr())
+
+        tm = Timer(torch, ctx, stream, flush, step, lambda: None, 1)
+        tm.run(T, 3, False)
+        ms, _ = tm.run(T, steps, False)
+        _, (prof, _) = tm.run(T, max(3, steps // 2), True)
+        sel = si_dev.cpu().numpy()
+        kb = kernel_bytes(cfg, weights, sel, T)
+        wl = f"{cfg.name} T={T}"
+        m = statistics.median(ms)
+        rows = np.sort(np.random.default_rng(cid).choice(T, min(8, T), replace=False))
+        par = oracle_parity(cfg, weights, x[rows], out_dev.cpu().numpy()[rows], sel[rows], os.cpu_count() or 1)
+        return {"workload": wl, "T": T, "tokens_per_s": round(T / (m / 1e3), 1), "ms_per_step": round(m, 4),
+                "experts_routed": kb["U"], "steps": steps,
+                "roofline": roofline_of(cfg, T, prof, kb, wl, tensor_peaks=tensor_peaks),
+                "layer_hbm_frac": round(kb["layer"] / (m / 1e3) / 1e9 / peaks()[0], 4),
+                "kernels": {k: round(1e3 * v[0] / v[1], 2) for k, v in prof.items()}, "parity": par}
+    finally:
+        ctx.close()
 
 
 def run_ours(args):
@@ -257,10 +425,12 @@ def run_ours(args):
     if T < 1:
         raise SystemExit(f"--strong needs at least {world} tokens")
     sweep_T = [] if (args.no_sweep or ep) else [t for t in cfg.tokens if t != T]
+    tensor_peaks = probe_peaks(jm) if (world == 1 and not args.no_configs) else None
     weights = synth.build_weights(cfg)
-    x_all = synth.gen_x(cfg, max([T] + sweep_T) * world)
-    x_host = x_all[rank * max([T] + sweep_T):(rank + 1) * max([T] + sweep_T)].copy()
-    ctx = jm.Context(local_rank, max([T] + sweep_T), 1, flags=args.flags)
+    Tmax = max([T] + sweep_T)
+    x_all = synth.gen_x(cfg, Tmax * world)
+    x_host = x_all[rank * Tmax:(rank + 1) * Tmax].copy()
+    ctx = jm.Context(local_rank, Tmax, 1, flags=args.flags)
     if ep:
         ids = [jm.ep_unique_id() if rank == 0 else None]
         dist.broadcast_object_list(ids, src=0)
@@ -287,25 +457,7 @@ def run_ours(args):
         if world > 1:
             dist.barrier(device_ids=[local_rank])
 
-    def timed(t, steps, profile):
-        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
-        barrier()
-        torch.cuda.synchronize()
-        if profile:
-            ctx.set_profiling(True)
-        for i in range(steps):
-            flush.fill_(i & 0xFF)
-            evs[i][0].record(stream)
-            step(t)
-            evs[i][1].record(stream)
-        torch.cuda.synchronize()
-        barrier()
-        prof = None
-        if profile:
-            prof = ctx.profile_read()
-            ctx.set_profiling(False)
-        return [a.elapsed_time(b) for a, b in evs], prof
-
+    tm = Timer(torch, ctx, stream, flush, step, barrier, world)
     sampler = ClockSampler(local_rank)
     sampler.start()
     for i in range(args.warmup):
@@ -321,62 +473,73 @@ def run_ours(args):
         El = cfg.E // world
         mine = (sel >= rank * El) & (sel < (rank + 1) * El)
         kb = kernel_bytes(cfg, weights, sel, T, (rank * El, (rank + 1) * El), int(mine.sum()))
+        U_global = len(np.unique(sel))
     else:
         sel = si_dev[:T].cpu().numpy()
         kb = kernel_bytes(cfg, weights, sel, T)
+        U_global = kb["U"]
     sampler.wait_first()
     # keep the GPU busy until the timed region starts so the samples see it under load
     for i in range(max(args.warmup, 20)):
         flush.fill_(i & 0xFF)
         step(T)
-    step_ms, _ = timed(T, args.steps, False)
+    step_ms, _ = tm.run(T, args.steps, False)
     clocks = sampler.stop()
     # per-stage breakdown from a second pass with an event at every stage
     # boundary (the events serialise the stages, so it is not the timed pass)
-    _, (prof, n_fwd) = timed(T, args.steps, True)
+    _, (prof, n_fwd) = tm.run(T, args.steps, True)
     total_ms = sum(step_ms)
     if world > 1:
         tt = torch.tensor([total_ms], device="cuda")
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
         total_ms = float(tt.item())
     value = world * T * args.steps / (total_ms / 1e3)
-    # the rank-0 kernels explain the rank-0 time; the slowest rank sets the value
-    tc = "gate_up_tc" in prof
-    i8 = "gate_up_i8" in prof   # int8 tensor-core path: weight streaming at HBM rate, like the dp4a kernels
-    kb["experts_tc"] = kb["gate_up"] + kb["down"]   # the fused launch streams both
-    cands = ("gate_up_tc", "down_tc") if tc else (("gate_up_i8", "down_i8") if i8 else
-                                                  (("experts_tc",) if "experts_tc" in prof else ("gate_up", "down")))
-    rows_here = kb["routed_rows"]
-    dom = max(cands, key=lambda k: prof.get(k, (0, 1))[0])
-    dom_ms = prof[dom][0] / prof[dom][1]
-    hbm, peak_kind = peaks()
-    if tc:   # tensor-bound: algorithmic FLOPs of the dominant GEMM per launch over its duration
-        fl = kernel_flops(cfg, T, rows_here)[dom]
-        tpk, tpk_kind = tensor_peak()
-        ach = fl / (dom_ms / 1e3) / 1e12
-        roofline = {"bound": "tensor", "kernel": dom, "achieved": round(ach, 1), "peak": tpk, "unit": "TFLOP/s",
-                    "frac": round(ach / tpk, 4), "traffic": measured_traffic(f"{cfg.name} T={T}", dom),
-                    "peak_source": tpk_kind, "algorithmic_flops_per_launch": int(fl),
-                    "operands": "f16 (weights dequantised from GGUF blocks in shared memory), f32 accumulate"}
-    else:    # HBM-bound: algorithmic bytes of the dominant kernel per launch
-        achieved = kb[dom.replace("_i8", "")] / (dom_ms / 1e3) / 1e9
-        roofline = {"bound": "hbm", "kernel": dom, "achieved": round(achieved, 1), "peak": hbm,
-                    "unit": "GB/s", "frac": round(achieved / hbm, 4),
-                    "traffic": measured_traffic(f"{cfg.name} T={T}", dom),
-                    "peak_source": peak_kind, "algorithmic_bytes_per_launch": int(kb[dom.replace("_i8", "")])}
+    wl = f"{cfg.name} T={T}"
+    roofline = roofline_of(cfg, T, prof, kb, wl, kb["routed_rows"] if ep else None, ep=ep, tensor_peaks=tensor_peaks)
     layer_ms = total_ms / args.steps
     kernels = {k: {"avg_us": round(1e3 * v[0] / v[1], 2), "launches": v[1]} for k, v in prof.items()}
     launches = sum(v[1] for v in prof.values())
 
+    # parity of the timed run's output, outside the timed region: sampled rows
+    # against the CPU oracle; with expert parallelism also every row against a
+    # single-GPU context holding all experts, on the same GPU and tokens
+    out_np = out_dev[:T].cpu().numpy()
+    rows = np.sort(np.random.default_rng(rank).choice(T, min(PARITY_ROWS, T), replace=False))
+    sel_rows = None
+    if ep:
+        _, si_ep, _ = ctx.forward_ep(0, x_host[:T])   # collective: every rank takes part
+        sel_rows = si_ep[rows]
+    else:
+        sel_rows = si_dev[:T].cpu().numpy()[rows]
+    par = oracle_parity(cfg, weights, x_host[rows], out_np[rows], sel_rows,
+                        max(1, (os.cpu_count() or 1) // world))
+    if ep:
+        with jm.Context(local_rank, T, 1) as one:
+            d1, keep1 = synth.desc_for(cfg, weights)
+            one.upload(0, d1)
+            o1, s1, _ = one.forward(0, x_host[:T])
+        par["routing_exact_vs_single_gpu"] = bool(np.array_equal(s1, si_ep))
+        par["max_row_rel_err_vs_single_gpu"] = float(row_rel_err(out_np, o1).max())
+        par["rows_vs_single_gpu"] = int(T)
+        agg = torch.tensor([par["max_row_rel_err"], par["max_row_rel_err_vs_single_gpu"],
+                            0.0 if (par["routing_exact"] and par["routing_exact_vs_single_gpu"]) else 1.0],
+                           device="cuda", dtype=torch.float64)
+        dist.all_reduce(agg, op=dist.ReduceOp.MAX)
+        par.update({"max_row_rel_err": float(agg[0]), "max_row_rel_err_vs_single_gpu": float(agg[1]),
+                    "routing_exact": bool(agg[2] == 0.0), "routing_exact_vs_single_gpu": bool(agg[2] == 0.0),
+                    "ranks": world, "rows_checked": par["rows_checked"] * world,
+                    "rows_vs_single_gpu": par["rows_vs_single_gpu"] * world})
+
     sweep = []
     for t in sweep_T:
-        ms, _ = timed(t, 10, False)
+        ms, _ = tm.run(t, 10, False)
         for _ in range(2):
             step(t)
         torch.cuda.synchronize()
         selt = si_dev[:t].cpu().numpy()
         b = kernel_bytes(cfg, weights, selt, t)["layer"]
         m = statistics.median(ms)
+        hbm = peaks()[0]
         sweep.append({"T": t, "tokens_per_s": round(t / (m / 1e3), 1), "us_per_layer": round(1e3 * m, 2),
                       "layer_gbs": round(b / (m / 1e3) / 1e9, 1), "layer_hbm_frac": round(b / (m / 1e3) / 1e9 / hbm, 4)})
 
@@ -405,31 +568,42 @@ def run_ours(args):
     if rank == 0 and world == 1 and not args.no_cpu:
         threads = os.cpu_count() or 1
         v, n, el = cpu_baseline(cfg, weights, x_host[:T], args.cpu_seconds, threads)
-        cpu = {"value": round(v, 3), "unit": "tokens/s", "cores": threads, "kind": "port",
+        cpu = {"value": round(v, 3), "unit": UNIT, "cores": threads, "kind": "port",
                "sample": f"{n} tokens of the T={T} workload in {el:.1f} s (oracle, one token at a time)"}
+
+    configs = []
+    if world == 1 and not args.no_configs:
+        ctx.close()   # frees the headline layer before the larger ones
+        for cid, t in EXTRA_CONFIGS:
+            if cid == args.config and t == T:
+                continue
+            try:
+                configs.append(extra_config(torch, jm, synth, cid, t, stream, flush, tensor_peaks))
+            except Exception as e:
+                configs.append({"workload": f"{synth.CONFIGS[cid].name} T={t}", "error": str(e)[:300]})
 
     if rank == 0:
         line = {
-            "metric": "MoE-layer tokens/s", "value": round(value, 1), "unit": "tokens/s", "n_gpus": world,
+            "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(layer_ms, 5),
             "higher_is_better": True, "scaling": "strong" if (ep and args.strong) else "weak",
             "vs_baseline": None, "dtype": "int8",
             "data": "synthetic (seeded N(0,1) activations, N(0,0.02) weights quantised to GGUF blocks)",
-            "config": {"workload": f"{cfg.name} T={T}", "T": T, "H": cfg.H, "E": cfg.E, "k": cfg.k, "I": cfg.I,
-                       "S": cfg.S, "quant": "Q4_K" if cfg.quant == 12 else "Q8_0",
-                       "experts_routed": kb["U"], "global_batch": world * T,
-                       "parallelism": f"ep{world}" if ep else "single",
-                       "l2": "flushed between timed steps (256 MiB write); per-step CUDA events",
-                       **({"flags": args.flags} if args.flags else {})},
+            "config": workload_config(cfg, T, world, args.strong, U_global),
+            "timing": "L2 flushed between timed steps (256 MiB write); per-step CUDA events on the library's "
+                      "stream; max over ranks" + (f"; context flags {args.flags}" if args.flags else ""),
             "roofline": roofline,
             "layer_roofline": {"bytes": int(kb["layer"]), "gbs": round(kb["layer"] / (layer_ms / 1e3) / 1e9, 1),
-                               "frac": round(kb["layer"] / (layer_ms / 1e3) / 1e9 / hbm, 4)},
+                               "frac": round(kb["layer"] / (layer_ms / 1e3) / 1e9 / peaks()[0], 4)},
             "kernels": kernels,
             "gpu_launches": int(launches),
-            "e2e": {"value": round(e2e, 1), "unit": "tokens/s",
+            "parity": par,
+            "e2e": {"value": round(e2e, 1), "unit": UNIT,
                     "h2d_bytes_per_step": int(T * cfg.H * 4),
                     "d2h_bytes_per_step": int(T * cfg.H * 4 + (0 if ep else T * cfg.k * 8))},
             "sweep": sweep,
+            "configs": configs,
+            "tensor_peaks": tensor_peaks,
             "cpu_baseline": cpu,
             "clocks": clocks,
         }

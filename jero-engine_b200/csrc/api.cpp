@@ -162,6 +162,8 @@ struct moe_ctx {
     std::string last_error;
     // last forward, for moe_debug_permutation
     int last_layer = -1, last_T = 0;
+    int32_t *dbg_isum = nullptr;   // moe_debug_capture_block_sums
+    uint64_t dbg_isum_cap = 0;
     int num_sms = 148;
     int *status_host = nullptr;   // pinned word for the device status flag
     Profiler prof;
@@ -530,6 +532,8 @@ FwdParams local_params(moe_ctx *ctx, const LayerStore &L, int T, int ptr_kind, c
     p.a16_stride = s.H; p.a16dn_stride = s.W; p.slots_cap = s.slots_cap;
     p.dep = s.dep;
     p.dep_done = s.dep ? s.dep + s.dep_cap : nullptr;
+    const uint64_t isum_need = (uint64_t)T * (L.k + (L.S ? 1 : 0)) * 2 * L.I * (L.H / 32);
+    p.dbg_isum = ctx->dbg_isum && isum_need <= ctx->dbg_isum_cap ? ctx->dbg_isum : nullptr;
     p.dep_cap = s.dep_cap;
     p.x16 = T < MOE_TENSOR_CORE_MIN_TOKENS ? s.x16 : nullptr;
     p.use_tc = use_tensor_cores(ctx->spec, L, s, T);
@@ -1213,6 +1217,15 @@ int moe_debug_permutation(moe_ctx *ctx, int32_t *offsets, int32_t *perm_token, i
                              cudaMemcpyDeviceToHost),
              "copy perm");
     if (T_out) *T_out = ctx->last_T;
+    return MOE_OK;
+}
+
+int moe_debug_capture_block_sums(moe_ctx *ctx, int32_t *device_buf, uint64_t n_ints)
+{
+    if (!ctx) return fail(nullptr, MOE_ERR_INVALID_ARGS, "null context");
+    if (!device_buf != !n_ints) return fail(ctx, MOE_ERR_INVALID_ARGS, "buffer and size go together");
+    ctx->dbg_isum = device_buf;
+    ctx->dbg_isum_cap = n_ints;
     return MOE_OK;
 }
 

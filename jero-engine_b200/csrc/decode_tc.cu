@@ -215,6 +215,16 @@ __device__ __forceinline__ bool epi_item(const FwdParams &p, const TcItem &x, in
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&es.t_empty[tr.slot]);
             }
+            if (NMAT == 2 && p.dbg_isum && !x.shared) {   // parity probe: the raw int32 block sums
+                const size_t f = (size_t)x.nt * kDM + r, nb = (size_t)(p.H >> 5);
+#pragma unroll
+                for (int t = 0; t < NT; t++)
+#pragma unroll
+                    for (int bb = 0; bb < BG; bb++)
+                        if (t < x.n)
+                            p.dbg_isum[(((size_t)(x.slot + t) * 2 + m) * p.I + f) * nb + 4 * kk + b0 + g + bb] =
+                                (int32_t)S[bb][t];
+            }
 #pragma unroll
             for (int t = 0; t < NT; t++) {
 #pragma unroll

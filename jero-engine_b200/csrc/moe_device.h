@@ -136,6 +136,11 @@ struct FwdParams {
     int32_t *dep;
     int32_t *dep_done;
     int dep_cap;
+
+    // parity probe (null in production): the int8 tensor-core gate/up launch
+    // stores each routed slot's raw int32 block sums here,
+    // [slot][matrix 0 gate / 1 up][row of I][block of H/32]
+    int32_t *dbg_isum;
 };
 
 // Entries of FwdParams::dep a forward over T tokens may use: one per slot

@@ -13,8 +13,8 @@ from __future__ import annotations
 
 import ctypes as C
 import os
-from dataclasses import dataclass, field
-from typing import Dict, Optional, Sequence
+from dataclasses import dataclass
+from typing import Optional, Sequence
 
 import numpy as np
 
@@ -22,21 +22,16 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libjeromoe.so")
 
 # ---------------------------------------------------------------- constants
-MOE_OK = 0
-MOE_ERR_INVALID_ARGS = 2
-MOE_ERR_CAPABILITY_MISMATCH = 10
-MOE_ERR_INSUFFICIENT_MEMORY = 11
-MOE_ERR_RESOURCE_EXHAUSTED = 12
-MOE_ERR_TENSOR_BOUNDS = 14
-MOE_ERR_CONTEXT_LENGTH = 15
-MOE_ERR_NOT_UPLOADED = 16
-MOE_ERR_CUDA = 20
-MOE_ERR_NCCL = 21
-MOE_ERR_TIMEOUT = 22
+# status codes, quant ids, the K3Error-named exceptions and the GGUF tensor
+# containers are plain Python (moe_types); re-exported here
+from moe_types import (  # noqa: F401,E402
+    MOE_OK, MOE_ERR_INVALID_ARGS, MOE_ERR_CAPABILITY_MISMATCH, MOE_ERR_INSUFFICIENT_MEMORY,
+    MOE_ERR_RESOURCE_EXHAUSTED, MOE_ERR_TENSOR_BOUNDS, MOE_ERR_CONTEXT_LENGTH, MOE_ERR_NOT_UPLOADED, MOE_ERR_CUDA,
+    MOE_ERR_NCCL, MOE_ERR_TIMEOUT, F32, Q8_0, Q4_K, QUANT_NAMES, ROUTE_SOFTMAX_TOPK, ROUTE_GROUP_LIMITED, MoeError,
+    InvalidArguments, CapabilityMismatch, InsufficientLockableMemory, ResourceExhausted, TensorBoundsError,
+    ContextLengthExceeded, NotUploaded, CudaError, NcclError, DeviceTimeout, Tensor, f32_tensor, ModelWeights,
+    RouteSpec, ERRORS as _ERRORS)
 
-F32, Q8_0, Q4_K = 0, 8, 12
-QUANT_NAMES = {F32: "F32", Q8_0: "Q8_0", Q4_K: "Q4_K"}
-ROUTE_SOFTMAX_TOPK, ROUTE_GROUP_LIMITED = 0, 1
 PTR_HOST, PTR_DEVICE = 0, 1
 FLAG_TENSOR_CORES_ALWAYS, FLAG_TENSOR_CORES_NEVER = 1, 2
 FLAG_EP_NCCL_ONLY = 4   # expert parallelism: NCCL exchange for every batch size
@@ -44,41 +39,6 @@ FLAG_EP_NCCL_ONLY = 4   # expert parallelism: NCCL exchange for every batch size
 FLAG_INT8_TENSOR_CORES_NEVER, FLAG_INT8_TENSOR_CORES_ALWAYS = 8, 16
 FLAG_FUSED_TC_NEVER = 32   # small batches: no fused f16 tensor-core expert launch
 TENSOR_CORE_MIN_TOKENS = 256
-
-
-class MoeError(RuntimeError):
-    code = -1
-
-    def __init__(self, code, msg):
-        super().__init__(f"[{code}] {msg}")
-        self.code = code
-        self.msg = msg
-
-
-class InvalidArguments(MoeError): pass
-class CapabilityMismatch(MoeError): pass
-class InsufficientLockableMemory(MoeError): pass
-class ResourceExhausted(MoeError): pass
-class TensorBoundsError(MoeError): pass
-class ContextLengthExceeded(MoeError): pass
-class NotUploaded(MoeError): pass
-class CudaError(MoeError): pass
-class NcclError(MoeError): pass
-class DeviceTimeout(MoeError): pass
-
-
-_ERRORS = {
-    MOE_ERR_INVALID_ARGS: InvalidArguments,
-    MOE_ERR_CAPABILITY_MISMATCH: CapabilityMismatch,
-    MOE_ERR_INSUFFICIENT_MEMORY: InsufficientLockableMemory,
-    MOE_ERR_RESOURCE_EXHAUSTED: ResourceExhausted,
-    MOE_ERR_TENSOR_BOUNDS: TensorBoundsError,
-    MOE_ERR_CONTEXT_LENGTH: ContextLengthExceeded,
-    MOE_ERR_NOT_UPLOADED: NotUploaded,
-    MOE_ERR_CUDA: CudaError,
-    MOE_ERR_NCCL: NcclError,
-    MOE_ERR_TIMEOUT: DeviceTimeout,
-}
 
 # ------------------------------------------------------------------- structs
 
@@ -145,6 +105,7 @@ EXPORTS = {
                                    C.POINTER(C.c_int32)]),
     "moe_last_error_message": (C.c_char_p, [C.c_void_p]),
     "moe_debug_permutation": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.POINTER(C.c_int32)]),
+    "moe_debug_capture_block_sums": (C.c_int, [C.c_void_p, C.c_void_p, C.c_uint64]),
     "moe_debug_block_dots": (C.c_int, [C.c_int32, C.c_int32, C.c_void_p, C.c_void_p, C.c_int32, C.c_int32,
                                        C.c_void_p, C.c_void_p, C.c_void_p]),
     "moe_route_noalloc": (C.c_int, [C.c_int32, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int32,
@@ -223,60 +184,17 @@ def gen_normal(seed: int, stream: int, n: int, sigma: float, n_threads: int = 0)
 # ------------------------------------------------------------------ tensors
 
 
-@dataclass
-class Tensor:
-    """A GGUF tensor: raw bytes + quant + GGUF shape (jero_core::TensorView)."""
-    quant: int
-    shape: Sequence[int]
-    data: np.ndarray  # uint8 (or float32 for F32) C-contiguous
-
-    def to_c(self) -> moe_tensor:
-        t = moe_tensor()
-        raw = self.data
-        t.data = raw.ctypes.data
-        t.nbytes = raw.nbytes
-        t.quant = self.quant
-        t.n_dims = len(self.shape)
-        for i, s in enumerate(self.shape):
-            t.shape[i] = int(s)
-        return t
-
-
-def f32_tensor(values: np.ndarray, shape: Sequence[int]) -> Tensor:
-    return Tensor(F32, list(shape), np.ascontiguousarray(values, dtype=np.float32))
-
-
-class ModelWeights:
-    """Name -> Tensor map, the role of jero_core::ModelWeights in the reference."""
-
-    def __init__(self, tensors: Optional[Dict[str, Tensor]] = None):
-        self.tensors: Dict[str, Tensor] = dict(tensors or {})
-
-    def contains_tensor(self, name: str) -> bool:
-        return name in self.tensors
-
-    def tensor(self, name: str) -> Tensor:
-        if name not in self.tensors:
-            raise TensorBoundsError(MOE_ERR_TENSOR_BOUNDS, f"tensor '{name}' not present")
-        return self.tensors[name]
-
-    def tensor_count(self) -> int:
-        return len(self.tensors)
-
-    def total_weight_bytes(self) -> int:
-        return sum(t.data.nbytes for t in self.tensors.values())
-
-    def insert(self, name: str, t: Tensor):
-        self.tensors[name] = t
-
-
-@dataclass
-class RouteSpec:
-    mode: int = ROUTE_SOFTMAX_TOPK
-    normalize: bool = True
-    n_groups: int = 0
-    topk_groups: int = 0
-    routed_scale: float = 1.0
+def tensor_c(t: Tensor) -> moe_tensor:
+    """moe_tensor view of a GGUF tensor (the caller keeps t alive)."""
+    c = moe_tensor()
+    raw = t.data
+    c.data = raw.ctypes.data
+    c.nbytes = raw.nbytes
+    c.quant = t.quant
+    c.n_dims = len(t.shape)
+    for i, dim in enumerate(t.shape):
+        c.shape[i] = int(dim)
+    return c
 
 
 def layer_desc(weights: ModelWeights, layer: int, num_experts: int, top_k: int, expert_ffn_dim: int,
@@ -313,7 +231,7 @@ def layer_desc(weights: ModelWeights, layer: int, num_experts: int, top_k: int, 
         if weights.contains_tensor(tname):
             t = weights.tensor(tname)
             keep.append(t)
-            setattr(d, field_name, t.to_c())
+            setattr(d, field_name, tensor_c(t))
     return d, keep
 
 
@@ -443,6 +361,11 @@ class Context:
         r = moe_residency()
         _check(lib.moe_residency_summary(self.h, C.byref(r)), self.h)
         return r
+
+    def debug_capture_block_sums(self, device_ptr: int, n_ints: int):
+        """Raw int32 block sums of the int8 tensor-core gate/up launch go to this
+        device buffer (0, 0: off); layout [slot][gate/up][row of I][block]."""
+        _check(lib.moe_debug_capture_block_sums(self.h, C.c_void_p(device_ptr or None), n_ints), self.h)
 
     def debug_permutation(self, E: int, k: int):
         T = C.c_int32()

@@ -11,15 +11,37 @@ is a prefix of a larger one and experts can be generated independently:
 Rows whose length is not a whole number of Q4_K super-blocks (the routed down
 projection of config 3 has 1408 columns) use Q8_0, as GGUF quantisers fall
 back to another block type for such tensors.
+
+The generator and the quantiser come from the product library (jeromoe) by
+default; use_backend(module) swaps in any module with the same gen_normal /
+quantize_rows functions (the CPU oracle's restatement, which produces the same
+bytes, lets the benchmark's reference arm build its layers without loading
+the product library).
 """
 from __future__ import annotations
 
-from dataclasses import dataclass, field
-from typing import Optional
+from dataclasses import dataclass
 
 import numpy as np
 
-import jeromoe as jm
+import moe_types as jm
+
+_backend = None
+
+
+def use_backend(module) -> None:
+    """Module providing gen_normal(seed, stream, n, sigma, n_threads) and
+    quantize_rows(quant, src, n_threads); None: the product library."""
+    global _backend
+    _backend = module
+
+
+def _be():
+    global _backend
+    if _backend is None:
+        import jeromoe
+        _backend = jeromoe
+    return _backend
 
 WEIGHT_SIGMA = 0.02
 
@@ -73,37 +95,37 @@ def expert_stream(e: int, which: int) -> int:
 
 
 def pick_quant(quant: int, cols: int) -> int:
-    return quant if jm.row_bytes(quant, cols) else jm.Q8_0
+    return quant if jm.gguf_row_bytes(quant, cols) else jm.Q8_0
 
 
 def gen_x(cfg: MoeConfig, T: int, n_threads: int = 0) -> np.ndarray:
-    return jm.gen_normal(cfg.seed, STREAM_X, T * cfg.H, 1.0, n_threads).reshape(T, cfg.H)
+    return _be().gen_normal(cfg.seed, STREAM_X, T * cfg.H, 1.0, n_threads).reshape(T, cfg.H)
 
 
 def _stack(cfg: MoeConfig, rows: int, cols: int, which: int, n_threads: int):
     q = pick_quant(cfg.quant, cols)
-    rb = jm.row_bytes(q, cols)
+    rb = jm.gguf_row_bytes(q, cols)
     out = np.empty((cfg.E, rows * rb), dtype=np.uint8)
     for e in range(cfg.E):
-        w = jm.gen_normal(cfg.seed, expert_stream(e, which), rows * cols, WEIGHT_SIGMA, n_threads)
-        out[e] = jm.quantize_rows(q, w.reshape(rows, cols), n_threads).reshape(-1)
+        w = _be().gen_normal(cfg.seed, expert_stream(e, which), rows * cols, WEIGHT_SIGMA, n_threads)
+        out[e] = _be().quantize_rows(q, w.reshape(rows, cols), n_threads).reshape(-1)
     return jm.Tensor(q, [cols, rows, cfg.E], out.reshape(-1))
 
 
 def _matrix(cfg: MoeConfig, rows: int, cols: int, stream: int, n_threads: int):
     q = pick_quant(cfg.quant, cols)
-    w = jm.gen_normal(cfg.seed, stream, rows * cols, WEIGHT_SIGMA, n_threads)
-    return jm.Tensor(q, [cols, rows], jm.quantize_rows(q, w.reshape(rows, cols), n_threads).reshape(-1))
+    w = _be().gen_normal(cfg.seed, stream, rows * cols, WEIGHT_SIGMA, n_threads)
+    return jm.Tensor(q, [cols, rows], _be().quantize_rows(q, w.reshape(rows, cols), n_threads).reshape(-1))
 
 
 def build_weights(cfg: MoeConfig, layer: int = 0, n_threads: int = 0) -> jm.ModelWeights:
     """GGUF-named tensors of one MoE layer for cfg."""
     w = jm.ModelWeights()
     H, E, I, S = cfg.H, cfg.E, cfg.I, cfg.S
-    router = jm.gen_normal(cfg.seed, STREAM_ROUTER, E * H, WEIGHT_SIGMA, n_threads)
+    router = _be().gen_normal(cfg.seed, STREAM_ROUTER, E * H, WEIGHT_SIGMA, n_threads)
     w.insert(f"blk.{layer}.ffn_gate_inp.weight", jm.f32_tensor(router, [H, E]))
     if cfg.logit_bias_sigma:
-        lb = jm.gen_normal(cfg.seed, STREAM_LOGIT_BIAS, E, cfg.logit_bias_sigma, n_threads)
+        lb = _be().gen_normal(cfg.seed, STREAM_LOGIT_BIAS, E, cfg.logit_bias_sigma, n_threads)
         w.insert(f"blk.{layer}.ffn_gate_inp.logit_bias", jm.f32_tensor(lb, [E]))
     w.insert(f"blk.{layer}.ffn_gate_exps.weight", _stack(cfg, I, H, 0, n_threads))
     w.insert(f"blk.{layer}.ffn_up_exps.weight", _stack(cfg, I, H, 1, n_threads))
@@ -116,7 +138,8 @@ def build_weights(cfg: MoeConfig, layer: int = 0, n_threads: int = 0) -> jm.Mode
 
 
 def desc_for(cfg: MoeConfig, weights: jm.ModelWeights, layer: int = 0):
-    return jm.layer_desc(weights, layer, cfg.E, cfg.k, cfg.I, cfg.S > 0, cfg.route, hidden=cfg.H)
+    import jeromoe
+    return jeromoe.layer_desc(weights, layer, cfg.E, cfg.k, cfg.I, cfg.S > 0, cfg.route, hidden=cfg.H)
 
 
 def algorithmic_bytes(cfg: MoeConfig, weights: jm.ModelWeights, sel_idx: np.ndarray, T: int, layer: int = 0) -> int:

@@ -407,7 +407,7 @@ typedef struct {
     const float *router;
     int e, H, r0, r1;
     const float *x;
-    const int8_t *xq;
+    const int8_t *xq;         /* NULL: quantised rows are dequantised and dotted with x in f32 */
     const float *dx;
     float *out;
 } mv_chunk;
@@ -421,10 +421,18 @@ static void run_chunk(const mv_chunk *c)
     const orc_matrix *m = c->m;
     size_t rb = orc_row_bytes(m->type, m->cols);
     const uint8_t *base = m->data + (size_t)c->e * m->expert_stride;
+    float wrow[16384];
     for (int r = c->r0; r < c->r1; r++) {
         const uint8_t *row = base + (size_t)r * rb;
-        c->out[r] = (m->type == ORC_F32) ? row_dot_f32((const float *)row, c->x, m->cols)
-                                         : orc_row_dot_q(m->type, row, c->xq, c->dx, m->cols);
+        if (m->type == ORC_F32) {
+            c->out[r] = row_dot_f32((const float *)row, c->x, m->cols);
+        } else if (c->xq) {
+            c->out[r] = orc_row_dot_q(m->type, row, c->xq, c->dx, m->cols);
+        } else if (m->cols <= 16384 && orc_dequantize_row(m->type, row, m->cols, wrow) == ORC_OK) {
+            c->out[r] = row_dot_f32(wrow, c->x, m->cols);   /* the other reading of vec_dot_* */
+        } else {
+            c->out[r] = NAN;
+        }
     }
 }
 
@@ -558,8 +566,10 @@ static void swiglu_expert(const orc_matrix *G, const orc_matrix *U, const orc_ma
     matvec(G, e, x, xq, dx, s->g, n_threads);
     matvec(U, e, x, xq, dx, s->u, n_threads);
     for (int i = 0; i < I; i++) s->a[i] = (s->g[i] / (1.0f + expf(-s->g[i]))) * s->u[i];
-    if (D->type != ORC_F32) orc_quantize_act(s->a, I, s->aq, s->adx);
-    matvec(D, e, s->a, s->aq, s->adx, s->y, n_threads);
+    /* xq == NULL: f32 activations throughout (no block quantisation of a) */
+    int quant = D->type != ORC_F32 && xq != NULL;
+    if (quant) orc_quantize_act(s->a, I, s->aq, s->adx);
+    matvec(D, e, s->a, quant ? s->aq : NULL, s->adx, s->y, n_threads);
 }
 
 static int check_matrix(const orc_matrix *m, int rows, int cols)
@@ -578,6 +588,17 @@ static int check_matrix(const orc_matrix *m, int rows, int cols)
 int orc_moe_forward(const orc_layer *L, int T, const float *x, float *out,
                     int32_t *sel_idx, float *sel_w, int n_threads)
 {
+    return orc_moe_forward_ex(L, T, x, out, sel_idx, sel_w, n_threads, 0);
+}
+
+/* act_f32 = 1: the same block with the other reading of the reference's
+ * quantised dots (vec_dot_q8_0 / vec_dot_q4_k_m, src/gemma.rs:66-95): every
+ * weight row dequantised to f32 (orc_dequantize_row) and dotted with the f32
+ * activations (sequential multiply-then-add), no activation quantisation of x
+ * or of the SwiGLU output. Routing is the same in both readings. */
+int orc_moe_forward_ex(const orc_layer *L, int T, const float *x, float *out,
+                       int32_t *sel_idx, float *sel_w, int n_threads, int act_f32)
+{
     int H = L->hidden, E = L->n_experts, k = L->top_k;
     if (T < 0 || H <= 0 || E <= 0 || k <= 0 || k > E || !L->router) return ORC_ERR_ARG;
     int I = L->gate.rows;
@@ -587,8 +608,8 @@ int orc_moe_forward(const orc_layer *L, int T, const float *x, float *out,
     if (S && (check_matrix(&L->sh_gate, S, H) || check_matrix(&L->sh_up, S, H) ||
               check_matrix(&L->sh_down, H, S)))
         return ORC_ERR_ARG;
-    int need_q = L->gate.type != ORC_F32 || L->up.type != ORC_F32 ||
-                 (S && (L->sh_gate.type != ORC_F32 || L->sh_up.type != ORC_F32));
+    int need_q = !act_f32 && (L->gate.type != ORC_F32 || L->up.type != ORC_F32 ||
+                              (S && (L->sh_gate.type != ORC_F32 || L->sh_up.type != ORC_F32)));
     if (need_q && H % 32) return ORC_ERR_ARG;
     if (n_threads < 1) n_threads = 1;
     pool_resize(n_threads - 1);
@@ -611,13 +632,13 @@ int orc_moe_forward(const orc_layer *L, int T, const float *x, float *out,
         if (need_q) orc_quantize_act(xt, H, xq, xdx);
         for (int h = 0; h < H; h++) ot[h] = 0.0f;
         if (S) {
-            swiglu_expert(&L->sh_gate, &L->sh_up, &L->sh_down, 0, xt, xq, xdx, &s, n_threads);
+            swiglu_expert(&L->sh_gate, &L->sh_up, &L->sh_down, 0, xt, act_f32 ? NULL : xq, xdx, &s, n_threads);
             for (int h = 0; h < H; h++) ot[h] += s.y[h];
         }
         router_matvec(L->router, xt, E, H, logits, n_threads);
         int n = orc_select(L, logits, idx, wsel);
         for (int r = 0; r < n; r++) {
-            swiglu_expert(&L->gate, &L->up, &L->down, idx[r], xt, xq, xdx, &s, n_threads);
+            swiglu_expert(&L->gate, &L->up, &L->down, idx[r], xt, act_f32 ? NULL : xq, xdx, &s, n_threads);
             for (int h = 0; h < H; h++) ot[h] += wsel[r] * s.y[h];
         }
         for (int r = 0; r < k; r++) {
@@ -648,3 +669,201 @@ int orc_permutation(const int32_t *sel_idx, int T, int k, int E, int32_t *offset
     free(fill);
     return ORC_OK;
 }
+
+/* ------------------------------------------------------ synthetic inputs */
+
+/* Seeded inputs of the benchmark configurations, restated independently of
+ * the library's moe_gen_normal / moe_quantize_rows so that the reference arm
+ * of the benchmark can build the same layers without loading the product
+ * library (tests check the two byte for byte). */
+
+static inline uint64_t orc_mix64(uint64_t z)
+{
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;   /* splitmix64 finaliser (Vigna) */
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}
+
+typedef struct {
+    uint64_t key, lo, hi, n;
+    float sigma;
+    float *dst;
+} gen_job;
+
+static void *gen_run(void *arg)
+{
+    const gen_job *j = (const gen_job *)arg;
+    const uint64_t G = 0x9E3779B97F4A7C15ull;
+    for (uint64_t m = j->lo; m < j->hi; m++) {
+        /* pair m: two uniforms from the counter stream, Box-Muller */
+        uint64_t r1 = orc_mix64(j->key + (2 * m + 1) * G);
+        uint64_t r2 = orc_mix64(j->key + (2 * m + 2) * G);
+        double u1 = (double)((r1 >> 11) + 1) * 0x1.0p-53;
+        double u2 = (double)(r2 >> 11) * 0x1.0p-53;
+        double rad = sqrt(-2.0 * log(u1));
+        double th = 6.283185307179586 * u2;
+        j->dst[2 * m] = (float)(rad * cos(th) * (double)j->sigma);
+        if (2 * m + 1 < j->n) j->dst[2 * m + 1] = (float)(rad * sin(th) * (double)j->sigma);
+    }
+    return NULL;
+}
+
+/* Element i of (seed, stream): normal pair i/2 of the counter stream keyed by
+ * mix(seed ^ mix(stream + G)), G the splitmix64 increment. */
+int orc_gen_normal(uint64_t seed, uint64_t stream, uint64_t n, float sigma, float *dst, int n_threads)
+{
+    const uint64_t G = 0x9E3779B97F4A7C15ull;
+    uint64_t key = orc_mix64(seed ^ orc_mix64(stream + G));
+    uint64_t pairs = (n + 1) / 2;
+    if (n_threads < 1) n_threads = 1;
+    if (n_threads > 64) n_threads = 64;
+    if ((uint64_t)n_threads > pairs) n_threads = pairs ? (int)pairs : 1;
+    pthread_t th[64];
+    gen_job jobs[64];
+    int ok[64] = {0};
+    uint64_t chunk = (pairs + n_threads - 1) / n_threads;
+    for (int t = 0; t < n_threads; t++) {
+        jobs[t].key = key;
+        jobs[t].lo = t * chunk < pairs ? t * chunk : pairs;
+        jobs[t].hi = (t + 1) * chunk < pairs ? (t + 1) * chunk : pairs;
+        jobs[t].n = n;
+        jobs[t].sigma = sigma;
+        jobs[t].dst = dst;
+    }
+    for (int t = 1; t < n_threads; t++) ok[t] = pthread_create(&th[t], NULL, gen_run, &jobs[t]) == 0;
+    gen_run(&jobs[0]);
+    for (int t = 1; t < n_threads; t++) {
+        if (ok[t]) pthread_join(th[t], NULL);
+        else gen_run(&jobs[t]);
+    }
+    return ORC_OK;
+}
+
+static inline uint16_t f32_to_f16_rne(float f)
+{
+    _Float16 h = (_Float16)f;   /* round to nearest even */
+    uint16_t b;
+    memcpy(&b, &h, 2);
+    return b;
+}
+
+static inline float clampf(float v, float lo, float hi) { return v < lo ? lo : (v > hi ? hi : v); }
+
+/* Q8_0 block: d = f16(amax / 127); q = round(x / d) with the f16 d, clamped to
+ * +-127 (GGUF layout: f16 d, 32 x int8). */
+static void q8_0_row(const float *x, int cols, uint8_t *dst)
+{
+    for (int b = 0; b < cols / 32; b++) {
+        const float *v = x + 32 * b;
+        float amax = 0.0f;
+        for (int i = 0; i < 32; i++) amax = fmaxf(amax, fabsf(v[i]));
+        uint16_t dh = f32_to_f16_rne(amax / 127.0f);
+        float d = orc_f16_to_f32(dh);
+        float id = d > 0.0f ? 1.0f / d : 0.0f;
+        uint8_t *o = dst + 34 * b;
+        o[0] = (uint8_t)(dh & 0xFF);
+        o[1] = (uint8_t)(dh >> 8);
+        for (int i = 0; i < 32; i++) o[2 + i] = (uint8_t)(int8_t)clampf(roundf(v[i] * id), -127.0f, 127.0f);
+    }
+}
+
+/* Q4_K super-block of 256 values: per 32-value sub-block j, scale_j = (max -
+ * min) / 15 and min_j = -min (min taken with 0); d = max scale_j / 63 and
+ * dmin = max min_j / 63 as f16; sc_j = round(scale_j / d), m_j = round(min_j /
+ * dmin) in 0..63; q = round((x + dmin m_j) / (d sc_j)) in 0..15. GGUF layout:
+ * f16 d, f16 dmin, 12 bytes of 6-bit sc / m, 128 bytes of nibbles (value 64g+l
+ * low nibble of byte 32g+l, value 64g+32+l its high nibble). */
+static void q4_k_row(const float *x, int cols, uint8_t *dst)
+{
+    for (int sb = 0; sb < cols / 256; sb++) {
+        const float *v = x + 256 * sb;
+        float scale[8], mn[8];
+        for (int j = 0; j < 8; j++) {
+            float lo = 0.0f, hi = -INFINITY;
+            for (int i = 0; i < 32; i++) {
+                lo = fminf(lo, v[32 * j + i]);
+                hi = fmaxf(hi, v[32 * j + i]);
+            }
+            scale[j] = (hi - lo) / 15.0f;
+            mn[j] = -lo;
+        }
+        float ms = 0.0f, mm = 0.0f;
+        for (int j = 0; j < 8; j++) {
+            ms = fmaxf(ms, scale[j]);
+            mm = fmaxf(mm, mn[j]);
+        }
+        uint16_t dh = f32_to_f16_rne(ms / 63.0f), mh = f32_to_f16_rne(mm / 63.0f);
+        float d = orc_f16_to_f32(dh), dmin = orc_f16_to_f32(mh);
+        int sc[8], m[8];
+        for (int j = 0; j < 8; j++) {
+            sc[j] = d > 0.0f ? (int)clampf(roundf(scale[j] / d), 0.0f, 63.0f) : 0;
+            m[j] = dmin > 0.0f ? (int)clampf(roundf(mn[j] / dmin), 0.0f, 63.0f) : 0;
+        }
+        uint8_t *o = dst + 144 * sb;
+        o[0] = (uint8_t)(dh & 0xFF);
+        o[1] = (uint8_t)(dh >> 8);
+        o[2] = (uint8_t)(mh & 0xFF);
+        o[3] = (uint8_t)(mh >> 8);
+        uint8_t *k = o + 4;
+        for (int j = 0; j < 4; j++) {   /* the inverse of q4k_scale_min */
+            k[j] = (uint8_t)((sc[j] & 63) | ((sc[j + 4] >> 4) << 6));
+            k[j + 4] = (uint8_t)((m[j] & 63) | ((m[j + 4] >> 4) << 6));
+            k[j + 8] = (uint8_t)((sc[j + 4] & 15) | ((m[j + 4] & 15) << 4));
+        }
+        uint8_t q[256];
+        for (int j = 0; j < 8; j++) {
+            float ds = d * (float)sc[j], dm = dmin * (float)m[j];
+            for (int i = 0; i < 32; i++)
+                q[32 * j + i] = (uint8_t)clampf(ds > 0.0f ? roundf((v[32 * j + i] + dm) / ds) : 0.0f, 0.0f, 15.0f);
+        }
+        for (int g = 0; g < 4; g++)
+            for (int l = 0; l < 32; l++) o[16 + 32 * g + l] = (uint8_t)(q[64 * g + l] | (q[64 * g + 32 + l] << 4));
+    }
+}
+
+typedef struct {
+    int type, cols;
+    const float *src;
+    uint8_t *dst;
+    int64_t lo, hi;
+} quant_job;
+
+static void *quant_run(void *arg)
+{
+    const quant_job *j = (const quant_job *)arg;
+    size_t rb = orc_row_bytes(j->type, j->cols);
+    for (int64_t r = j->lo; r < j->hi; r++) {
+        const float *x = j->src + (size_t)r * j->cols;
+        uint8_t *o = j->dst + (size_t)r * rb;
+        if (j->type == ORC_F32) memcpy(o, x, rb);
+        else if (j->type == ORC_Q8_0) q8_0_row(x, j->cols, o);
+        else q4_k_row(x, j->cols, o);
+    }
+    return NULL;
+}
+
+/* rows x cols f32 -> GGUF rows of type (F32, Q8_0 or Q4_K). */
+int orc_quantize_rows(int type, const float *src, int64_t rows, int cols, uint8_t *dst, int n_threads)
+{
+    if (!orc_row_bytes(type, cols) || (type != ORC_F32 && type != ORC_Q8_0 && type != ORC_Q4_K) || rows < 0)
+        return ORC_ERR_ARG;
+    if (n_threads < 1) n_threads = 1;
+    if (n_threads > 64) n_threads = 64;
+    if (rows < n_threads) n_threads = rows > 0 ? (int)rows : 1;
+    pthread_t th[64];
+    quant_job jobs[64];
+    int64_t chunk = (rows + n_threads - 1) / n_threads;
+    int ok[64] = {0};
+    for (int t = 0; t < n_threads; t++) {
+        jobs[t] = (quant_job){type, cols, src, dst, t * chunk < rows ? t * chunk : rows,
+                              (t + 1) * chunk < rows ? (t + 1) * chunk : rows};
+    }
+    for (int t = 1; t < n_threads; t++) ok[t] = pthread_create(&th[t], NULL, quant_run, &jobs[t]) == 0;
+    quant_run(&jobs[0]);
+    for (int t = 1; t < n_threads; t++) {
+        if (ok[t]) pthread_join(th[t], NULL);
+        else quant_run(&jobs[t]);
+    }
+    return ORC_OK;
+}
+

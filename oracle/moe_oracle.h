@@ -99,6 +99,18 @@ int orc_moe_forward(const orc_layer *L, int T, const float *x, float *out,
 int orc_permutation(const int32_t *sel_idx, int T, int k, int E,
                     int32_t *offsets, int32_t *perm_token);
 
+/* orc_moe_forward with act_f32 = 1: quantised weight rows dequantised to f32
+ * and dotted with f32 activations (no activation blocks), the other reading
+ * of the reference's vec_dot_q8_0 / vec_dot_q4_k_m. act_f32 = 0 is
+ * orc_moe_forward. */
+int orc_moe_forward_ex(const orc_layer *L, int T, const float *x, float *out,
+                       int32_t *sel_idx, float *sel_w, int n_threads, int act_f32);
+
+/* ---- synthetic inputs (same bytes as the library's moe_gen_normal and
+ * moe_quantize_rows; used to build the benchmark's layers without it) ---- */
+int orc_gen_normal(uint64_t seed, uint64_t stream, uint64_t n, float sigma, float *dst, int n_threads);
+int orc_quantize_rows(int type, const float *src, int64_t rows, int cols, uint8_t *dst, int n_threads);
+
 #ifdef __cplusplus
 }
 #endif

@@ -53,6 +53,10 @@ def _load():
         "orc_moe_forward": (C.c_int, [C.POINTER(orc_layer), C.c_int, C.c_void_p, C.c_void_p, C.c_void_p,
                                       C.c_void_p, C.c_int]),
         "orc_permutation": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p]),
+        "orc_moe_forward_ex": (C.c_int, [C.POINTER(orc_layer), C.c_int, C.c_void_p, C.c_void_p, C.c_void_p,
+                                         C.c_void_p, C.c_int, C.c_int]),
+        "orc_gen_normal": (C.c_int, [C.c_uint64, C.c_uint64, C.c_uint64, C.c_float, C.c_void_p, C.c_int]),
+        "orc_quantize_rows": (C.c_int, [C.c_int, C.c_void_p, C.c_int64, C.c_int, C.c_void_p, C.c_int]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -162,13 +166,15 @@ class Layer:
         self.H = L.hidden
         self.E = num_experts
 
-    def forward(self, x: np.ndarray, n_threads: int = 1):
+    def forward(self, x: np.ndarray, n_threads: int = 1, act_f32: bool = False):
+        """The block over the rows of x. act_f32: the other reading of the
+        reference's quantised dots (dequantised weights . f32 activations)."""
         x = np.ascontiguousarray(x, dtype=np.float32)
         T = x.shape[0]
         out = np.empty((T, self.H), dtype=np.float32)
         si = np.empty((T, self.k), dtype=np.int32)
         sw = np.empty((T, self.k), dtype=np.float32)
-        rc = lib.orc_moe_forward(C.byref(self.c), T, _p(x), _p(out), _p(si), _p(sw), n_threads)
+        rc = lib.orc_moe_forward_ex(C.byref(self.c), T, _p(x), _p(out), _p(si), _p(sw), n_threads, int(act_f32))
         if rc != 0:
             raise ValueError(f"oracle rejected the layer (code {rc})")
         return out, si, sw
@@ -188,3 +194,30 @@ def permutation(sel_idx: np.ndarray, E: int):
     perm = np.empty(T * k, dtype=np.int32)
     assert lib.orc_permutation(_p(sel_idx), T, k, E, _p(offs), _p(perm)) == 0
     return offs, perm
+
+
+# ---------------------------------------------------- synthetic inputs
+# The same bytes as the product library's moe_gen_normal / moe_quantize_rows,
+# restated here so the benchmark's reference arm builds its layers without
+# loading the product library.
+
+def _threads(n):
+    return n or max(1, min(32, os.cpu_count() or 1))
+
+
+def gen_normal(seed: int, stream: int, n: int, sigma: float, n_threads: int = 0) -> np.ndarray:
+    out = np.empty(n, dtype=np.float32)
+    assert lib.orc_gen_normal(seed, stream, n, sigma, _p(out), _threads(n_threads)) == 0
+    return out
+
+
+def quantize_rows(quant: int, src: np.ndarray, n_threads: int = 0) -> np.ndarray:
+    src = np.ascontiguousarray(src, dtype=np.float32)
+    rows, cols = src.reshape(-1, src.shape[-1]).shape
+    rb = row_bytes(quant, cols)
+    if rb == 0:
+        raise ValueError(f"{cols} columns are not whole blocks of quant {quant}")
+    out = np.empty((rows, rb), dtype=np.uint8)
+    assert lib.orc_quantize_rows(quant, _p(src), rows, cols, _p(out), _threads(n_threads)) == 0
+    return out
+

@@ -25,3 +25,19 @@ def test_reference_arm_json_line():
     assert e2e["value"] == line["value"] and e2e["unit"] == line["unit"]
     assert e2e["h2d_bytes_per_step"] == 0 and e2e["d2h_bytes_per_step"] == 0
     assert line["config"]["workload"].endswith("T=2")
+    assert set(line["config"]) >= {"workload", "T", "H", "E", "k", "I", "S", "quant", "experts_routed",
+                                   "global_batch", "parallelism"}
+
+
+def test_reference_arm_does_not_load_the_product_library():
+    """The reference arm builds its layer with the oracle's generator and
+    quantiser and times the oracle: libjeromoe.so is never mapped."""
+    code = (
+        "import sys, json; sys.argv = ['bench.py', '--impl', 'reference', '--steps', '1', '--warmup', '1',"
+        " '--tokens', '2']; import bench; bench.main();"
+        " maps = open('/proc/self/maps').read();"
+        " print(json.dumps({'jeromoe': 'libjeromoe' in maps, 'oracle': 'liboracle' in maps}))")
+    res = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=600, cwd=ROOT)
+    assert res.returncode == 0, res.stderr[-2000:]
+    loaded = json.loads(res.stdout.strip().splitlines()[-1])
+    assert loaded == {"jeromoe": False, "oracle": True}
