@@ -24,9 +24,11 @@ extern "C" {
 
 #define MOE_ABI_VERSION 1
 
-/* Status codes. Values follow the worker exit codes that the reference maps
- * its K3Error variants to (src/worker/error.rs:10-32); device-side failures
- * get codes of their own. */
+/* Status codes. 2, 10, 11, 12 and 14 are the worker exit codes that the
+ * reference maps its K3Error variants to (src/worker/error.rs:10-32, which
+ * stops at 14); 15 and 16 extend that list for ContextLengthExceeded and for a
+ * layer that was never uploaded, and 20-22 are device-side failures that the
+ * reference (a CPU runtime) does not have. */
 typedef enum moe_status {
     MOE_OK = 0,
     MOE_ERR_INVALID_ARGS = 2,          /* null pointer, bad count, unknown flag */
@@ -291,7 +293,8 @@ int moe_probe_tensor(int32_t device, int32_t kind, int32_t m, int32_t n, int32_t
  * MOE_ERR_CONTEXT_LENGTH. Asynchronous on `stream` (a cudaStream_t). The
  * first call on a device resolves the array's address, so make it before
  * capturing the stream into a graph. Every call shares the array: calls that
- * overlap on the GPU race. Errors: moe_last_error_message(NULL). */
+ * overlap on the GPU race. The calling thread's current device is the same
+ * after the call. Errors: moe_last_error_message(NULL). */
 int moe_route_noalloc(int32_t device, const float *x, const float *router, const float *logit_bias,
                       const float *sel_bias, int32_t T, int32_t H, int32_t E, int32_t top_k, int32_t normalize,
                       float routed_scale, int32_t n_groups, int32_t topk_groups, int32_t *sel_idx, float *sel_w,
@@ -327,6 +330,23 @@ int moe_ep_init(moe_ctx *ctx, int32_t rank, int32_t world, const uint8_t *id);
  * per-expert slot counts (the exchange sizes). */
 int moe_forward_ep(moe_ctx *ctx, int32_t layer, int32_t T, const float *x, float *out,
                    int32_t *sel_idx, float *sel_w, int32_t ptr_kind);
+
+/* After moe_forward_ep (or moe_device_status) reports MOE_ERR_TIMEOUT for a
+ * peer-rank wait -- a peer's flag that did not arrive within the bound, or one
+ * already past the current forward -- the exchange state of the world is lost:
+ * the failing rank stored nothing into any peer's memory for that forward, its
+ * peers' waits run out too, and every later moe_forward_ep fails until every
+ * rank has called moe_ep_reset. Collective: clears this rank's exchange flags
+ * and counters, with a rendezvous before and after so that no rank writes into
+ * a peer before the peer is clean. No counterpart in the reference. */
+int moe_ep_reset(moe_ctx *ctx);
+
+/* Fault injection for tests (no counterpart in the reference): the next
+ * moe_forward_ep on ctx waits for a flag epoch skewed by epoch_skew (a flag
+ * nothing raises), and every peer-flag wait from now on is bounded by
+ * wait_cycles SM clock cycles (0: the default, about 2 s). Makes a bounded
+ * device wait run out without a device fault. */
+int moe_debug_ep_fault(moe_ctx *ctx, uint32_t epoch_skew, int64_t wait_cycles);
 
 /* The exchange plan of one rank, as moe_forward_ep computes it from the
  * all-gathered slot offsets all_offsets [world][E+1] (host work only):

@@ -119,6 +119,9 @@ struct Profiler {
 
 namespace {
 
+// Bound of each peer-flag wait of the peer-memory exchange (about 2 s at 2 GHz).
+constexpr long long kEpWaitCycles = 4000000000LL;
+
 // Expert-parallel state of a context: the communicator and a device arena for
 // the exchange buffers and the local expert stage, grown on demand.
 struct EpState {
@@ -148,6 +151,9 @@ struct EpState {
     uint8_t *p2p_arena = nullptr;
     uint8_t *p2p_peer[kEpMaxRanks] = {};
     uint32_t p2p_epoch = 0;
+    bool p2p_broken = false;      // a flag wait failed: unusable until moe_ep_reset
+    uint32_t dbg_skew = 0;        // test hook (moe_debug_ep_fault): the next forward waits for a skewed epoch
+    long long dbg_wait_cycles = 0;   // test hook: bound of the flag waits (0: the default)
 };
 
 }  // namespace
@@ -1140,8 +1146,48 @@ int moe_device_status(moe_ctx *ctx, int32_t *status)
     *status = *ctx->status_host;
     if (*status) {
         CUDA_TRY(ctx, cudaMemsetAsync(ctx->scratch.err, 0, sizeof(int), ctx->stream), "clear status");
+        if (ctx->ep.world && (*status == kErrEpTimeout || *status == kErrEpDesync)) {
+            ctx->ep.p2p_broken = true;
+            return fail(ctx, MOE_ERR_TIMEOUT,
+                        "a bounded peer-rank wait failed (status %d); call moe_ep_reset on every rank", *status);
+        }
         return fail(ctx, MOE_ERR_TIMEOUT, "a bounded device wait ran out (status %d)", *status);
     }
+    return MOE_OK;
+}
+
+int moe_ep_reset(moe_ctx *ctx)
+{
+    if (!ctx) return fail(nullptr, MOE_ERR_INVALID_ARGS, "null context");
+    EpState &ep = ctx->ep;
+    if (!ep.world) return fail(ctx, MOE_ERR_INVALID_ARGS, "moe_ep_init was not called on this context");
+    const NcclApi *nc = nccl_api();
+    if (!nc) return fail(ctx, MOE_ERR_NCCL, "NCCL unavailable");
+    CUDA_TRY(ctx, cudaSetDevice(ctx->spec.device), "cudaSetDevice");
+    int all[kEpMaxRanks] = {};
+    int rc;
+    // every rank has finished its own forwards before any arena is cleared ...
+    CUDA_TRY(ctx, cudaStreamSynchronize(ctx->stream), "cudaStreamSynchronize");
+    if ((rc = ep_allgather_int(ctx, nc, 1, all))) return rc;
+    if (ep.p2p_arena) CUDA_TRY(ctx, cudaMemset(ep.p2p_arena + ep.p2p.o_flags, 0, ep.p2p.o_peers - ep.p2p.o_flags),
+                               "cudaMemset(peer-exchange arena)");
+    if (ep.p2p_arena) CUDA_TRY(ctx, cudaMemset(ep.p2p_arena + ep.p2p.o_misc, 0, 128), "cudaMemset(tickets)");
+    if (ctx->scratch.err) CUDA_TRY(ctx, cudaMemset(ctx->scratch.err, 0, sizeof(int)), "cudaMemset(status)");
+    CUDA_TRY(ctx, cudaDeviceSynchronize(), "cudaDeviceSynchronize");
+    ep.p2p_epoch = 0;
+    ep.p2p_broken = false;
+    ep.dbg_skew = 0;
+    // ... and before any rank's next forward writes into a peer's arena
+    return ep_allgather_int(ctx, nc, 1, all);
+}
+
+int moe_debug_ep_fault(moe_ctx *ctx, uint32_t epoch_skew, int64_t wait_cycles)
+{
+    if (!ctx) return fail(nullptr, MOE_ERR_INVALID_ARGS, "null context");
+    if (!ctx->ep.world) return fail(ctx, MOE_ERR_INVALID_ARGS, "moe_ep_init was not called on this context");
+    if (wait_cycles < 0) return fail(ctx, MOE_ERR_INVALID_ARGS, "negative wait bound");
+    ctx->ep.dbg_skew = epoch_skew;
+    ctx->ep.dbg_wait_cycles = wait_cycles;
     return MOE_OK;
 }
 
@@ -1374,8 +1420,12 @@ static int ep_forward_p2p(moe_ctx *ctx, LayerStore &L, FwdParams p, int T, int p
     a.rank = me; a.world = G; a.E = E; a.El = El; a.e0 = me * El; a.H = H; a.cap = l.cap;
     a.rb = l.rb; a.o_flags = l.o_flags; a.o_off = l.o_off; a.o_xin = l.o_xin; a.o_yin = l.o_yin;
     a.epoch = ep.p2p_epoch;
+    a.wait_epoch = ep.p2p_epoch + ep.dbg_skew;
+    a.wait_cycles = ep.dbg_wait_cycles > 0 ? ep.dbg_wait_cycles : kEpWaitCycles;
+    ep.dbg_skew = 0;
     a.err = s.err;
     int32_t *misc = reinterpret_cast<int32_t *>(A + l.o_misc);
+    a.ok = misc + 16;
     a.ticket = misc;
     a.n_active = misc + 4;
     a.total = misc + 8;
@@ -1467,8 +1517,14 @@ static int ep_forward_p2p(moe_ctx *ctx, LayerStore &L, FwdParams p, int T, int p
         if (*ctx->status_host) {
             const int code = *ctx->status_host;
             cudaMemsetAsync(s.err, 0, sizeof(int), st);
-            return fail(ctx, MOE_ERR_TIMEOUT, "a bounded %s wait ran out in layer %d (status %d)",
-                        code == kErrEpTimeout ? "peer-rank" : "device", layer, code);
+            if (code == kErrEpTimeout || code == kErrEpDesync) {
+                ep.p2p_broken = true;
+                return fail(ctx, MOE_ERR_TIMEOUT,
+                            "a bounded peer-rank wait %s in layer %d (status %d); the exchange state is lost: "
+                            "call moe_ep_reset on every rank",
+                            code == kErrEpTimeout ? "ran out" : "saw a later forward", layer, code);
+            }
+            return fail(ctx, MOE_ERR_TIMEOUT, "a bounded device wait ran out in layer %d (status %d)", layer, code);
         }
     }
     return MOE_OK;
@@ -1492,6 +1548,9 @@ int moe_forward_ep(moe_ctx *ctx, int32_t layer, int32_t T, const float *x, float
     if (T > 0 && (!x || !out)) return fail(ctx, MOE_ERR_INVALID_ARGS, "null x or out");
     if (T > 0 && ptr_kind == MOE_PTR_DEVICE && (((uintptr_t)x | (uintptr_t)out) & 15))
         return fail(ctx, MOE_ERR_INVALID_ARGS, "device x and out must be 16-byte aligned");
+    if (ep.p2p_broken)
+        return fail(ctx, MOE_ERR_TIMEOUT,
+                    "the peer exchange failed in an earlier forward; call moe_ep_reset on every rank first");
     const NcclApi *nc = nccl_api();
     if (!nc) return fail(ctx, MOE_ERR_NCCL, "NCCL unavailable");
     CUDA_TRY(ctx, cudaSetDevice(ctx->spec.device), "cudaSetDevice");

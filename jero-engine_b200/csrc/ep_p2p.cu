@@ -1,7 +1,8 @@
 // ep_p2p.cu -- kernels of the expert-parallel exchange over peer memory.
 // Peer arenas are written with plain stores from this GPU; nothing reads a
-// peer's memory. Every wait on a peer's flag is bounded (about 2 s at 2 GHz)
-// and records kErrEpTimeout in the status word instead of waiting on.
+// peer's memory. Every wait on a peer's flag is bounded (about 2 s at 2 GHz
+// unless a test shortens it) and records kErrEpTimeout (or kErrEpDesync for a
+// flag already past this forward) in the status word instead of waiting on.
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -12,8 +13,6 @@
 
 namespace jmoe {
 namespace {
-
-constexpr long long kEpWaitCycles = 4000000000LL;
 
 __device__ __forceinline__ uint32_t *ep_flag(uint8_t *arena, size_t o_flags, int phase, int src)
 {
@@ -32,15 +31,18 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t *p)
     return v;
 }
 
-// Waits until flag >= epoch (wrap-safe); false after kEpWaitCycles.
-__device__ __forceinline__ bool wait_epoch(const uint32_t *flag, uint32_t epoch)
+// Waits until flag == epoch. Returns 0, or kErrEpDesync at once when the flag
+// is already past it (wrap-safe), or kErrEpTimeout after `cycles`.
+__device__ __forceinline__ int wait_epoch(const uint32_t *flag, uint32_t epoch, long long cycles)
 {
     const long long t0 = clock64();
-    while ((int32_t)(ld_acquire_sys(flag) - epoch) < 0) {
-        if (clock64() - t0 > kEpWaitCycles) return false;
+    for (;;) {
+        const int32_t d = (int32_t)(ld_acquire_sys(flag) - epoch);
+        if (d == 0) return 0;
+        if (d > 0) return kErrEpDesync;
+        if (clock64() - t0 > cycles) return kErrEpTimeout;
         __nanosleep(256);
     }
-    return true;
 }
 
 // Raises this rank's flag of `phase` in every rank's arena once every CTA of
@@ -81,11 +83,15 @@ __global__ void __launch_bounds__(256) ep_p2p_plan_kernel(EpP2PArgs a)
     if (tid == 0) s_ok = 1;
     __syncthreads();
     if (tid < G) st_release_sys(ep_flag(a.peers[tid], a.o_flags, 0, a.rank), a.epoch);
-    if (tid < G && !wait_epoch(ep_flag(a.own, a.o_flags, 0, tid), a.epoch)) {
-        s_ok = 0;
-        atomicExch(a.err, kErrEpTimeout);
+    if (tid < G) {
+        const int r = wait_epoch(ep_flag(a.own, a.o_flags, 0, tid), a.wait_epoch, a.wait_cycles);
+        if (r) {
+            s_ok = 0;
+            atomicExch(a.err, r);
+        }
     }
     __syncthreads();
+    if (tid == 0) *a.ok = s_ok;   // read by this forward's dispatch, return and waits
     if (!s_ok) {
         if (tid == 0) { *a.n_active = 0; *a.total = 0; }
         return;
@@ -155,6 +161,7 @@ __global__ void __launch_bounds__(256) ep_p2p_dispatch_kernel(EpP2PArgs a)
     const int warp = (int)((blockIdx.x * (size_t)blockDim.x + threadIdx.x) >> 5);
     const int nwarps = (int)((gridDim.x * (size_t)blockDim.x) >> 5);
     const int H = a.H, chunks = H >> 4, nd = H >> 5;
+    if (!*a.ok) return;   // no stores into any peer's arena, no flags (uniform over the grid)
     for (int i = threadIdx.x; i <= a.E; i += blockDim.x) s_off[i] = a.offsets[i];
     __syncthreads();
     for (int s = warp; s < a.n_slots; s += nwarps) {
@@ -189,6 +196,7 @@ __global__ void __launch_bounds__(256) ep_p2p_return_kernel(EpP2PArgs a)
     const int warp = (int)((blockIdx.x * (size_t)blockDim.x + threadIdx.x) >> 5);
     const int nwarps = (int)((gridDim.x * (size_t)blockDim.x) >> 5);
     const int H = a.H, chunks = H >> 2;
+    if (!*a.ok) return;   // no stores into any peer's arena, no flags (uniform over the grid)
     const int total = *a.total;
     for (int s = warp; s < total; s += nwarps) {
         const int2 rr = a.ret[s];
@@ -205,7 +213,11 @@ __global__ void ep_p2p_wait_kernel(EpP2PArgs a, int phase)
     pdl_wait();
     pdl_trigger();
     const int lane = threadIdx.x;
-    if (lane < a.world && !wait_epoch(ep_flag(a.own, a.o_flags, phase, lane), a.epoch)) atomicExch(a.err, kErrEpTimeout);
+    if (!*a.ok) return;   // the forward has already failed: nobody raises these flags
+    if (lane < a.world) {
+        const int r = wait_epoch(ep_flag(a.own, a.o_flags, phase, lane), a.wait_epoch, a.wait_cycles);
+        if (r) atomicExch(a.err, r);
+    }
 }
 
 int rows_grid(long long rows, int num_sms)

@@ -10,7 +10,13 @@
 //   2 outputs: expert outputs of received rows -> the source's output inbox.
 // Reuse across forwards is ordered by the phases themselves: a rank writes a
 // peer's row inbox for forward n only after seeing that peer's counts of
-// forward n, which the peer raises after its forward n-1 has finished.
+// forward n, which the peer raises after its forward n-1 has finished. So a
+// flag never runs ahead of the forward that waits for it: a rank waits for
+// exactly its own epoch, and a later epoch is reported as a desync. When the
+// counts wait fails (a peer missing or out of step), the rank stores nothing
+// into any peer's arena and raises no further flag in that forward; its peers'
+// waits then run out as well, and every rank must reset the exchange
+// (moe_ep_reset) before the next forward.
 #pragma once
 
 #include <cuda_runtime.h>
@@ -24,6 +30,7 @@ namespace jmoe {
 constexpr int kEpMaxRanks = 8;
 constexpr int kEpP2PMaxTokens = 256;   // per rank; larger batches use the NCCL exchange
 constexpr int kErrEpTimeout = 2;       // device status: a peer's flag did not arrive in time
+constexpr int kErrEpDesync = 3;        // device status: a peer's flag was already past this forward
 
 struct EpP2PLayout {
     int world = 0, E = 0, El = 0, H = 0, W = 0, cap = 0, slots_y = 0;
@@ -35,7 +42,7 @@ struct EpP2PLayout {
     size_t o_yin = 0;       // [slots_y][H] f32 outputs of my own slots (routed, then shared)
     // regions only this rank touches
     size_t o_peers = 0;     // [kEpMaxRanks] arena bases of the ranks (device copy)
-    size_t o_misc = 0;      // tickets [2], n_active, total (16 B each)
+    size_t o_misc = 0;      // tickets [2], n_active, total, a zero word, ok (16 B each)
     size_t o_prob = 0;      // [El] Problem
     size_t o_perm = 0;      // [world*cap] received row of each local slot
     size_t o_ret = 0;       // [world*cap] int2 (source rank, source slot) of each local slot
@@ -61,7 +68,7 @@ inline EpP2PLayout ep_p2p_layout(int world, int E, int H, int W, int cap, int sl
     l.o_xin = take(R * l.rb);
     l.o_yin = take((size_t)slots_y * H * 4);
     l.o_peers = take(kEpMaxRanks * sizeof(void *));
-    l.o_misc = take(64);
+    l.o_misc = take(128);
     l.o_prob = take((size_t)l.El * sizeof(Problem));
     l.o_perm = take(R * 4);
     l.o_ret = take(R * 8);
@@ -79,8 +86,11 @@ struct EpP2PArgs {
     uint8_t *own;
     int rank, world, E, El, e0, H, cap;
     size_t rb, o_flags, o_off, o_xin, o_yin;
-    uint32_t epoch;
+    uint32_t epoch;             // this forward's epoch, raised in this rank's flags
+    uint32_t wait_epoch;        // the epoch the waits expect (epoch, unless a test skews it)
+    long long wait_cycles;      // bound of each flag wait (clock cycles)
     int *err;                   // the context's device status word
+    int *ok;                    // own arena: 1 once every source's counts of this forward were seen
     int *ticket;                // [2] in the own arena (dispatch, return)
     int32_t *n_active, *total;  // local problems of the received rows
     Problem *problems;

@@ -15,6 +15,7 @@
 //   - The first call on a device resolves the array's device address
 //     (cudaGetSymbolAddress); make that first call before capturing a stream
 //     into a CUDA graph.
+//   - The calling thread's current device is the same after the call.
 #include <cuda_runtime.h>
 
 #include <mutex>
@@ -86,8 +87,15 @@ extern "C" int moe_route_noalloc(int32_t device, const float *x, const float *ro
     const size_t o_slot_of = off;  off += align256((size_t)T * top_k * 4);
     if (off > kNoAllocScratchBytes) return fail(MOE_ERR_CONTEXT_LENGTH, "routing scratch for this shape exceeds 2 MiB");
 
-    cudaError_t e = cudaSetDevice(device);
+    // the caller's current device is restored before returning
+    int prev = -1;
+    cudaError_t e = cudaGetDevice(&prev);
     if (e != cudaSuccess) return fail(MOE_ERR_CUDA, cudaGetErrorString(e));
+    if ((e = cudaSetDevice(device)) != cudaSuccess) return fail(MOE_ERR_CUDA, cudaGetErrorString(e));
+    struct Restore {
+        int dev;
+        ~Restore() { cudaSetDevice(dev); }
+    } restore{prev};
     unsigned char *base;
     {
         std::lock_guard<std::mutex> lock(g_mu);

@@ -115,6 +115,8 @@ EXPORTS = {
                                    C.c_int32, C.POINTER(C.c_double), C.POINTER(C.c_double)]),
     "moe_ep_unique_id": (C.c_int, [C.c_void_p]),
     "moe_ep_init": (C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.c_void_p]),
+    "moe_ep_reset": (C.c_int, [C.c_void_p]),
+    "moe_debug_ep_fault": (C.c_int, [C.c_void_p, C.c_uint32, C.c_int64]),
     "moe_forward_ep": (C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
                                  C.c_int32]),
     "moe_ep_plan": (C.c_int, [C.c_int32, C.c_int32, C.c_int32, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
@@ -340,6 +342,15 @@ class Context:
     def forward_ep_ptrs(self, layer: int, T: int, x_ptr: int, out_ptr: int, ptr_kind: int = PTR_DEVICE):
         _check(lib.moe_forward_ep(self.h, layer, T, C.c_void_p(x_ptr or None), C.c_void_p(out_ptr or None), None,
                                   None, ptr_kind), self.h)
+
+    def ep_reset(self):
+        """Collective recovery of the peer exchange after a peer-rank timeout."""
+        _check(lib.moe_ep_reset(self.h), self.h)
+
+    def debug_ep_fault(self, epoch_skew: int, wait_cycles: int = 0):
+        """Test hook: the next expert-parallel forward waits for a flag nothing
+        raises (epoch_skew), and flag waits are bounded by wait_cycles."""
+        _check(lib.moe_debug_ep_fault(self.h, epoch_skew, wait_cycles), self.h)
 
     def device_status(self) -> int:
         st = C.c_int32()

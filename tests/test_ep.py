@@ -128,3 +128,38 @@ def test_gpu_ep_two_ranks(flags, exact):
     over = dict(E=16, k=4, I=384, S=512, H=512)
     T = 300 if flags & jm.FLAG_TENSOR_CORES_ALWAYS else 40
     mp.spawn(gpu_worker, args=(2, free_port(), 3, over, T, flags, exact), nprocs=2, join=True)
+
+
+@pytest.mark.gpu
+def test_gpu_ep_peer_wait_times_out_and_recovers():
+    """Failure detection without a device fault: a world of one on the
+    peer-memory exchange is made to wait for a flag epoch that nothing raises,
+    with the flag waits bounded to about a millisecond. The forward returns
+    MOE_ERR_TIMEOUT naming the peer-rank wait, within a short host-side limit;
+    later forwards refuse until moe_ep_reset; after it the context is usable
+    and matches moe_forward again."""
+    import time
+    cfg, d, keep, x = _ep_layer(2, dict(E=16, I=256, H=512), STREAM, 40)
+    uid = jm.ep_unique_id()
+    with jm.Context(0, 40, 1, flags=STREAM) as ep, jm.Context(0, 40, 1, flags=STREAM) as ref:
+        ep.ep_init(0, 1, uid)
+        ep.upload(0, d)
+        ref.upload(0, d)
+        r_out, r_si, _ = ref.forward(0, x)
+        out0, _, _ = ep.forward_ep(0, x)
+        np.testing.assert_array_equal(out0, r_out)
+        ep.debug_ep_fault(5, 2_000_000)   # ~1 ms per wait at 2 GHz
+        t0 = time.time()
+        with pytest.raises(jm.DeviceTimeout) as ei:
+            ep.forward_ep(0, x)
+        assert time.time() - t0 < 5.0
+        assert "peer-rank" in ei.value.msg
+        with pytest.raises(jm.DeviceTimeout) as ei2:
+            ep.forward_ep(0, x)   # refused until the world resets
+        assert "moe_ep_reset" in ei2.value.msg
+        ep.ep_reset()
+        ep.debug_ep_fault(0, 0)
+        out, si, _ = ep.forward_ep(0, x)
+        assert ep.device_status() == 0
+    np.testing.assert_array_equal(si, r_si)
+    np.testing.assert_array_equal(out, r_out)

@@ -53,7 +53,9 @@ def test_route_noalloc_matches_forward_twice(cid):
     ctx = jm.Context(0, 300, 1)
     d, keep = synth.desc_for(cfg, w)
     ctx.upload(0, d)
-    for T in (37, 300):   # two calls in a row, different token counts
+    # calls in a row with different token counts: the small-batch kernel after
+    # the tiled one relies on the routing tickets being back at zero
+    for T in (37, 300, 37):
         x = synth.gen_x(cfg.scaled(seed=cfg.seed + T), T)
         _, ref_si, ref_sw = ctx.forward(0, x)
         ref_offs, ref_perm = ctx.debug_permutation(cfg.E, cfg.k)
@@ -65,6 +67,33 @@ def test_route_noalloc_matches_forward_twice(cid):
         np.testing.assert_array_equal(offs, ref_offs)
         np.testing.assert_array_equal(perm, ref_perm)
     ctx.close()
+
+
+def test_route_noalloc_hidden_not_a_multiple_of_four():
+    """H = 510 takes the scalar router and the ticketed selection kernel (no
+    memset): routing and permutation equal the CPU oracle's, twice in a row,
+    and the caller's current device is left as it was."""
+    import torch
+    import oracle as orc
+    H, E, k = 510, 32, 4
+    rng = np.random.default_rng(3)
+    router_h = (rng.standard_normal((E, H)) * 0.02).astype(np.float32)
+    wts = jm.ModelWeights({"blk.0.ffn_gate_inp.weight": jm.f32_tensor(router_h, [H, E])})
+    L = orc.Layer(wts, 0, E, k, False, hidden=H)
+    router = torch.from_numpy(router_h).cuda()
+    for T in (19, 19):
+        x = rng.standard_normal((T, H)).astype(np.float32)
+        dev_before = torch.cuda.current_device()
+        rc, si, sw, offs, perm = _route_noalloc(torch.from_numpy(x).cuda(), router, T, H, E, k, jm.RouteSpec())
+        assert rc == jm.MOE_OK, jm.lib.moe_last_error_message(None)
+        assert torch.cuda.current_device() == dev_before
+        ref_si = np.stack([L.select(orc.router_logits(router_h, x[t]))[0] for t in range(T)])
+        ref_sw = np.stack([L.select(orc.router_logits(router_h, x[t]))[1] for t in range(T)])
+        np.testing.assert_array_equal(si, ref_si)
+        np.testing.assert_allclose(sw, ref_sw, rtol=W_RTOL, atol=1e-7)
+        ro, rp = orc.permutation(ref_si, E)
+        np.testing.assert_array_equal(offs, ro)
+        np.testing.assert_array_equal(perm, rp)
 
 
 def test_route_noalloc_rejects_oversized_calls():
