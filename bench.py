@@ -196,7 +196,8 @@ def kernel_bytes(cfg, weights, sel_idx, T, expert_range=None, routed_rows=None):
     if expert_range is not None:   # activation rows out and expert outputs back through the exchange
         layer += routed * cfg.H * 1.25 + routed * cfg.H * 4
     # the fused small-batch launch streams both projections
-    return {"gate_up": gate_up, "down": down, "experts_tc": gate_up + down, "layer": layer, "U": U,
+    return {"gate_up": gate_up, "down": down, "experts_tc": gate_up + down, "experts_i8": gate_up + down,
+            "layer": layer, "U": U,
             "routed_rows": routed}
 
 
@@ -207,8 +208,9 @@ def roofline_of(cfg, T, prof, kb, workload, rows_here=None, ep=False, tensor_pea
     this run's own f16 and int8 probe peaks beside it)."""
     tc = "gate_up_tc" in prof
     i8 = "gate_up_i8" in prof
+    fused = [k for k in ("experts_i8", "experts_tc") if k in prof]
     cands = ("gate_up_tc", "down_tc") if tc else (("gate_up_i8", "down_i8") if i8 else
-                                                  (("experts_tc",) if "experts_tc" in prof else ("gate_up", "down")))
+                                                  (tuple(fused) if fused else ("gate_up", "down")))
     dom = max(cands, key=lambda k: prof.get(k, (0, 1))[0])
     dom_ms = prof[dom][0] / prof[dom][1]
     traffic = None if ep else measured_traffic(workload, dom)   # captures are single-GPU workloads
@@ -225,7 +227,7 @@ def roofline_of(cfg, T, prof, kb, workload, rows_here=None, ep=False, tensor_pea
             r["frac_of_probe_int8"] = round(ach / tensor_peaks["int8_tops"], 4)
         return r
     hbm, peak_kind = peaks()
-    b = kb[dom.replace("_i8", "")]
+    b = kb[dom if dom.startswith("experts") else dom.replace("_i8", "")]
     ach = b / (dom_ms / 1e3) / 1e9
     return {"bound": "hbm", "kernel": dom, "achieved": round(ach, 1), "peak": hbm, "unit": "GB/s",
             "frac": round(ach / hbm, 4), "traffic": traffic, "peak_source": peak_kind,

@@ -131,6 +131,13 @@ typedef struct moe_device_spec {
  * that off (the int8 paths above then apply); the two MOE_FLAG_INT8_* flags
  * also select the int8 paths. */
 #define MOE_FLAG_FUSED_TC_NEVER 32
+/* The fused launch has two forms: integer operands (tcgen05 kind::i8 on the
+ * GGUF quants and the int8 activation blocks, exact int32 block sums scaled
+ * per block in f32) when the routed slots per expert average at most
+ * MOE_FUSED_I8_MAX_SLOTS_PER_EXPERT, f16 operands above. These flags force one. */
+#define MOE_FLAG_FUSED_I8_NEVER 64
+#define MOE_FLAG_FUSED_I8_ALWAYS 128
+#define MOE_FUSED_I8_MAX_SLOTS_PER_EXPERT 8
 
 /* Memory the admission check compares against. The real inspector reads
  * cudaMemGetInfo on spec->device; tests pass a fixed one, as the reference's

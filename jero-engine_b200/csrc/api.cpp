@@ -491,6 +491,16 @@ bool use_fused_tc(const moe_device_spec &spec, int T)
     return T < MOE_TENSOR_CORE_MIN_TOKENS;
 }
 
+// Between the two fused launches: integer operands while the routed slots
+// per expert stay few (the int8 epilogue's work grows with the slots of an
+// item, the f16 expansion's does not), f16 operands above.
+bool use_fused_i8(const moe_device_spec &spec, const LayerStore &L, int T)
+{
+    if (spec.flags & MOE_FLAG_FUSED_I8_NEVER) return false;
+    if (spec.flags & MOE_FLAG_FUSED_I8_ALWAYS) return true;
+    return (int64_t)T * L.k <= (int64_t)MOE_FUSED_I8_MAX_SLOTS_PER_EXPERT * L.E;
+}
+
 bool use_tensor_cores(const moe_device_spec &spec, const LayerStore &L, const Scratch &s, int T)
 {
     if (!s.tc || (spec.flags & MOE_FLAG_TENSOR_CORES_NEVER)) return false;
@@ -543,8 +553,10 @@ FwdParams local_params(moe_ctx *ctx, const LayerStore &L, int T, int ptr_kind, c
     p.dep_cap = s.dep_cap;
     p.x16 = T < MOE_TENSOR_CORE_MIN_TOKENS ? s.x16 : nullptr;
     p.use_tc = use_tensor_cores(ctx->spec, L, s, T);
-    p.use_xtc = !p.use_tc && use_fused_tc(ctx->spec, T) && fused_experts_ok(p, L.dev);
-    if (!p.use_xtc) p.x16 = nullptr;   // the routing writes the f16 rows only for the fused launch
+    const bool fused = !p.use_tc && use_fused_tc(ctx->spec, T);
+    p.use_xi8 = fused && use_fused_i8(ctx->spec, L, T) && fused_i8_ok(p, L.dev);
+    p.use_xtc = fused && !p.use_xi8 && fused_experts_ok(p, L.dev);
+    if (!p.use_xtc) p.x16 = nullptr;   // the routing writes the f16 rows only for the f16 fused launch
     p.use_dtc = !p.use_tc && !p.use_xtc && use_int8_tc(ctx->spec, L, T, T * L.k) && decode_tc_ok(p, L.dev);
     return p;
 }

@@ -28,6 +28,13 @@ int launch_forward(const FwdParams &p, const LayerDev &L, const LayerMaps &maps,
         mk.mark("combine");
         return cudaSuccess;
     }
+    if (p.use_xi8) {
+        if ((err = launch_fused_i8(p, L, maps, p.S > 0 ? 2 : 0, num_sms, st)) != cudaSuccess) return err;
+        mk.mark("experts_i8");
+        if ((err = launch_combine(p, st)) != cudaSuccess) return err;
+        mk.mark("combine");
+        return cudaSuccess;
+    }
     if (p.use_xtc) {
         if ((err = launch_fused_experts(p, L, maps, p.S > 0 ? 2 : 0, num_sms, st)) != cudaSuccess) return err;
         mk.mark("experts_tc");

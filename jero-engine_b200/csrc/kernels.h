@@ -79,6 +79,13 @@ bool fused_experts_ok(const FwdParams &p, const LayerDev &L);
 cudaError_t launch_fused_experts(const FwdParams &p, const LayerDev &L, const LayerMaps &maps, int mode, int num_sms,
                                  cudaStream_t st);
 
+// The same fused launch with integer operands (experts_i8.cu): exact int32
+// block sums from tcgen05 kind::i8 scaled per block by the epilogue; items of
+// up to 16 slots. fused_i8_ok: the layer's formats, shapes and buffers suit it.
+bool fused_i8_ok(const FwdParams &p, const LayerDev &L);
+cudaError_t launch_fused_i8(const FwdParams &p, const LayerDev &L, const LayerMaps &maps, int mode, int num_sms,
+                            cudaStream_t st);
+
 // Expert-parallel exchange (ep.cu): bytes of one packed token row, and the
 // pack / unpack / receive-plan kernels.
 size_t ep_row_bytes(int H);

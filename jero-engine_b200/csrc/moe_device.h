@@ -78,6 +78,7 @@ struct FwdParams {
     int use_tc;                  // experts on the f16 tensor-core path (prefill.cu)
     int use_dtc;                 // experts on the int8 tensor-core path (decode_tc.cu)
     int use_xtc;                 // experts in one fused f16 tensor-core launch (experts_tc.cu)
+    int use_xi8;                 // experts in one fused int8 tensor-core launch (experts_i8.cu)
 
     const float *x;              // [T][H]
     const float *router;         // [E][H]
@@ -144,8 +145,8 @@ struct FwdParams {
 };
 
 // Entries of FwdParams::dep a forward over T tokens may use: one per slot
-// chunk of up to 32 slots of every problem.
-inline int dep_entries(int T, int k, int E) { return (T * k + T) / 32 + (E < T * k ? E : T * k) + 2; }
+// chunk (of at least 8 slots, the smallest item cap) of every problem.
+inline int dep_entries(int T, int k, int E) { return (T * k + T) / 8 + (E < T * k ? E : T * k) + 2; }
 
 struct LayerDev {
     DevMatrix gate, up, down;

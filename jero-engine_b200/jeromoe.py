@@ -37,7 +37,8 @@ FLAG_TENSOR_CORES_ALWAYS, FLAG_TENSOR_CORES_NEVER = 1, 2
 FLAG_EP_NCCL_ONLY = 4   # expert parallelism: NCCL exchange for every batch size
 # small batches: int8 weight-streaming kernels only / int8 tensor cores for every size below the f16 path
 FLAG_INT8_TENSOR_CORES_NEVER, FLAG_INT8_TENSOR_CORES_ALWAYS = 8, 16
-FLAG_FUSED_TC_NEVER = 32   # small batches: no fused f16 tensor-core expert launch
+FLAG_FUSED_TC_NEVER = 32   # small batches: no fused tensor-core expert launch
+FLAG_FUSED_I8_NEVER, FLAG_FUSED_I8_ALWAYS = 64, 128   # the fused launch's f16 / int8 form
 TENSOR_CORE_MIN_TOKENS = 256
 
 # ------------------------------------------------------------------- structs

@@ -224,7 +224,7 @@ def test_gpu_fused_tensor_core_path(name, T):
     w = synth.build_weights(cfg)
     x = synth.gen_x(cfg, T)
     ref = oracle_layer(w, cfg).forward(x, 8)
-    with gpu_layer(w, cfg.E, cfg.k, cfg.I, cfg.S > 0, cfg.route, cfg.H, T) as ctx:
+    with gpu_layer(w, cfg.E, cfg.k, cfg.I, cfg.S > 0, cfg.route, cfg.H, T, flags=jm.FLAG_FUSED_I8_NEVER) as ctx:
         ctx.set_profiling(True)
         first = ctx.forward(0, x)
         second = ctx.forward(0, x)
@@ -238,6 +238,30 @@ def test_gpu_fused_tensor_core_path(name, T):
         stream = ctx.forward(0, x)
     np.testing.assert_array_equal(first[1], stream[1])
     assert row_rel_err(first[0], stream[0]).max() <= OUT_TOL
+
+
+@pytest.mark.parametrize("name", list(TC_CASES))
+@pytest.mark.parametrize("T", [1, 5, 33, 100, 255])
+def test_gpu_fused_int8_path(name, T):
+    """The fused launch with integer operands (exact int32 block sums from
+    tcgen05 kind::i8, f32 block scaling in the epilogue), forced for every T:
+    same routing as the oracle and the streaming path, outputs within the
+    contract tolerance of the oracle, identical on a second call, and the
+    launch is the one that ran."""
+    cid, over = TC_CASES[name]
+    cfg = synth.CONFIGS[cid].scaled(**over)
+    w = synth.build_weights(cfg)
+    x = synth.gen_x(cfg, T)
+    ref = oracle_layer(w, cfg).forward(x, 8)
+    with gpu_layer(w, cfg.E, cfg.k, cfg.I, cfg.S > 0, cfg.route, cfg.H, T, flags=jm.FLAG_FUSED_I8_ALWAYS) as ctx:
+        ctx.set_profiling(True)
+        first = ctx.forward(0, x)
+        second = ctx.forward(0, x)
+        prof, _ = ctx.profile_read()
+        assert ctx.device_status() == 0
+    assert "experts_i8" in prof, sorted(prof)
+    assert_parity(*first, *ref)
+    np.testing.assert_array_equal(first[0], second[0])
 
 
 # ---------------------------------- int8 tensor-core path (small batches)
