@@ -145,8 +145,8 @@ struct FwdParams {
 };
 
 // Entries of FwdParams::dep a forward over T tokens may use: one per slot
-// chunk (of at least 8 slots, the smallest item cap) of every problem.
-inline int dep_entries(int T, int k, int E) { return (T * k + T) / 8 + (E < T * k ? E : T * k) + 2; }
+// chunk (of at least 4 slots, the smallest item cap) of every problem.
+inline int dep_entries(int T, int k, int E) { return (T * k + T) / 4 + (E < T * k ? E : T * k) + 2; }
 
 struct LayerDev {
     DevMatrix gate, up, down;

@@ -83,6 +83,12 @@ __device__ __forceinline__ void cp_async16_s(uint32_t saddr, const void *gmem)
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(saddr), "l"(gmem) : "memory");
 }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+// An arrival on the mbarrier once all of this thread's earlier cp.async copies
+// have landed; .noinc: the arrival counts against the barrier's expected count.
+__device__ __forceinline__ void cp_async_mbar_arrive_noinc(uint64_t *bar)
+{
+    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
 // Waits until at most N of this thread's committed groups are pending.
 template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
@@ -273,6 +279,13 @@ __device__ __forceinline__ void fence_proxy_async_global()
 }
 
 // Acquire load of a 32-bit flag at GPU scope (pairs with a fence + atomic on the writer side).
+// Adds v to *p with release semantics at GPU scope: every write this thread
+// has made or observed before it (a warp barrier counts) is visible first.
+__device__ __forceinline__ void red_release_add(int *p, int v)
+{
+    asm volatile("red.release.gpu.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
 __device__ __forceinline__ int ld_acquire_gpu(const int *p)
 {
     int v;
