@@ -256,9 +256,10 @@ const char *moe_last_error_message(const moe_ctx *ctx);
  * each slot, experts ascending, tokens ascending inside an expert). */
 int moe_debug_permutation(moe_ctx *ctx, int32_t *offsets, int32_t *perm_token, int32_t *T_out);
 
-/* Parity probe of the int8 tensor-core expert path: while device_buf is set
+/* Parity probe of the int8 tensor-core expert paths (the per-projection
+ * launches and the fused small-batch launch): while device_buf is set
  * (n_ints int32 on the context's device; NULL, 0 turns it off), forwards that
- * run that path store the raw int32 sum of every 32-value block of the routed
+ * run such a path store the raw int32 sum of every 32-value block of the routed
  * gate/up products before any scaling, at
  * [slot][0 gate / 1 up][row of I][block of H/32] (slots as in
  * moe_debug_permutation). Forwards whose sums do not fit store nothing. */

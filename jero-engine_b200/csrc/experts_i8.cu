@@ -175,7 +175,7 @@ struct YEpi {
 // slot scales from the item's scale buffer sc: [slot][kb] dx, then [slot][kb] sx.
 __device__ __forceinline__ bool epi_steps(const FwdParams &p, const YEpi &e, bool q4, int K, uint32_t tb0, int r,
                                           RingPos &qr, RingPos &cr, RingPos &br, RingPos &ar, float (&a0)[kYCap],
-                                          float (&a1)[kYCap])
+                                          float (&a1)[kYCap], int32_t *dbg, int n)
 {
     const int nk = (K + kYKS - 1) / kYKS;
 #pragma unroll
@@ -221,6 +221,15 @@ __device__ __forceinline__ bool epi_steps(const FwdParams &p, const YEpi &e, boo
                     for (int b = 0; b < 4; b++) mn[b] = 0.0f;
                 }
                 tmem_ld_wait();
+                if (dbg) {   // parity probe: the raw int32 block sums, [slot][matrix][row][block]
+#pragma unroll
+                    for (int j = 0; j < kYCap; j++)
+#pragma unroll
+                        for (int b = 0; b < 4; b++)
+                            if (j < n)
+                                dbg[((size_t)j * 2 + m) * p.I * (size_t)(K >> 5) + 8 * kk + 4 * h + b] =
+                                    (int32_t)S[4 * b + j];
+                }
 #pragma unroll
                 for (int j = 0; j < kYCap; j++) {
                     const float dxv[4] = {__uint_as_float(dx[j].x), __uint_as_float(dx[j].y),
@@ -640,7 +649,10 @@ __global__ void __launch_bounds__(kYThreads, 1)
             ei.sc = smem_addr(ssc + (size_t)sr.slot * sc_stride);
             ei.kb = M.cols >> 5;
             float a0[kYCap], a1[kYCap];
-            const bool ok = epi_steps(p, ei, q4, M.cols, tb0, r, qr, cr, br, ar, a0, a1);
+            int32_t *dbg = p.dbg_isum && x.phase == 0 && !x.shared
+                               ? p.dbg_isum + ((size_t)x.slot * 2 * p.I + (size_t)x.tile * kYM + r) * (size_t)(M.cols >> 5)
+                               : nullptr;
+            const bool ok = epi_steps(p, ei, q4, M.cols, tb0, r, qr, cr, br, ar, a0, a1, dbg, x.n);
             __syncwarp();
             if (lane == 0) mbar_arrive(&sc_empty[sr.slot]);
             sr.advance(2);

@@ -266,13 +266,21 @@ def test_gpu_fused_int8_path(name, T):
 
 # ---------------------------------- int8 tensor-core path (small batches)
 
+INT8_PATHS = {"streaming_tc": ("gate_up_i8", jm.FLAG_INT8_TENSOR_CORES_ALWAYS),
+              "fused": ("experts_i8", jm.FLAG_FUSED_I8_ALWAYS)}
+
+
+@pytest.mark.parametrize("path", list(INT8_PATHS))
 @pytest.mark.parametrize("name", ["cfg2_q4k", "cfg1_q8_0"])
 @pytest.mark.parametrize("T", [5, 33])
-def test_gpu_int8_tensor_core_block_sums_bit_exact(name, T):
+def test_gpu_int8_tensor_core_block_sums_bit_exact(name, T, path):
     """The tcgen05 kind::i8 MMAs produce the int32 sum of every 32-value block
-    of every routed gate/up product; captured before any scaling, each equals
-    the oracle's integer block dot (orc_block_dots) of the GGUF row and the
-    token's int8 activation block, bit for bit."""
+    of every routed gate/up product -- per block accumulator (the per-launch
+    path) or four blocks of four slots in one accumulator off block-diagonal
+    activation tiles (the fused launch); captured before any scaling, each
+    equals the oracle's integer block dot (orc_block_dots) of the GGUF row and
+    the token's int8 activation block, bit for bit."""
+    stage, flags = INT8_PATHS[path]
     import torch
     cid, over = TC_CASES[name]
     cfg = synth.CONFIGS[cid].scaled(**over)
@@ -281,15 +289,14 @@ def test_gpu_int8_tensor_core_block_sums_bit_exact(name, T):
     nb = cfg.H // 32
     slots = T * cfg.k
     buf = torch.zeros(slots * 2 * cfg.I * nb, dtype=torch.int32, device="cuda")
-    with gpu_layer(w, cfg.E, cfg.k, cfg.I, False, cfg.route, cfg.H, T,
-                   flags=jm.FLAG_INT8_TENSOR_CORES_ALWAYS) as ctx:
+    with gpu_layer(w, cfg.E, cfg.k, cfg.I, False, cfg.route, cfg.H, T, flags=flags) as ctx:
         ctx.debug_capture_block_sums(buf.data_ptr(), buf.numel())
         ctx.set_profiling(True)
         ctx.forward(0, x)
         prof, _ = ctx.profile_read()
         offs, perm = ctx.debug_permutation(cfg.E, cfg.k)
         ctx.debug_capture_block_sums(0, 0)
-    assert "gate_up_i8" in prof, sorted(prof)
+    assert stage in prof, sorted(prof)
     got = buf.cpu().numpy().reshape(slots, 2, cfg.I, nb)
     xq = [orc.quantize_act(x[t])[0] for t in range(T)]
     for m, name_m in enumerate(("gate", "up")):
