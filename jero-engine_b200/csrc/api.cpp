@@ -397,7 +397,10 @@ size_t carve_scratch(const ScratchDims &d, uint8_t *base, Scratch *s)
     const size_t Tx = std::min<size_t>(Tm, MOE_TENSOR_CORE_MIN_TOKENS - 1), slots_x = Tx * k + Tx;
     t.a16dn = take((d.tc ? slots : slots_x) * W * 2);
     t.x16 = take(Tx * H * 2);
-    t.dep_cap = dep_entries((int)Tm, (int)k, (int)E);
+    // chunk counters: this context's forwards, and the fused launch over the
+    // rows an expert-parallel forward receives (up to kEpMaxRanks sources, f16
+    // items of at least 16 slots)
+    t.dep_cap = std::max(dep_entries((int)Tm, (int)k, (int)E), (int)((kEpMaxRanks * Tm * k) / 16 + E + 2));
     t.dep = (int32_t *)take(((size_t)t.dep_cap + 1) * 4);
     if (s && base) {
         void *blk = s->block;
@@ -1448,13 +1451,8 @@ static int ep_forward_p2p(moe_ctx *ctx, LayerStore &L, FwdParams p, int T, int p
     a.n_slots = T * L.k;
     a.y = reinterpret_cast<const float *>(A + l.o_y);
 
-    if ((ce = launch_ep_p2p_plan(a, st)) != cudaSuccess) return cuda_fail(ctx, ce, "ep plan");
-    mk.mark("ep_plan");
-    if ((ce = launch_ep_p2p_dispatch(a, ctx->num_sms, st)) != cudaSuccess) return cuda_fail(ctx, ce, "ep dispatch");
-    if ((ce = launch_ep_p2p_wait(a, 1, st)) != cudaSuccess) return cuda_fail(ctx, ce, "ep wait");
-    mk.mark("ep_dispatch");
-
-    // the local experts over the received rows, read in place from the row inbox
+    // the local experts over the received rows, read in place: packed int8
+    // rows, or (the fused launch) the f16 rows the sources wrote
     FwdParams pe{};
     pe.T = G * l.cap; pe.H = H; pe.E = El; pe.k = 1; pe.I = L.I; pe.S = 0;
     pe.quant_x = 1;
@@ -1472,8 +1470,41 @@ static int ep_forward_p2p(moe_ctx *ctx, LayerStore &L, FwdParams p, int T, int p
     pe.y = reinterpret_cast<float *>(A + l.o_y); pe.y_rows = nullptr;
     pe.err = s.err;
     pe.use_tc = 0;
-    pe.use_dtc = use_int8_tc(ctx->spec, L, T, T * L.k) && decode_tc_ok(pe, L.dev);
-    if (pe.use_dtc) {
+    // the fused f16 launch over the received rows: one pass over the local
+    // experts' weights for up to 32 rows per expert (the per-source rows of
+    // every rank together), gate/up + SwiGLU + down in one launch
+    FwdParams pf = pe;
+    pf.x_qstride = 0;   // its operands are the f16 rows below, not the packed int8 rows
+    pf.x16 = A + l.o_x16;
+    pf.a16dn = A + l.o_a16dn;
+    pf.a16dn_stride = l.W;
+    pf.dep = s.dep; pf.dep_done = s.dep ? s.dep + s.dep_cap : nullptr; pf.dep_cap = s.dep_cap;
+    // its down epilogue stores each output row straight into the source rank's
+    // output inbox and its last CTA raises the outputs flag: no return pass
+    pf.y_peer = a.peers;
+    pf.y_ret = a.ret;
+    pf.y_peer_off = l.o_yin;
+    pf.y_flag_off = l.o_flags + ((size_t)kEpPhaseOut * kEpMaxRanks + me) * 4;
+    pf.y_epoch = a.epoch;
+    pf.y_world = G;
+    pf.y_ok = a.ok;
+    // (the same flags as the single-GPU policy pin the streaming or int8 paths)
+    const bool fused = use_fused_tc(ctx->spec, T) && (long long)G * l.cap / 16 + El + 2 <= s.dep_cap &&
+                       fused_experts_ok(pf, L.dev);
+    pe.use_dtc = !fused && use_int8_tc(ctx->spec, L, T, T * L.k) && decode_tc_ok(pe, L.dev);
+    a.o_x16 = fused ? l.o_x16 : 0;   // the fused launch takes the rows as f16 straight from the dispatch
+
+    // rows (with the slot offsets) out first; the plan waits for every source's
+    if ((ce = launch_ep_p2p_dispatch(a, ctx->num_sms, st)) != cudaSuccess) return cuda_fail(ctx, ce, "ep dispatch");
+    mk.mark("ep_dispatch");
+    if ((ce = launch_ep_p2p_plan(a, st)) != cudaSuccess) return cuda_fail(ctx, ce, "ep plan");
+    mk.mark("ep_plan");
+
+    if (fused) {
+        if ((ce = launch_fused_experts(pf, L.dev, L.maps, 0, ctx->num_sms, st)) != cudaSuccess)
+            return cuda_fail(ctx, ce, "experts (fused f16 tensor cores)");
+        mk.mark("experts_tc");
+    } else if (pe.use_dtc) {
         if ((ce = launch_decode_tc(pe, L.dev, L.maps, ctx->num_sms, mk, st)) != cudaSuccess)
             return cuda_fail(ctx, ce, "experts (int8 tensor cores)");
     } else {
@@ -1483,8 +1514,10 @@ static int ep_forward_p2p(moe_ctx *ctx, LayerStore &L, FwdParams p, int T, int p
         if ((ce = launch_down(pe, L.dev, L.maps, 0, ctx->num_sms, st)) != cudaSuccess) return cuda_fail(ctx, ce, "down");
         mk.mark("down");
     }
-    if ((ce = launch_ep_p2p_return(a, ctx->num_sms, st)) != cudaSuccess) return cuda_fail(ctx, ce, "ep return");
-    mk.mark("ep_return");
+    if (!fused) {
+        if ((ce = launch_ep_p2p_return(a, ctx->num_sms, st)) != cudaSuccess) return cuda_fail(ctx, ce, "ep return");
+        mk.mark("ep_return");
+    }
 
     p.y = reinterpret_cast<float *>(A + l.o_yin);   // routed outputs arrive here; shared rows follow
     if (T > 0 && L.S > 0) {
@@ -1505,7 +1538,7 @@ static int ep_forward_p2p(moe_ctx *ctx, LayerStore &L, FwdParams p, int T, int p
         }
         mk.mark("shared");
     }
-    if ((ce = launch_ep_p2p_wait(a, 2, st)) != cudaSuccess) return cuda_fail(ctx, ce, "ep wait");
+    if ((ce = launch_ep_p2p_wait(a, kEpPhaseOut, st)) != cudaSuccess) return cuda_fail(ctx, ce, "ep wait");
     mk.mark("ep_wait");
     if (T > 0) {
         if ((ce = launch_combine(p, st)) != cudaSuccess) return cuda_fail(ctx, ce, "combine");

@@ -146,6 +146,19 @@ __device__ __forceinline__ int q8_isum(uint4 q0, uint4 q1, int4 a, int4 b)
 
 // SiLU(g) * u with silu(g) = g / (1 + exp(-g)), each operation rounded (the oracle's form).
 // Row of y that holds the expert output of slot s.
+__device__ __forceinline__ size_t y_row(const FwdParams &p, size_t s);
+
+// Output row of slot s: this rank's y, or (expert parallel, fused launch) the
+// source rank's output inbox over peer memory.
+__device__ __forceinline__ float *y_dst(const FwdParams &p, size_t s)
+{
+    if (p.y_peer) {
+        const int2 rr = p.y_ret[s];
+        return reinterpret_cast<float *>(p.y_peer[rr.x] + p.y_peer_off) + (size_t)rr.y * p.H;
+    }
+    return p.y + y_row(p, s) * p.H;
+}
+
 __device__ __forceinline__ size_t y_row(const FwdParams &p, size_t s)
 {
     return p.y_rows ? (size_t)p.y_rows[s] : s;

@@ -3,6 +3,7 @@
 // peer's memory. Every wait on a peer's flag is bounded (about 2 s at 2 GHz
 // unless a test shortens it) and records kErrEpTimeout (or kErrEpDesync for a
 // flag already past this forward) in the status word instead of waiting on.
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -62,10 +63,11 @@ __device__ __forceinline__ void signal_when_done(const EpP2PArgs &a, int *ticket
     }
 }
 
-// One CTA: publish my slot offsets to every rank, wait for every rank's, then
-// the plan of the rows I receive: my experts in order, each with its rows in
-// (source rank, source slot) order -- the global canonical order restricted
-// to my experts. perm[slot] = received row, ret[slot] = (source, source slot).
+// One CTA, after the dispatch: wait for every source's rows (and with them
+// its slot offsets), then the plan of the rows I receive: my experts in order,
+// each with its rows in (source rank, source slot) order -- the global
+// canonical order restricted to my experts. perm[slot] = received row,
+// ret[slot] = (source, source slot).
 __global__ void __launch_bounds__(256) ep_p2p_plan_kernel(EpP2PArgs a)
 {
     __shared__ int s_off[kEpMaxRanks * (kMaxRouteExperts + 1)];
@@ -75,23 +77,17 @@ __global__ void __launch_bounds__(256) ep_p2p_plan_kernel(EpP2PArgs a)
     pdl_trigger();
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
     const int E = a.E, G = a.world, El = a.El;
-    for (int g = 0; g < G; g++) {
-        int32_t *dst = reinterpret_cast<int32_t *>(a.peers[g] + a.o_off) + (size_t)a.rank * (E + 1);
-        for (int i = tid; i <= E; i += blockDim.x) dst[i] = a.offsets[i];
-    }
-    __threadfence_system();
     if (tid == 0) s_ok = 1;
     __syncthreads();
-    if (tid < G) st_release_sys(ep_flag(a.peers[tid], a.o_flags, 0, a.rank), a.epoch);
     if (tid < G) {
-        const int r = wait_epoch(ep_flag(a.own, a.o_flags, 0, tid), a.wait_epoch, a.wait_cycles);
+        const int r = wait_epoch(ep_flag(a.own, a.o_flags, kEpPhaseRows, tid), a.wait_epoch, a.wait_cycles);
         if (r) {
             s_ok = 0;
             atomicExch(a.err, r);
         }
     }
     __syncthreads();
-    if (tid == 0) *a.ok = s_ok;   // read by this forward's dispatch, return and waits
+    if (tid == 0) *a.ok = s_ok;   // read by this forward's expert launch, return and waits
     if (!s_ok) {
         if (tid == 0) { *a.n_active = 0; *a.total = 0; }
         return;
@@ -149,9 +145,11 @@ __global__ void __launch_bounds__(256) ep_p2p_plan_kernel(EpP2PArgs a)
     }
 }
 
-// My routed rows, packed [H int8 | H/32 d | H/32 s], into the row inbox of the
-// rank that owns each row's expert, at (my rank, position among my rows for
-// that rank). One warp per row.
+// The first step of a forward's exchange: my slot offsets into every rank's
+// offset inbox, and my routed rows, packed [H int8 | H/32 d | H/32 s], into
+// the row inbox of the rank that owns each row's expert, at (my rank,
+// position among my rows for that rank). One warp per row; the rows flag
+// follows once every CTA's stores are fenced.
 __global__ void __launch_bounds__(256) ep_p2p_dispatch_kernel(EpP2PArgs a)
 {
     __shared__ int s_off[kMaxRouteExperts + 1];
@@ -161,7 +159,11 @@ __global__ void __launch_bounds__(256) ep_p2p_dispatch_kernel(EpP2PArgs a)
     const int warp = (int)((blockIdx.x * (size_t)blockDim.x + threadIdx.x) >> 5);
     const int nwarps = (int)((gridDim.x * (size_t)blockDim.x) >> 5);
     const int H = a.H, chunks = H >> 4, nd = H >> 5;
-    if (!*a.ok) return;   // no stores into any peer's arena, no flags (uniform over the grid)
+    if (blockIdx.x == 0)
+        for (int g = 0; g < a.world; g++) {
+            int32_t *dst = reinterpret_cast<int32_t *>(a.peers[g] + a.o_off) + (size_t)a.rank * (a.E + 1);
+            for (int i = threadIdx.x; i <= a.E; i += blockDim.x) dst[i] = a.offsets[i];
+        }
     for (int i = threadIdx.x; i <= a.E; i += blockDim.x) s_off[i] = a.offsets[i];
     __syncthreads();
     for (int s = warp; s < a.n_slots; s += nwarps) {
@@ -174,6 +176,24 @@ __global__ void __launch_bounds__(256) ep_p2p_dispatch_kernel(EpP2PArgs a)
         const int dest = lo / a.El;
         const int r = s - s_off[dest * a.El];
         const size_t tok = (size_t)a.perm_token[s];
+        if (a.o_x16) {
+            // f16(q * d), groups of four as (0, 2, 1, 3): the token row operand of
+            // the receiver's fused f16 expert launch (quantize_tile's arithmetic)
+            uint2 *row16 = reinterpret_cast<uint2 *>(a.peers[dest] + a.o_x16 +
+                                                     ((size_t)a.rank * a.cap + r) * (size_t)H * 2);
+            const uint32_t *q4 = reinterpret_cast<const uint32_t *>(a.xq + tok * H);
+            const float *dv = a.xd + tok * nd;
+#pragma unroll 4
+            for (int g = lane; g < (H >> 2); g += 32) {
+                const uint32_t q = q4[g];
+                const float d = dv[g >> 3];
+                const float q0 = (float)(int8_t)(q & 0xFF), q1 = (float)(int8_t)((q >> 8) & 0xFF);
+                const float q2 = (float)(int8_t)((q >> 16) & 0xFF), q3 = (float)(int8_t)(q >> 24);
+                const __half2 lo = __floats2half2_rn(q0 * d, q2 * d), hi = __floats2half2_rn(q1 * d, q3 * d);
+                row16[g] = make_uint2(*reinterpret_cast<const uint32_t *>(&lo), *reinterpret_cast<const uint32_t *>(&hi));
+            }
+            continue;
+        }
         uint8_t *row = a.peers[dest] + a.o_xin + ((size_t)a.rank * a.cap + r) * a.rb;
         const int4 *q = reinterpret_cast<const int4 *>(a.xq + tok * H);
         for (int c = lane; c < chunks; c += 32) reinterpret_cast<int4 *>(row)[c] = q[c];
@@ -183,7 +203,7 @@ __global__ void __launch_bounds__(256) ep_p2p_dispatch_kernel(EpP2PArgs a)
             rd[nd + c] = a.xs[tok * nd + c];
         }
     }
-    signal_when_done(a, a.ticket, 1);
+    signal_when_done(a, a.ticket, kEpPhaseRows);
 }
 
 // Expert outputs of the rows I received, by local slot, into each source's
@@ -204,7 +224,7 @@ __global__ void __launch_bounds__(256) ep_p2p_return_kernel(EpP2PArgs a)
         const float4 *src = reinterpret_cast<const float4 *>(a.y + (size_t)s * H);
         for (int c = lane; c < chunks; c += 32) dst[c] = src[c];
     }
-    signal_when_done(a, a.ticket + 1, 2);
+    signal_when_done(a, a.ticket + 1, kEpPhaseOut);
 }
 
 // Waits for every rank's flag of `phase` in this rank's arena.

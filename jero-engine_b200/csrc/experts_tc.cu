@@ -489,7 +489,7 @@ __global__ void __launch_bounds__(kXThreads, 1)
 #pragma unroll
                     for (int j = 0; j < 16; j++) {
                         if (j < n_here) {
-                            float *yr = p.y + y_row(p, s0 + j) * p.H;
+                            float *yr = y_dst(p, s0 + j);
                             yr[f0] = __fadd_rn(__uint_as_float(a0[j]), __uint_as_float(a1[j]));
                             yr[f0 + kXM] = __fadd_rn(__uint_as_float(b0[j]), __uint_as_float(b1[j]));
                         }
@@ -514,9 +514,12 @@ __global__ void __launch_bounds__(kXThreads, 1)
         tc_fence_after();
         tmem_dealloc(tmem, 512);
     }
-    // the last CTA returns the chunk counters and the ticket to zero
+    // the last CTA returns the chunk counters and the ticket to zero (and,
+    // returning rows over peer memory, raises the output flags once every
+    // CTA's stores are fenced at system scope)
     if (threadIdx.x == 0) {
-        __threadfence();
+        if (p.y_peer) __threadfence_system();
+        else __threadfence();
         *s_last = atomicAdd(p.dep_done, 1) == (int)gridDim.x - 1;
     }
     __syncthreads();
@@ -525,6 +528,11 @@ __global__ void __launch_bounds__(kXThreads, 1)
         const int n = min(nq > 0 ? s_cb[nq] : 0, p.dep_cap);
         for (int i = threadIdx.x; i < n; i += blockDim.x) p.dep[i] = 0;
         if (threadIdx.x == 0) *p.dep_done = 0;
+        if (p.y_peer && threadIdx.x < p.y_world && *p.y_ok) {
+            __threadfence_system();
+            uint32_t *flag = reinterpret_cast<uint32_t *>(p.y_peer[threadIdx.x] + p.y_flag_off);
+            asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(flag), "r"(p.y_epoch) : "memory");
+        }
     }
 }
 

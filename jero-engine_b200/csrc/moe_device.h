@@ -15,6 +15,7 @@
 #include <cuda.h>
 #include <stddef.h>
 #include <stdint.h>
+#include <vector_types.h>
 
 namespace jmoe {
 
@@ -137,6 +138,20 @@ struct FwdParams {
     int32_t *dep;
     int32_t *dep_done;
     int dep_cap;
+
+    // expert-parallel return through peer memory (the fused f16 expert
+    // launch): when y_peer is set, the down epilogue stores the output row of
+    // local slot s straight into its source rank's output inbox, at
+    // y_peer[y_ret[s].x] + y_peer_off, row y_ret[s].y; the launch's last CTA
+    // then raises this rank's output flag (value y_epoch, at y_flag_off in
+    // every rank's arena) once every CTA's stores are fenced at system scope,
+    // unless *y_ok is 0 (the forward's exchange has failed).
+    uint8_t *const *y_peer;
+    const int2 *y_ret;
+    size_t y_peer_off, y_flag_off;
+    uint32_t y_epoch;
+    int y_world;
+    const int *y_ok;
 
     // parity probe (null in production): the int8 tensor-core gate/up launch
     // stores each routed slot's raw int32 block sums here,

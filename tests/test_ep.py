@@ -69,6 +69,10 @@ EP1_CASES = {
     "cfg2_stream_nccl": (2, dict(E=16, I=256, H=512), STREAM | jm.FLAG_EP_NCCL_ONLY, 40, True),
     "cfg3_shared_stream": (3, dict(E=16, k=4, I=384, S=512, H=512), STREAM, 33, True),
     "cfg2_int8": (2, dict(E=16, I=256, H=512), INT8, 40, True),
+    # default flags: the local experts of the peer-memory exchange run the fused
+    # f16 launch over the received rows, the single-GPU forward the fused int8
+    # one -- two arithmetics, compared within the contract tolerance
+    "cfg2_fused": (2, dict(E=16, I=256, H=512), 0, 40, False),
     "cfg3_shared_int8_nccl": (3, dict(E=16, k=4, I=384, S=512, H=512), INT8 | jm.FLAG_EP_NCCL_ONLY, 33, True),
     "cfg5_groups_shared_int8": (5, dict(E=32, k=6, I=256, S=512, H=512, n_groups=8, topk_groups=3), INT8, 64, True),
     "cfg2_tensor_cores": (2, dict(E=16, I=256, H=512), jm.FLAG_TENSOR_CORES_ALWAYS, 300, False),
@@ -121,6 +125,7 @@ def test_gpu_ep_requires_init_and_split():
 @pytest.mark.parametrize("flags,exact", [(STREAM, True),
                                          (STREAM | jm.FLAG_EP_NCCL_ONLY, True),
                                          (INT8, True),
+                                         (0, False),
                                          (jm.FLAG_TENSOR_CORES_ALWAYS, False)])
 def test_gpu_ep_two_ranks(flags, exact):
     if torch.cuda.device_count() < 2:
