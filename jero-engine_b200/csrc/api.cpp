@@ -560,7 +560,7 @@ FwdParams local_params(moe_ctx *ctx, const LayerStore &L, int T, int ptr_kind, c
     p.use_xi8 = fused && use_fused_i8(ctx->spec, L, T) && fused_i8_ok(p, L.dev);
     p.use_xtc = fused && !p.use_xi8 && fused_experts_ok(p, L.dev);
     if (!p.use_xtc) p.x16 = nullptr;   // the routing writes the f16 rows only for the f16 fused launch
-    p.use_dtc = !p.use_tc && !p.use_xtc && use_int8_tc(ctx->spec, L, T, T * L.k) && decode_tc_ok(p, L.dev);
+    p.use_dtc = !p.use_tc && !p.use_xtc && !p.use_xi8 && use_int8_tc(ctx->spec, L, T, T * L.k) && decode_tc_ok(p, L.dev);
     return p;
 }
 
