@@ -221,6 +221,18 @@ int moe_layer_set_ffn_norm(moe_ctx *ctx, int32_t layer, const float *weight, flo
 int moe_forward_block(moe_ctx *ctx, int32_t layer, int32_t T, const float *hidden, float *out,
                       int32_t *sel_idx, float *sel_w, int32_t ptr_kind);
 
+/* Layer-major prefill of a stack of MoE FFN sublayers: layers first_layer ..
+ * first_layer + n_layers - 1 (uploaded, with their FFN norm set, one hidden
+ * width) each take all T tokens at once, in layer order, in place on hidden
+ * [T x H] (moe_forward_block per layer). For such a stack this equals the
+ * reference's token-major prefill loop, run_prefill_with_hidden
+ * (src/qwen_deepseek.rs:2217-2316), since each sublayer treats its tokens
+ * independently (the attention sublayers between them stay on the host path).
+ * MOE_PTR_HOST: one copy each way for the whole stack, synchronous;
+ * MOE_PTR_DEVICE: asynchronous on the context's stream. */
+int moe_prefill_ffn_layers(moe_ctx *ctx, int32_t first_layer, int32_t n_layers, int32_t T, float *hidden,
+                           int32_t ptr_kind);
+
 int moe_residency_summary(const moe_ctx *ctx, moe_residency *out);
 
 /* Reads and clears the device status word of ctx (synchronises the context

@@ -172,6 +172,8 @@ struct moe_ctx {
     uint64_t dbg_isum_cap = 0;
     int num_sms = 148;
     int *status_host = nullptr;   // pinned word for the device status flag
+    float *stack_buf = nullptr;   // moe_prefill_ffn_layers: the hidden rows on the device
+    size_t stack_buf_n = 0;
     Profiler prof;
     EpState ep;
 };
@@ -828,6 +830,7 @@ int moe_ctx_destroy(moe_ctx *ctx)
     if (ctx->scratch.block) cudaFree(ctx->scratch.block);
     ctx->prof.release();
     if (ctx->status_host) cudaFreeHost(ctx->status_host);
+    if (ctx->stack_buf) cudaFree(ctx->stack_buf);
     EpState &ep = ctx->ep;
     if (ep.comm) {
         if (const NcclApi *nc = nccl_api()) nc->CommDestroy(ep.comm);
@@ -1126,6 +1129,61 @@ int moe_forward_block(moe_ctx *ctx, int32_t layer, int32_t T, const float *hidde
                       float *sel_w, int32_t ptr_kind)
 {
     return forward_impl(ctx, layer, T, hidden, out, sel_idx, sel_w, ptr_kind, true);
+}
+
+// Layer-major prefill of a stack of MoE FFN sublayers: every layer takes all T
+// tokens at once (moe_forward_block in place on the device), in layer order.
+// For a stack of FFN sublayers this equals the reference's token-major prefill
+// (run_prefill_with_hidden, src/qwen_deepseek.rs:2217-2316: every layer per
+// token), because each sublayer treats its tokens independently; with host
+// pointers the rows cross PCIe once each way for the whole stack.
+int moe_prefill_ffn_layers(moe_ctx *ctx, int32_t first_layer, int32_t n_layers, int32_t T, float *hidden,
+                           int32_t ptr_kind)
+{
+    if (!ctx || (!hidden && T > 0)) return fail(ctx, MOE_ERR_INVALID_ARGS, "null argument");
+    if (n_layers < 0 || first_layer < 0 || first_layer + n_layers > (int)ctx->layers.size())
+        return fail(ctx, MOE_ERR_INVALID_ARGS, "layers %d..%d outside 0..%d", first_layer, first_layer + n_layers - 1,
+                    (int)ctx->layers.size() - 1);
+    if (ptr_kind != MOE_PTR_HOST && ptr_kind != MOE_PTR_DEVICE)
+        return fail(ctx, MOE_ERR_INVALID_ARGS, "ptr_kind must be MOE_PTR_HOST or MOE_PTR_DEVICE");
+    if (T < 0 || T > ctx->spec.max_tokens)
+        return fail(ctx, MOE_ERR_CONTEXT_LENGTH, "T = %d outside 0..max_tokens %d", T, ctx->spec.max_tokens);
+    if (T == 0 || n_layers == 0) return MOE_OK;
+    const int H = ctx->layers[first_layer].H;
+    for (int l = first_layer; l < first_layer + n_layers; l++) {
+        const LayerStore &L = ctx->layers[l];
+        if (!L.present) return fail(ctx, MOE_ERR_NOT_UPLOADED, "layer %d was never uploaded", l);
+        if (L.H != H) return fail(ctx, MOE_ERR_INVALID_ARGS, "layer %d has hidden %d, layer %d %d", l, L.H,
+                                  first_layer, H);
+    }
+    CUDA_TRY(ctx, cudaSetDevice(ctx->spec.device), "cudaSetDevice");
+    cudaStream_t st = ctx->stream;
+    const size_t n = (size_t)T * H;
+    float *rows = hidden;
+    if (ptr_kind == MOE_PTR_HOST) {
+        if (ctx->stack_buf_n < n) {
+            CUDA_TRY(ctx, cudaStreamSynchronize(st), "cudaStreamSynchronize");
+            if (ctx->stack_buf) cudaFree(ctx->stack_buf);
+            ctx->stack_buf = nullptr;
+            ctx->stack_buf_n = 0;
+            CUDA_TRY(ctx, cudaMalloc(&ctx->stack_buf, n * 4), "cudaMalloc(prefill rows)");
+            ctx->stack_buf_n = n;
+        }
+        rows = ctx->stack_buf;
+        CUDA_TRY(ctx, cudaMemcpyAsync(rows, hidden, n * 4, cudaMemcpyHostToDevice, st), "copy hidden");
+    }
+    for (int l = first_layer; l < first_layer + n_layers; l++) {
+        const int rc = forward_impl(ctx, l, T, rows, rows, nullptr, nullptr, MOE_PTR_DEVICE, true);
+        if (rc != MOE_OK) return rc;
+    }
+    if (ptr_kind == MOE_PTR_HOST) {
+        CUDA_TRY(ctx, cudaMemcpyAsync(hidden, rows, n * 4, cudaMemcpyDeviceToHost, st), "copy hidden");
+        int32_t status = 0;
+        const int rc = moe_device_status(ctx, &status);   // synchronises the stream
+        if (rc != MOE_OK) return rc;
+        if (status) return fail(ctx, MOE_ERR_TIMEOUT, "a bounded device wait ran out (status %d)", status);
+    }
+    return MOE_OK;
 }
 
 int moe_layer_set_ffn_norm(moe_ctx *ctx, int32_t layer, const float *weight, float eps)

@@ -99,6 +99,7 @@ EXPORTS = {
     "moe_layer_set_ffn_norm": (C.c_int, [C.c_void_p, C.c_int32, C.c_void_p, C.c_float]),
     "moe_forward_block": (C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.c_void_p, C.c_void_p, C.c_void_p,
                                     C.c_void_p, C.c_int32]),
+    "moe_prefill_ffn_layers": (C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.c_int32, C.c_void_p, C.c_int32]),
     "moe_residency_summary": (C.c_int, [C.c_void_p, C.POINTER(moe_residency)]),
     "moe_device_status": (C.c_int, [C.c_void_p, C.POINTER(C.c_int32)]),
     "moe_ctx_set_profiling": (C.c_int, [C.c_void_p, C.c_int32]),
@@ -319,6 +320,14 @@ class Context:
         _check(lib.moe_forward_block(self.h, layer, T, C.c_void_p(hidden_ptr), C.c_void_p(out_ptr),
                                      C.c_void_p(sel_idx_ptr or None), C.c_void_p(sel_w_ptr or None), ptr_kind),
                self.h)
+
+    def prefill_ffn_layers(self, first_layer: int, n_layers: int, hidden: np.ndarray) -> np.ndarray:
+        """Layer-major prefill of FFN sublayers first_layer .. + n_layers - 1 over all
+        rows of hidden [T, H] at once (moe_prefill_ffn_layers); returns the new rows."""
+        rows = np.array(hidden, dtype=np.float32, order="C", copy=True)
+        T = rows.shape[0]
+        _check(lib.moe_prefill_ffn_layers(self.h, first_layer, n_layers, T, _ptr(rows), PTR_HOST), self.h)
+        return rows
 
     # ---- expert parallelism (moe_ep_init / moe_forward_ep)
 

@@ -402,6 +402,43 @@ def test_gpu_forward_block_is_norm_block_residual(cid, over, T):
     assert_parity(out_b[rows], si_b[rows], sw_b[rows], hidden[rows] + r_out, r_si, r_sw)
 
 
+@pytest.mark.parametrize("cid,over,T", [(2, dict(E=32, I=256, H=512), 40),
+                                        (3, dict(E=16, k=4, I=384, S=512, H=512), 300)])
+def test_gpu_layer_major_prefill_of_a_stack(cid, over, T):
+    """moe_prefill_ffn_layers over three FFN sublayers (different weights and
+    norms): bit for bit the layer-by-layer moe_forward_block calls, and within
+    the contract tolerance of the oracle run token-major as the reference's
+    prefill loop does it (each token through every layer in turn)."""
+    n_layers = 3
+    cfgs = [synth.CONFIGS[cid].scaled(**over, seed=synth.CONFIGS[cid].seed + 10 * l) for l in range(n_layers)]
+    rng = np.random.default_rng(11)
+    hidden = (synth.gen_x(cfgs[0], T) * 3.0).astype(np.float32)
+    norms = [rng.uniform(0.5, 1.5, cfgs[0].H).astype(np.float32) for _ in range(n_layers)]
+    eps = 1e-6
+    ws = [synth.build_weights(cfgs[l], layer=l) for l in range(n_layers)]
+    with jm.Context(0, T, n_layers) as ctx:
+        keep = []
+        for l, c in enumerate(cfgs):
+            d, k = jm.layer_desc(ws[l], l, c.E, c.k, c.I, c.S > 0, c.route, c.H)
+            keep.append(k)
+            ctx.upload(l, d)
+            ctx.set_ffn_norm(l, norms[l], eps)
+        got = ctx.prefill_ffn_layers(0, n_layers, hidden)
+        ref = hidden
+        for l in range(n_layers):
+            ref, _, _ = ctx.forward_block(l, ref)
+        assert ctx.device_status() == 0
+    np.testing.assert_array_equal(got, ref)
+    layers = [orc.Layer(ws[l], l, c.E, c.k, c.S > 0, c.route, hidden=c.H) for l, c in enumerate(cfgs)]
+    rows = np.arange(0, T, max(1, T // 8))
+    for t in rows:   # token-major, as run_prefill_with_hidden
+        h = hidden[t:t + 1].copy()
+        for l in range(n_layers):
+            o, _, _ = layers[l].forward(orc.rmsnorm(h, norms[l], eps), 1)
+            h = h + o
+        assert row_rel_err(got[t:t + 1], h).max() <= OUT_TOL, f"token {t}"
+
+
 def test_gpu_forward_block_needs_norm():
     cfg = synth.CONFIGS[2].scaled(E=32, I=256, H=512)
     w = synth.build_weights(cfg)
