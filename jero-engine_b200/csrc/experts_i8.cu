@@ -173,6 +173,7 @@ struct YEpi {
 // row r and the item's slots (a0 / a1; slots >= n hold nothing of use). The
 // weight scales come from the quant stage (waited for, then released), the
 // slot scales from the item's scale buffer sc: [slot][kb] dx, then [slot][kb] sx.
+template <bool DBG>
 __device__ __forceinline__ bool epi_steps(const FwdParams &p, const YEpi &e, bool q4, int K, uint32_t tb0, int r,
                                           RingPos &qr, RingPos &cr, RingPos &br, RingPos &ar, float (&a0)[kYCap],
                                           float (&a1)[kYCap], int32_t *dbg, int n)
@@ -221,7 +222,7 @@ __device__ __forceinline__ bool epi_steps(const FwdParams &p, const YEpi &e, boo
                     for (int b = 0; b < 4; b++) mn[b] = 0.0f;
                 }
                 tmem_ld_wait();
-                if (dbg) {   // parity probe: the raw int32 block sums, [slot][matrix][row][block]
+                if (DBG) {   // parity probe: the raw int32 block sums, [slot][matrix][row][block]
 #pragma unroll
                     for (int j = 0; j < kYCap; j++)
 #pragma unroll
@@ -652,7 +653,9 @@ __global__ void __launch_bounds__(kYThreads, 1)
             int32_t *dbg = p.dbg_isum && x.phase == 0 && !x.shared
                                ? p.dbg_isum + ((size_t)x.slot * 2 * p.I + (size_t)x.tile * kYM + r) * (size_t)(M.cols >> 5)
                                : nullptr;
-            const bool ok = epi_steps(p, ei, q4, M.cols, tb0, r, qr, cr, br, ar, a0, a1, dbg, x.n);
+            // the parity probe's stores in their own instance, off the production loop
+            const bool ok = dbg ? epi_steps<true>(p, ei, q4, M.cols, tb0, r, qr, cr, br, ar, a0, a1, dbg, x.n)
+                                : epi_steps<false>(p, ei, q4, M.cols, tb0, r, qr, cr, br, ar, a0, a1, nullptr, x.n);
             __syncwarp();
             if (lane == 0) mbar_arrive(&sc_empty[sr.slot]);
             sr.advance(2);
