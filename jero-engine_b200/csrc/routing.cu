@@ -228,7 +228,7 @@ __device__ __forceinline__ void select_token(const FwdParams &p, int t, int lane
                               (uint64_t)(0xFFFFFFFFu - (uint32_t)(lane + 32 * i))
                         : 0ull;
     int my_e = -1;
-    float my_w = 0.0f;
+    float my_w = 0.0f, my_p = 0.0f;
     int nsel = 0;
     for (int r = 0; r < k; r++) {
         uint64_t loc = pk[0];
@@ -248,10 +248,14 @@ __device__ __forceinline__ void select_token(const FwdParams &p, int t, int lane
         const float bp = __shfl_sync(0xffffffffu, hp, e & 31);
         if (lane == r) {
             my_e = e;
-            if (p.sel_bias) my_w = sum_ok ? __fdiv_rn(bp, psum) : 0.0f;
-            else my_w = sum_ok ? __fdiv_rn(bp, psum) : __fdiv_rn(1.0f, (float)E);
+            my_p = bp;
         }
         nsel = r + 1;
+    }
+    // the chosen probabilities, all ranks at once (lane r holds rank r)
+    if (lane < nsel) {
+        if (p.sel_bias) my_w = sum_ok ? __fdiv_rn(my_p, psum) : 0.0f;
+        else my_w = sum_ok ? __fdiv_rn(my_p, psum) : __fdiv_rn(1.0f, (float)E);
     }
     if (p.sel_bias || p.normalize) {
         // sum of the chosen weights in rank order, as the reference adds them
@@ -635,6 +639,12 @@ __global__ void __launch_bounds__(128) router_small_kernel(FwdParams p)
     __threadfence();   // the tile's logits from every CTA are visible
     if (t0 + warp < p.T) select_token<NL>(p, t0 + warp, lane);
     __syncthreads();
+    if (gridDim.y == 1) {   // one token tile: this CTA saw every selection, no second ticket
+        if (threadIdx.x == 0) p.sync[1] = 0;
+        __threadfence();
+        build_permutation_small(p);
+        return;
+    }
     if (threadIdx.x == 0) {
         p.sync[1 + blockIdx.y] = 0;
         __threadfence();
