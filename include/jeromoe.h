@@ -233,6 +233,25 @@ int moe_forward_block(moe_ctx *ctx, int32_t layer, int32_t T, const float *hidde
 int moe_prefill_ffn_layers(moe_ctx *ctx, int32_t first_layer, int32_t n_layers, int32_t T, float *hidden,
                            int32_t ptr_kind);
 
+/* The LM head, project_lm_head (src/qwen_deepseek.rs:584-632), on the device.
+ * Upload: the head is output_weight when present, else token_embd (the tied
+ * embedding alias the reference resolves by tensor presence); GGUF [hidden,
+ * vocab] F32 / Q8_0 / Q4_K (other types: MOE_ERR_CAPABILITY_MISMATCH). Both
+ * absent (NULL or data NULL) is allowed: calls then give the reference's
+ * synthetic logits. A tensor of another shape is kept as elements / hidden
+ * rows and used only when a call's n_logits equals them (the reference's
+ * second branch); otherwise the synthetic logits. A new upload replaces the
+ * head. */
+int moe_lm_head_upload(moe_ctx *ctx, const moe_tensor *output_weight, const moe_tensor *token_embd, int32_t hidden);
+/* logits [T x n_logits] of T final-normed rows normed [T x hidden]: per row
+ * the head's first min(n_logits, rows) rows (the product with int8 activation
+ * blocks, as the expert matrices), then normed[i mod hidden] * 0.05 for the
+ * logits past them; without a usable head base + normed[i mod hidden] * 0.1 +
+ * (i mod 13) * 0.01 with base = tanh(sum(normed) / 16). T <= max_tokens.
+ * MOE_PTR_HOST: synchronous; MOE_PTR_DEVICE: asynchronous on the context's
+ * stream (status via moe_device_status once a layer is uploaded). */
+int moe_lm_head(moe_ctx *ctx, int32_t T, const float *normed, float *logits, int32_t n_logits, int32_t ptr_kind);
+
 int moe_residency_summary(const moe_ctx *ctx, moe_residency *out);
 
 /* Reads and clears the device status word of ctx (synchronises the context

@@ -174,6 +174,19 @@ struct moe_ctx {
     int *status_host = nullptr;   // pinned word for the device status flag
     float *stack_buf = nullptr;   // moe_prefill_ffn_layers: the hidden rows on the device
     size_t stack_buf_n = 0;
+    // the LM head (moe_lm_head_upload / moe_lm_head)
+    struct Head {
+        bool uploaded = false;   // moe_lm_head_upload was called
+        bool has = false;        // a head tensor exists (output.weight or the tied token_embd.weight)
+        bool shaped = false;     // GGUF [hidden, rows]; else rows = elements / hidden
+        int hidden = 0, rows = 0;
+        void *block = nullptr;   // the head in device layout
+        DevMatrix m{};
+        MatMaps maps{};
+        void *buf = nullptr;     // call buffers
+        size_t buf_bytes = 0;
+        int *errw = nullptr;     // the status word at the start of buf
+    } head;
     Profiler prof;
     EpState ep;
 };
@@ -831,6 +844,8 @@ int moe_ctx_destroy(moe_ctx *ctx)
     ctx->prof.release();
     if (ctx->status_host) cudaFreeHost(ctx->status_host);
     if (ctx->stack_buf) cudaFree(ctx->stack_buf);
+    if (ctx->head.block) cudaFree(ctx->head.block);
+    if (ctx->head.buf) cudaFree(ctx->head.buf);
     EpState &ep = ctx->ep;
     if (ep.comm) {
         if (const NcclApi *nc = nccl_api()) nc->CommDestroy(ep.comm);
@@ -1186,6 +1201,169 @@ int moe_prefill_ffn_layers(moe_ctx *ctx, int32_t first_layer, int32_t n_layers, 
     return MOE_OK;
 }
 
+// The LM head of project_lm_head (src/qwen_deepseek.rs:584-632): output.weight
+// when present, else the tied token_embd.weight; GGUF [hidden, rows] (rows =
+// vocabulary). A tensor of another shape is kept as elements / hidden rows,
+// used only by calls whose logit count equals them (the reference's second
+// branch); a head that fits neither leaves the synthetic logits.
+int moe_lm_head_upload(moe_ctx *ctx, const moe_tensor *output_weight, const moe_tensor *token_embd, int32_t hidden)
+{
+    if (!ctx) return fail(nullptr, MOE_ERR_INVALID_ARGS, "null context");
+    if (hidden <= 0) return fail(ctx, MOE_ERR_INVALID_ARGS, "hidden must be positive");
+    const moe_tensor *t = output_weight && output_weight->data ? output_weight
+                          : (token_embd && token_embd->data ? token_embd : nullptr);
+    if (t && t->quant != MOE_QUANT_F32 && t->quant != MOE_QUANT_Q8_0 && t->quant != MOE_QUANT_Q4_K)
+        return fail(ctx, MOE_ERR_CAPABILITY_MISMATCH, "unsupported LM head quantization %d", t->quant);
+    if (t && (t->n_dims < 1 || t->n_dims > 4)) return fail(ctx, MOE_ERR_TENSOR_BOUNDS, "LM head dims %d", t->n_dims);
+    CUDA_TRY(ctx, cudaSetDevice(ctx->spec.device), "cudaSetDevice");
+    CUDA_TRY(ctx, cudaStreamSynchronize(ctx->stream), "cudaStreamSynchronize");
+    moe_ctx::Head &hd = ctx->head;
+    if (hd.block) cudaFree(hd.block);
+    hd = moe_ctx::Head{hd.uploaded, false, false, hidden, 0, nullptr, DevMatrix{}, MatMaps{}, hd.buf, hd.buf_bytes, hd.errw};
+    hd.uploaded = true;
+    if (!t) return MOE_OK;
+    hd.has = true;
+    hd.shaped = t->n_dims == 2 && t->shape[0] == hidden && t->shape[1] > 0;
+    int64_t rows = 0;
+    if (hd.shaped) {
+        rows = t->shape[1];
+    } else {
+        int64_t n = 1;
+        for (int i = 0; i < t->n_dims; i++) n *= t->shape[i];
+        rows = n > 0 && n % hidden == 0 ? n / hidden : 0;
+    }
+    if (rows <= 0) return MOE_OK;   // a head that fits no branch: synthetic logits, as the reference
+    if (rows > (1 << 24)) return fail(ctx, MOE_ERR_TENSOR_BOUNDS, "LM head rows %lld out of range", (long long)rows);
+    const size_t rb = gguf_row_bytes(t->quant, hidden);
+    if (!rb)
+        return fail(ctx, MOE_ERR_CAPABILITY_MISMATCH, "LM head: %d columns are not whole %s blocks", hidden,
+                    quant_name(t->quant));
+    if (t->nbytes != rb * (size_t)rows)
+        return fail(ctx, MOE_ERR_TENSOR_BOUNDS, "LM head: %llu bytes, shape needs %llu",
+                    (unsigned long long)t->nbytes, (unsigned long long)(rb * (size_t)rows));
+    MatrixPlan plan = plan_matrix(t->quant, (int)rows, hidden, 1);
+    const size_t o_meta = align_up(plan.qs_bytes, 256);
+    const size_t bytes = o_meta + align_up(plan.meta_bytes, 256);
+    std::vector<uint8_t> host(bytes, 0);
+    repack_rows(plan, static_cast<const uint8_t *>(t->data), host.data(),
+                plan.meta_bytes ? host.data() + o_meta : nullptr);
+    void *blk = nullptr;
+    if (cudaMalloc(&blk, bytes) != cudaSuccess) {
+        cudaGetLastError();
+        hd.has = false;
+        return fail(ctx, MOE_ERR_INSUFFICIENT_MEMORY, "LM head needs %zu bytes of device memory", bytes);
+    }
+    cudaError_t e = cudaMemcpy(blk, host.data(), bytes, cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) {
+        cudaFree(blk);
+        hd.has = false;
+        return cuda_fail(ctx, e, "cudaMemcpy(LM head)");
+    }
+    uint8_t *base = static_cast<uint8_t *>(blk);
+    hd.block = blk;
+    hd.rows = (int)rows;
+    hd.m = to_dev(plan, base, plan.meta_bytes ? base + o_meta : nullptr);
+    plan_slices(hd.m);
+    const int r = make_matrix_maps(hd.m, &hd.maps, 32);
+    if (r != 0) return fail(ctx, MOE_ERR_CUDA, "cuTensorMapEncodeTiled failed (CUresult %d)", r);
+    return MOE_OK;
+}
+
+// logits [T x n_logits] of T normed rows [T x hidden], each row as
+// project_lm_head: the head's first min(n_logits, rows) rows as a quantised
+// matrix-vector product (int8 activation blocks, as the experts), the rest
+// normed[i mod hidden] * 0.05; without a usable head the synthetic logits.
+int moe_lm_head(moe_ctx *ctx, int32_t T, const float *normed, float *logits, int32_t n_logits, int32_t ptr_kind)
+{
+    if (!ctx) return fail(nullptr, MOE_ERR_INVALID_ARGS, "null context");
+    moe_ctx::Head &hd = ctx->head;
+    if (!hd.uploaded) return fail(ctx, MOE_ERR_NOT_UPLOADED, "no LM head was uploaded (moe_lm_head_upload)");
+    if (T < 0 || n_logits < 0) return fail(ctx, MOE_ERR_INVALID_ARGS, "negative token or logit count");
+    if (T > ctx->spec.max_tokens)
+        return fail(ctx, MOE_ERR_CONTEXT_LENGTH, "T = %d exceeds max_tokens %d", T, ctx->spec.max_tokens);
+    if (ptr_kind != MOE_PTR_HOST && ptr_kind != MOE_PTR_DEVICE)
+        return fail(ctx, MOE_ERR_INVALID_ARGS, "ptr_kind must be MOE_PTR_HOST or MOE_PTR_DEVICE");
+    if (T == 0 || n_logits == 0) return MOE_OK;
+    if (!normed || !logits) return fail(ctx, MOE_ERR_INVALID_ARGS, "null argument");
+    CUDA_TRY(ctx, cudaSetDevice(ctx->spec.device), "cudaSetDevice");
+    cudaStream_t st = ctx->stream;
+    const int H = hd.hidden;
+    const bool product = hd.has && hd.rows > 0 && (hd.shaped || hd.rows == n_logits);
+    const int target = product ? std::min(n_logits, hd.rows) : 0;
+    const bool direct = ptr_kind == MOE_PTR_DEVICE && target == n_logits;
+    // call buffers: the status word and the problem first (fixed offsets, so the
+    // word is zero from its allocation on), then normed rows, int8 blocks,
+    // product rows, logits
+    size_t off = 0;
+    auto take = [&](size_t b) { size_t o = off; off += align_up(b ? b : 1, 256); return o; };
+    const size_t o_e = take(16), o_p = take(sizeof(Problem) + 16), o_x = take((size_t)T * H * 4),
+                 o_q = take((size_t)T * H), o_d = take((size_t)T * (H / 32) * 4), o_s = take((size_t)T * (H / 32) * 4),
+                 o_y = take(direct ? 0 : (size_t)T * std::max(target, 1) * 4), o_l = take((size_t)T * n_logits * 4);
+    if (hd.buf_bytes < off) {
+        CUDA_TRY(ctx, cudaStreamSynchronize(st), "cudaStreamSynchronize");
+        if (hd.buf) cudaFree(hd.buf);
+        hd.buf = nullptr;
+        hd.buf_bytes = 0;
+        hd.errw = nullptr;
+        CUDA_TRY(ctx, cudaMalloc(&hd.buf, off), "cudaMalloc(LM head buffers)");
+        hd.buf_bytes = off;
+        CUDA_TRY(ctx, cudaMemset(hd.buf, 0, off), "cudaMemset(LM head buffers)");
+    }
+    uint8_t *b = static_cast<uint8_t *>(hd.buf);
+    // the device status word: the context's, or (no layer uploaded yet) one of the head's own
+    int *errw = ctx->scratch.err ? ctx->scratch.err : reinterpret_cast<int *>(b + o_e);
+    hd.errw = reinterpret_cast<int *>(b + o_e);
+    const float *x = normed;
+    if (ptr_kind == MOE_PTR_HOST) {
+        CUDA_TRY(ctx, cudaMemcpyAsync(b + o_x, normed, (size_t)T * H * 4, cudaMemcpyHostToDevice, st), "copy rows");
+        x = reinterpret_cast<const float *>(b + o_x);
+    }
+    float *lg = ptr_kind == MOE_PTR_DEVICE ? logits : reinterpret_cast<float *>(b + o_l);
+    cudaError_t e;
+    if (product) {
+        FwdParams pl{};
+        pl.T = T; pl.H = target; pl.E = 1; pl.k = 1; pl.I = H; pl.S = 0; pl.W = H;
+        pl.max_problems = 1;
+        pl.problems = reinterpret_cast<Problem *>(b + o_p);
+        pl.n_active = reinterpret_cast<int32_t *>(b + o_p + sizeof(Problem));
+        pl.err = errw;
+        pl.y = direct ? lg : reinterpret_cast<float *>(b + o_y);
+        LayerDev Lh{};
+        Lh.down = hd.m;
+        Lh.down.rows = target;   // the first rows of the head (rows are contiguous)
+        LayerMaps lm{};
+        lm.down = hd.maps;
+        if (hd.m.type == FMT_F32) {
+            pl.af = const_cast<float *>(x);
+        } else {
+            pl.aq = reinterpret_cast<int8_t *>(b + o_q);
+            pl.ad = reinterpret_cast<float *>(b + o_d);
+            pl.as = reinterpret_cast<float *>(b + o_s);
+            if ((e = (cudaError_t)launch_quantize_rows(x, T, H, pl.aq, pl.ad, pl.as, st)) != cudaSuccess)
+                return cuda_fail(ctx, e, "LM head activation blocks");
+        }
+        if ((e = launch_lm_head_prep(pl.problems, pl.n_active, T, st)) != cudaSuccess)
+            return cuda_fail(ctx, e, "LM head problem");
+        if ((e = launch_down(pl, Lh, lm, 0, ctx->num_sms, st)) != cudaSuccess) return cuda_fail(ctx, e, "LM head");
+        if (!direct && (e = launch_lm_head_scatter(pl.y, target, x, H, lg, n_logits, T, ctx->num_sms, st)) !=
+                           cudaSuccess)
+            return cuda_fail(ctx, e, "LM head rows");
+    } else if ((e = launch_lm_head_synth(x, H, lg, n_logits, T, st)) != cudaSuccess) {
+        return cuda_fail(ctx, e, "LM head (synthetic)");
+    }
+    if (ptr_kind == MOE_PTR_HOST) {
+        CUDA_TRY(ctx, cudaMemcpyAsync(logits, lg, (size_t)T * n_logits * 4, cudaMemcpyDeviceToHost, st), "copy logits");
+        CUDA_TRY(ctx, cudaMemcpyAsync(ctx->status_host, errw, sizeof(int), cudaMemcpyDeviceToHost, st), "copy status");
+        CUDA_TRY(ctx, cudaStreamSynchronize(st), "LM head");
+        if (*ctx->status_host) {
+            const int code = *ctx->status_host;
+            cudaMemsetAsync(errw, 0, sizeof(int), st);
+            return fail(ctx, MOE_ERR_TIMEOUT, "a bounded device wait ran out in the LM head (status %d)", code);
+        }
+    }
+    return MOE_OK;
+}
+
 int moe_layer_set_ffn_norm(moe_ctx *ctx, int32_t layer, const float *weight, float eps)
 {
     if (!ctx) return fail(nullptr, MOE_ERR_INVALID_ARGS, "null context");
@@ -1210,15 +1388,19 @@ int moe_device_status(moe_ctx *ctx, int32_t *status)
 {
     if (!ctx || !status) return fail(nullptr, MOE_ERR_INVALID_ARGS, "null argument");
     *status = 0;
-    if (!ctx->scratch.err) return MOE_OK;
+    // the context's word, or (LM head calls before any layer upload) the head's own
+    int *word = ctx->scratch.err ? ctx->scratch.err : ctx->head.errw;
     CUDA_TRY(ctx, cudaSetDevice(ctx->spec.device), "cudaSetDevice");
-    CUDA_TRY(ctx, cudaMemcpyAsync(ctx->status_host, ctx->scratch.err, sizeof(int), cudaMemcpyDeviceToHost,
-                                  ctx->stream),
+    if (!word) {
+        CUDA_TRY(ctx, cudaStreamSynchronize(ctx->stream), "status sync");
+        return MOE_OK;
+    }
+    CUDA_TRY(ctx, cudaMemcpyAsync(ctx->status_host, word, sizeof(int), cudaMemcpyDeviceToHost, ctx->stream),
              "copy status");
     CUDA_TRY(ctx, cudaStreamSynchronize(ctx->stream), "status sync");
     *status = *ctx->status_host;
     if (*status) {
-        CUDA_TRY(ctx, cudaMemsetAsync(ctx->scratch.err, 0, sizeof(int), ctx->stream), "clear status");
+        CUDA_TRY(ctx, cudaMemsetAsync(word, 0, sizeof(int), ctx->stream), "clear status");
         if (ctx->ep.world && (*status == kErrEpTimeout || *status == kErrEpDesync)) {
             ctx->ep.p2p_broken = true;
             return fail(ctx, MOE_ERR_TIMEOUT,

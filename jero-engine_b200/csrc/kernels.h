@@ -86,6 +86,13 @@ bool fused_i8_ok(const FwdParams &p, const LayerDev &L);
 cudaError_t launch_fused_i8(const FwdParams &p, const LayerDev &L, const LayerMaps &maps, int mode, int num_sms,
                             cudaStream_t st);
 
+// LM head (lm_head.cu): the problem entry of its product on the down-projection
+// kernels, the rows past the head's rows, the synthetic logits without a head.
+cudaError_t launch_lm_head_prep(Problem *prob, int32_t *n_active, int T, cudaStream_t st);
+cudaError_t launch_lm_head_scatter(const float *y, int target, const float *normed, int hidden, float *logits, int n,
+                                   int T, int num_sms, cudaStream_t st);
+cudaError_t launch_lm_head_synth(const float *normed, int hidden, float *logits, int n, int T, cudaStream_t st);
+
 // Expert-parallel exchange (ep.cu): bytes of one packed token row, and the
 // pack / unpack / receive-plan kernels.
 size_t ep_row_bytes(int H);

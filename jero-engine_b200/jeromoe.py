@@ -100,6 +100,8 @@ EXPORTS = {
     "moe_forward_block": (C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.c_void_p, C.c_void_p, C.c_void_p,
                                     C.c_void_p, C.c_int32]),
     "moe_prefill_ffn_layers": (C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.c_int32, C.c_void_p, C.c_int32]),
+    "moe_lm_head_upload": (C.c_int, [C.c_void_p, C.POINTER(moe_tensor), C.POINTER(moe_tensor), C.c_int32]),
+    "moe_lm_head": (C.c_int, [C.c_void_p, C.c_int32, C.c_void_p, C.c_void_p, C.c_int32, C.c_int32]),
     "moe_residency_summary": (C.c_int, [C.c_void_p, C.POINTER(moe_residency)]),
     "moe_device_status": (C.c_int, [C.c_void_p, C.POINTER(C.c_int32)]),
     "moe_ctx_set_profiling": (C.c_int, [C.c_void_p, C.c_int32]),
@@ -320,6 +322,25 @@ class Context:
         _check(lib.moe_forward_block(self.h, layer, T, C.c_void_p(hidden_ptr), C.c_void_p(out_ptr),
                                      C.c_void_p(sel_idx_ptr or None), C.c_void_p(sel_w_ptr or None), ptr_kind),
                self.h)
+
+    def lm_head_upload(self, output_weight: Optional["Tensor"], token_embd: Optional["Tensor"], hidden: int):
+        """The LM head: output.weight, or the tied token_embd.weight when it is
+        absent (moe_lm_head_upload); both None: the synthetic logits."""
+        o = tensor_c(output_weight) if output_weight is not None else None
+        e = tensor_c(token_embd) if token_embd is not None else None
+        _check(lib.moe_lm_head_upload(self.h, C.byref(o) if o is not None else None,
+                                      C.byref(e) if e is not None else None, hidden), self.h)
+        self._keep_head = (output_weight, token_embd)
+
+    def lm_head(self, normed: np.ndarray, n_logits: int) -> np.ndarray:
+        """logits [T, n_logits] of final-normed rows [T, hidden] (moe_lm_head)."""
+        x = np.ascontiguousarray(normed, dtype=np.float32)
+        out = np.empty((x.shape[0], n_logits), dtype=np.float32)
+        _check(lib.moe_lm_head(self.h, x.shape[0], _ptr(x), _ptr(out), n_logits, PTR_HOST), self.h)
+        return out
+
+    def lm_head_ptrs(self, T: int, normed_ptr: int, logits_ptr: int, n_logits: int, ptr_kind: int = PTR_DEVICE):
+        _check(lib.moe_lm_head(self.h, T, C.c_void_p(normed_ptr), C.c_void_p(logits_ptr), n_logits, ptr_kind), self.h)
 
     def prefill_ffn_layers(self, first_layer: int, n_layers: int, hidden: np.ndarray) -> np.ndarray:
         """Layer-major prefill of FFN sublayers first_layer .. + n_layers - 1 over all

@@ -650,6 +650,55 @@ int orc_moe_forward_ex(const orc_layer *L, int T, const float *x, float *out,
     return ORC_OK;
 }
 
+/* project_lm_head (src/qwen_deepseek.rs:584-632) for T rows. head: GGUF bytes
+ * of the chosen tensor (output.weight, else token_embd.weight; NULL: none),
+ * shaped = its shape is [hidden, head_rows] with head_rows > 0, else
+ * head_rows = elements / hidden (0: not whole rows). Per row: the first
+ * min(n_logits, head_rows) logits are the matvec (matvec_any: F32 rows
+ * sequential multiply-then-add, quantised rows with int8 activation blocks as
+ * the experts), the rest normed[i mod hidden] * 0.05; the unshaped head is used
+ * only when head_rows == n_logits; otherwise base + normed[i mod hidden] * 0.1 +
+ * (i mod 13) * 0.01 with base = tanh(sum(normed) / 16), the sum in element
+ * order. */
+int orc_lm_head(int type, const uint8_t *head, int shaped, int64_t head_rows, int hidden, int T,
+                const float *normed, int n_logits, float *logits)
+{
+    if (n_logits <= 0 || T <= 0) return ORC_OK;
+    if (hidden <= 0) return ORC_ERR_ARG;
+    const int product = head && head_rows > 0 && (shaped || head_rows == n_logits);
+    int8_t *xq = NULL;
+    float *dx = NULL;
+    if (product && type != ORC_F32) {
+        xq = (int8_t *)malloc((size_t)hidden);
+        dx = (float *)malloc((size_t)(hidden / 32 + 1) * sizeof(float));
+        if (!xq || !dx) { free(xq); free(dx); return ORC_ERR_ARG; }
+    }
+    const size_t rb = product ? orc_row_bytes(type, hidden) : 0;
+    if (product && !rb) { free(xq); free(dx); return ORC_ERR_ARG; }
+    for (int t = 0; t < T; t++) {
+        const float *x = normed + (size_t)t * hidden;
+        float *out = logits + (size_t)t * n_logits;
+        if (product) {
+            const int target = n_logits < head_rows ? n_logits : (int)head_rows;
+            if (type != ORC_F32 && orc_quantize_act(x, hidden, xq, dx) != ORC_OK) { free(xq); free(dx); return ORC_ERR_ARG; }
+            for (int r = 0; r < target; r++) {
+                const uint8_t *row = head + (size_t)r * rb;
+                out[r] = type == ORC_F32 ? row_dot_f32((const float *)row, x, hidden)
+                                         : orc_row_dot_q(type, row, xq, dx, hidden);
+            }
+            for (int i = target; i < n_logits; i++) out[i] = x[i % hidden] * 0.05f;
+        } else {
+            float sum = 0.0f;
+            for (int i = 0; i < hidden; i++) sum += x[i];
+            const float base = tanhf(sum / 16.0f);
+            for (int i = 0; i < n_logits; i++) out[i] = base + x[i % hidden] * 0.1f + (float)(i % 13) * 0.01f;
+        }
+    }
+    free(xq);
+    free(dx);
+    return ORC_OK;
+}
+
 /* Canonical dispatch order of the batched path: slots grouped by expert
  * ascending, tokens ascending inside each expert (a stable counting sort). */
 int orc_permutation(const int32_t *sel_idx, int T, int k, int E, int32_t *offsets, int32_t *perm_token)

@@ -94,6 +94,10 @@ int  orc_select(const orc_layer *L, const float *logits, int32_t *idx, float *w)
 int orc_moe_forward(const orc_layer *L, int T, const float *x, float *out,
                     int32_t *sel_idx, float *sel_w, int n_threads);
 
+/* project_lm_head for T rows (see moe_oracle.c). */
+int orc_lm_head(int type, const uint8_t *head, int shaped, int64_t head_rows, int hidden, int T,
+                const float *normed, int n_logits, float *logits);
+
 /* Canonical dispatch permutation: slots sorted by (expert asc, token asc).
  * offsets[E+1]; perm_token[T*k] = token of each slot. */
 int orc_permutation(const int32_t *sel_idx, int T, int k, int E,

@@ -53,6 +53,8 @@ def _load():
         "orc_moe_forward": (C.c_int, [C.POINTER(orc_layer), C.c_int, C.c_void_p, C.c_void_p, C.c_void_p,
                                       C.c_void_p, C.c_int]),
         "orc_permutation": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p]),
+        "orc_lm_head": (C.c_int, [C.c_int, C.c_void_p, C.c_int, C.c_int64, C.c_int, C.c_int, C.c_void_p, C.c_int,
+                                  C.c_void_p]),
         "orc_moe_forward_ex": (C.c_int, [C.POINTER(orc_layer), C.c_int, C.c_void_p, C.c_void_p, C.c_void_p,
                                          C.c_void_p, C.c_int, C.c_int]),
         "orc_gen_normal": (C.c_int, [C.c_uint64, C.c_uint64, C.c_uint64, C.c_float, C.c_void_p, C.c_int]),
@@ -121,6 +123,25 @@ def rmsnorm(x: np.ndarray, w, eps: float) -> np.ndarray:
     out = np.empty_like(x)
     for t in range(T):
         lib.orc_rmsnorm(_p(x[t]), _p(wv) if wv is not None else None, H, C.c_float(eps), _p(out[t]))
+    return out
+
+
+def lm_head(head, hidden: int, normed: np.ndarray, n_logits: int) -> np.ndarray:
+    """project_lm_head (orc_lm_head) of normed rows [T, hidden]; head: a
+    jeromoe Tensor (output.weight or the tied token_embd.weight) or None."""
+    x = np.ascontiguousarray(normed, dtype=np.float32)
+    T = x.shape[0]
+    out = np.zeros((T, n_logits), dtype=np.float32)
+    if head is None:
+        rc = lib.orc_lm_head(0, None, 0, 0, hidden, T, _p(x), n_logits, _p(out))
+    else:
+        shape = list(head.shape)
+        shaped = len(shape) == 2 and shape[0] == hidden and shape[1] > 0
+        n = int(np.prod(shape))
+        rows = shape[1] if shaped else (n // hidden if n % hidden == 0 else 0)
+        data = np.ascontiguousarray(head.data)
+        rc = lib.orc_lm_head(int(head.quant), _p(data), int(shaped), rows, hidden, T, _p(x), n_logits, _p(out))
+    assert rc == 0, rc
     return out
 
 

@@ -576,3 +576,75 @@ def test_gpu_reupload_replaces_layer():
     assert not np.allclose(a, b)
     ref = oracle_layer(w2, cfg).forward(x, 2)[0]
     assert row_rel_err(b, ref).max() <= OUT_TOL
+
+
+# ------------------------------------------------------------------ LM head
+
+def _lm_head_case(quant, hidden, rows, seed):
+    rng = np.random.default_rng(seed)
+    W = (rng.standard_normal((rows, hidden)) * 0.05).astype(np.float32)
+    if quant == jm.F32:
+        return jm.f32_tensor(W, [hidden, rows])
+    return jm.Tensor(quant, [hidden, rows], orc.quantize_rows(quant, W).reshape(-1))
+
+
+@pytest.mark.parametrize("quant", [jm.F32, jm.Q8_0, jm.Q4_K])
+@pytest.mark.parametrize("T", [1, 7, 64])
+def test_gpu_lm_head(quant, T):
+    """moe_lm_head against the oracle's project_lm_head: fewer logits than
+    head rows (the first rows), more (the rows past the head are
+    normed * 0.05, bit for bit), and the tied token_embd head when
+    output.weight is absent. Rows within 1e-2 max relative error."""
+    hidden, rows = 1024, 10000
+    head = _lm_head_case(quant, hidden, rows, 3)
+    x = np.random.default_rng(T).standard_normal((T, hidden)).astype(np.float32)
+    with jm.Context(0, 64, 1) as ctx:
+        ctx.lm_head_upload(head, None, hidden)
+        for n in (9000, 10050):
+            got = ctx.lm_head(x, n)
+            ref = orc.lm_head(head, hidden, x, n)
+            assert np.all(np.isfinite(got))
+            tgt = min(n, rows)
+            assert row_rel_err(got[:, :tgt], ref[:, :tgt]).max() <= OUT_TOL
+            np.testing.assert_array_equal(got[:, tgt:], ref[:, tgt:])
+        ctx.lm_head_upload(None, head, hidden)   # tied embeddings
+        got = ctx.lm_head(x, rows)
+        assert row_rel_err(got, orc.lm_head(head, hidden, x, rows)).max() <= OUT_TOL
+        assert ctx.device_status() == 0
+
+
+def test_gpu_lm_head_flat_synthetic_device_pointers_and_errors():
+    """A flat head of n_logits * hidden elements, the synthetic logits (no
+    head, or one that fits no branch), device pointers (bit for bit the host
+    call), T = 0, and the errors: no upload, T above max_tokens, an
+    unsupported quantisation, a byte count that does not match the shape."""
+    import torch
+    hidden, T, n = 512, 5, 777
+    rng = np.random.default_rng(1)
+    x = rng.standard_normal((T, hidden)).astype(np.float32)
+    flat = jm.Tensor(jm.Q8_0, [n * hidden],
+                     orc.quantize_rows(jm.Q8_0, rng.standard_normal((n, hidden)).astype(np.float32)).reshape(-1))
+    with jm.Context(0, 8, 1) as ctx:
+        with pytest.raises(jm.NotUploaded):
+            ctx.lm_head(x, n)
+        ctx.lm_head_upload(flat, None, hidden)
+        got = ctx.lm_head(x, n)
+        assert row_rel_err(got, orc.lm_head(flat, hidden, x, n)).max() <= OUT_TOL
+        syn = ctx.lm_head(x, n + 1)   # the flat head no longer fits: synthetic logits
+        np.testing.assert_allclose(syn, orc.lm_head(None, hidden, x, n + 1), rtol=0, atol=2e-6)
+        xd = torch.from_numpy(x).cuda()
+        for m in (n, n + 1):
+            od = torch.empty((T, m), dtype=torch.float32, device="cuda")
+            ctx.lm_head_ptrs(T, xd.data_ptr(), od.data_ptr(), m)
+            assert ctx.device_status() == 0
+            np.testing.assert_array_equal(od.cpu().numpy(), ctx.lm_head(x, m))
+        ctx.lm_head_upload(None, None, hidden)
+        np.testing.assert_allclose(ctx.lm_head(x, 300), orc.lm_head(None, hidden, x, 300), rtol=0, atol=2e-6)
+        assert ctx.lm_head(x[:0], 300).shape == (0, 300)
+        with pytest.raises(jm.ContextLengthExceeded):
+            ctx.lm_head(np.zeros((9, hidden), np.float32), 300)
+        with pytest.raises(jm.CapabilityMismatch):
+            ctx.lm_head_upload(jm.Tensor(14, [hidden, 4],
+                                         np.zeros(4 * 420, np.uint8)), None, hidden)
+        with pytest.raises(jm.TensorBoundsError):
+            ctx.lm_head_upload(jm.Tensor(jm.Q8_0, [hidden, 4], np.zeros(10, np.uint8)), None, hidden)

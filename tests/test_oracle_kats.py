@@ -154,3 +154,66 @@ def test_oracle_two_readings_of_the_quantised_dot(cid):
     np.testing.assert_array_equal(sw8, swf)
     err = np.abs(o8 - of).max(axis=1) / np.abs(of).max(axis=1)
     assert 1e-3 < err.max() < 3e-2, err
+
+
+def _lm_head_numpy(hidden, normed, n_logits, head_rows_f32=None, flat=False):
+    """project_lm_head (src/qwen_deepseek.rs:584-632) in numpy for an f32 head
+    of rows [rows, hidden], or the synthetic logits when head_rows_f32 is None."""
+    T = normed.shape[0]
+    out = np.zeros((T, n_logits), np.float32)
+    for t in range(T):
+        x = normed[t]
+        if head_rows_f32 is None:
+            s = np.float32(0)
+            for v in x:
+                s = np.float32(s + v)
+            base = np.float32(np.tanh(np.float32(s / np.float32(16))))
+            idx = np.arange(n_logits)
+            out[t] = base + x[idx % hidden] * np.float32(0.1) + (idx % 13).astype(np.float32) * np.float32(0.01)
+            continue
+        target = n_logits if flat else min(n_logits, head_rows_f32.shape[0])
+        out[t, :target] = head_rows_f32[:target].astype(np.float64) @ x.astype(np.float64)
+        idx = np.arange(target, n_logits)
+        out[t, target:] = x[idx % hidden] * np.float32(0.05)
+    return out
+
+
+@pytest.mark.parametrize("n_logits", [37, 64, 100])
+def test_oracle_lm_head_branches(n_logits):
+    """The oracle LM head: a shaped f32 head [hidden, rows] (fewer, equal and
+    more logits than rows; the rows past the head are normed * 0.05), a flat
+    head of n_logits * hidden elements, a head that fits neither branch and no
+    head (the synthetic logits)."""
+    hidden, rows, T = 64, 64, 3
+    rng = np.random.default_rng(5)
+    W = rng.standard_normal((rows, hidden)).astype(np.float32)
+    x = rng.standard_normal((T, hidden)).astype(np.float32)
+    head = jm.f32_tensor(W, [hidden, rows])
+    got = orc.lm_head(head, hidden, x, n_logits)
+    np.testing.assert_allclose(got, _lm_head_numpy(hidden, x, n_logits, W), rtol=1e-5, atol=1e-5)
+    np.testing.assert_array_equal(got[:, rows:], _lm_head_numpy(hidden, x, n_logits, W)[:, rows:])
+    Wf = rng.standard_normal((n_logits, hidden)).astype(np.float32)
+    flat = jm.f32_tensor(Wf, [n_logits * hidden])
+    np.testing.assert_allclose(orc.lm_head(flat, hidden, x, n_logits),
+                               _lm_head_numpy(hidden, x, n_logits, Wf, flat=True), rtol=1e-5, atol=1e-5)
+    synth_ref = _lm_head_numpy(hidden, x, n_logits)
+    odd = jm.f32_tensor(np.ones(hidden * 3 + 1, np.float32), [hidden * 3 + 1])
+    np.testing.assert_allclose(orc.lm_head(odd, hidden, x, n_logits), synth_ref, rtol=1e-6, atol=1e-6)
+    np.testing.assert_allclose(orc.lm_head(None, hidden, x, n_logits), synth_ref, rtol=1e-6, atol=1e-6)
+
+
+@pytest.mark.parametrize("quant", [jm.Q8_0, jm.Q4_K])
+def test_oracle_lm_head_quantised(quant):
+    """A quantised head: the product with int8 activation blocks stays within
+    the quantisation error of the dequantised f32 product."""
+    hidden, rows, T, n_logits = 256, 48, 2, 40
+    rng = np.random.default_rng(9)
+    W = rng.standard_normal((rows, hidden)).astype(np.float32) * 0.05
+    q = orc.quantize_rows(quant, W)
+    head = jm.Tensor(quant, [hidden, rows], q.reshape(-1))
+    x = rng.standard_normal((T, hidden)).astype(np.float32)
+    got = orc.lm_head(head, hidden, x, n_logits)
+    Wd = np.stack([orc.dequantize_row(quant, q[r], hidden) for r in range(rows)])
+    ref = _lm_head_numpy(hidden, x, n_logits, Wd)
+    err = np.abs(got - ref).max(axis=1) / np.abs(ref).max(axis=1)
+    assert err.max() <= 1e-2, err
