@@ -186,6 +186,8 @@ struct moe_ctx {
         void *buf = nullptr;     // call buffers
         size_t buf_bytes = 0;
         int *errw = nullptr;     // the status word at the start of buf
+        MatMaps maps_tc{};       // tensor-core boxes (128 rows), when tc
+        bool tc = false;         // the head suits the int8 tensor-core down launch
     } head;
     Profiler prof;
     EpState ep;
@@ -657,6 +659,7 @@ int ep_reserve(moe_ctx *ctx, EpDims d)
         ep.arena = blk;
         ep_carve(d, static_cast<uint8_t *>(blk), &ep);
         CUDA_TRY(ctx, cudaMemset(ep.zero, 0, 4), "cudaMemset");
+        CUDA_TRY(ctx, cudaDeviceSynchronize(), "cudaDeviceSynchronize");   // before any context-stream use
     }
     const size_t off_bytes = (size_t)ep.world * (ep.E + 1) * 4, plan_bytes = ep_plan_bytes(ep.world, ep.E);
     if (ep.h_off_bytes < off_bytes) {
@@ -761,6 +764,7 @@ int ep_p2p_prepare(moe_ctx *ctx, const LayerStore &L, bool *use)
     CUDA_TRY(ctx, cudaMalloc(&arena, ep.p2p.bytes), "cudaMalloc(peer-exchange arena)");
     ep.p2p_arena = static_cast<uint8_t *>(arena);
     CUDA_TRY(ctx, cudaMemset(arena, 0, ep.p2p.bytes), "cudaMemset(peer-exchange arena)");
+    CUDA_TRY(ctx, cudaDeviceSynchronize(), "cudaDeviceSynchronize");   // zero before peers map it
     ep.p2p_peer[me] = ep.p2p_arena;
     int ok = 1;
     if (G > 1) {
@@ -1003,6 +1007,7 @@ int moe_layer_upload(moe_ctx *ctx, int32_t layer, const moe_layer_desc *desc)
         CUDA_TRY(ctx, cudaMemset(ctx->scratch.sync, 0, kRoutingTicketBytes), "cudaMemset(routing tickets)");
         CUDA_TRY(ctx, cudaMemset(ctx->scratch.dep, 0, ((size_t)ctx->scratch.dep_cap + 1) * 4),
                  "cudaMemset(chunk counters)");
+        CUDA_TRY(ctx, cudaDeviceSynchronize(), "cudaDeviceSynchronize");   // the context stream does not wait for it
     }
     LayerStore &L = ctx->layers[layer];
     void *blk = nullptr;
@@ -1264,10 +1269,17 @@ int moe_lm_head_upload(moe_ctx *ctx, const moe_tensor *output_weight, const moe_
     hd.rows = (int)rows;
     hd.m = to_dev(plan, base, plan.meta_bytes ? base + o_meta : nullptr);
     plan_slices(hd.m);
-    const int r = make_matrix_maps(hd.m, &hd.maps, 32);
+    int r = make_matrix_maps(hd.m, &hd.maps, 32);
     if (r != 0) return fail(ctx, MOE_ERR_CUDA, "cuTensorMapEncodeTiled failed (CUresult %d)", r);
+    hd.tc = t->quant != MOE_QUANT_F32 && rows % 128 == 0 && hidden % (t->quant == MOE_QUANT_Q4_K ? 256 : 128) == 0;
+    if (hd.tc && (r = make_matrix_maps(hd.m, &hd.maps_tc, 128)) != 0)
+        return fail(ctx, MOE_ERR_CUDA, "cuTensorMapEncodeTiled failed (CUresult %d)", r);
     return MOE_OK;
 }
+
+// Rows of normed activations from which the LM head's product runs on the
+// int8 tensor cores (decode_tc.cu down launch) instead of the streaming kernel.
+constexpr int kLmHeadTcMinTokens = 8;
 
 // logits [T x n_logits] of T normed rows [T x hidden], each row as
 // project_lm_head: the head's first min(n_logits, rows) rows as a quantised
@@ -1290,7 +1302,13 @@ int moe_lm_head(moe_ctx *ctx, int32_t T, const float *normed, float *logits, int
     const int H = hd.hidden;
     const bool product = hd.has && hd.rows > 0 && (hd.shaped || hd.rows == n_logits);
     const int target = product ? std::min(n_logits, hd.rows) : 0;
-    const bool direct = ptr_kind == MOE_PTR_DEVICE && target == n_logits;
+    // int8 tensor cores from kLmHeadTcMinTokens rows on: items of 128 head rows,
+    // so the product covers target rounded up to 128 (at most the head's rows)
+    const bool tc = product && hd.tc &&
+                    !(ctx->spec.flags & MOE_FLAG_INT8_TENSOR_CORES_NEVER) &&
+                    ((ctx->spec.flags & MOE_FLAG_INT8_TENSOR_CORES_ALWAYS) || T >= kLmHeadTcMinTokens);
+    const int yrows = tc ? (target + 127) / 128 * 128 : target;
+    const bool direct = ptr_kind == MOE_PTR_DEVICE && target == n_logits && yrows == target;
     // call buffers: the status word and the problem first (fixed offsets, so the
     // word is zero from its allocation on), then normed rows, int8 blocks,
     // product rows, logits
@@ -1298,7 +1316,7 @@ int moe_lm_head(moe_ctx *ctx, int32_t T, const float *normed, float *logits, int
     auto take = [&](size_t b) { size_t o = off; off += align_up(b ? b : 1, 256); return o; };
     const size_t o_e = take(16), o_p = take(sizeof(Problem) + 16), o_x = take((size_t)T * H * 4),
                  o_q = take((size_t)T * H), o_d = take((size_t)T * (H / 32) * 4), o_s = take((size_t)T * (H / 32) * 4),
-                 o_y = take(direct ? 0 : (size_t)T * std::max(target, 1) * 4), o_l = take((size_t)T * n_logits * 4);
+                 o_y = take(direct ? 0 : (size_t)T * std::max(yrows, 1) * 4), o_l = take((size_t)T * n_logits * 4);
     if (hd.buf_bytes < off) {
         CUDA_TRY(ctx, cudaStreamSynchronize(st), "cudaStreamSynchronize");
         if (hd.buf) cudaFree(hd.buf);
@@ -1307,7 +1325,8 @@ int moe_lm_head(moe_ctx *ctx, int32_t T, const float *normed, float *logits, int
         hd.errw = nullptr;
         CUDA_TRY(ctx, cudaMalloc(&hd.buf, off), "cudaMalloc(LM head buffers)");
         hd.buf_bytes = off;
-        CUDA_TRY(ctx, cudaMemset(hd.buf, 0, off), "cudaMemset(LM head buffers)");
+        // on the call's stream: the context stream does not wait for the legacy stream
+        CUDA_TRY(ctx, cudaMemsetAsync(hd.buf, 0, off, st), "cudaMemset(LM head buffers)");
     }
     uint8_t *b = static_cast<uint8_t *>(hd.buf);
     // the device status word: the context's, or (no layer uploaded yet) one of the head's own
@@ -1322,7 +1341,7 @@ int moe_lm_head(moe_ctx *ctx, int32_t T, const float *normed, float *logits, int
     cudaError_t e;
     if (product) {
         FwdParams pl{};
-        pl.T = T; pl.H = target; pl.E = 1; pl.k = 1; pl.I = H; pl.S = 0; pl.W = H;
+        pl.T = T; pl.H = yrows; pl.E = 1; pl.k = 1; pl.I = H; pl.S = 0; pl.W = H;
         pl.max_problems = 1;
         pl.problems = reinterpret_cast<Problem *>(b + o_p);
         pl.n_active = reinterpret_cast<int32_t *>(b + o_p + sizeof(Problem));
@@ -1330,9 +1349,10 @@ int moe_lm_head(moe_ctx *ctx, int32_t T, const float *normed, float *logits, int
         pl.y = direct ? lg : reinterpret_cast<float *>(b + o_y);
         LayerDev Lh{};
         Lh.down = hd.m;
-        Lh.down.rows = target;   // the first rows of the head (rows are contiguous)
+        Lh.down.rows = yrows;   // the first rows of the head (rows are contiguous)
         LayerMaps lm{};
         lm.down = hd.maps;
+        lm.down_tc = hd.maps_tc;
         if (hd.m.type == FMT_F32) {
             pl.af = const_cast<float *>(x);
         } else {
@@ -1344,8 +1364,10 @@ int moe_lm_head(moe_ctx *ctx, int32_t T, const float *normed, float *logits, int
         }
         if ((e = launch_lm_head_prep(pl.problems, pl.n_active, T, st)) != cudaSuccess)
             return cuda_fail(ctx, e, "LM head problem");
-        if ((e = launch_down(pl, Lh, lm, 0, ctx->num_sms, st)) != cudaSuccess) return cuda_fail(ctx, e, "LM head");
-        if (!direct && (e = launch_lm_head_scatter(pl.y, target, x, H, lg, n_logits, T, ctx->num_sms, st)) !=
+        e = tc && decode_tc_down_ok(pl, Lh) ? launch_decode_tc_down(pl, Lh, lm, ctx->num_sms, st)
+                                            : launch_down(pl, Lh, lm, 0, ctx->num_sms, st);
+        if (e != cudaSuccess) return cuda_fail(ctx, e, "LM head");
+        if (!direct && (e = launch_lm_head_scatter(pl.y, yrows, target, x, H, lg, n_logits, T, ctx->num_sms, st)) !=
                            cudaSuccess)
             return cuda_fail(ctx, e, "LM head rows");
     } else if ((e = launch_lm_head_synth(x, H, lg, n_logits, T, st)) != cudaSuccess) {

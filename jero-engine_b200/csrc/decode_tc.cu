@@ -697,6 +697,20 @@ bool decode_tc_ok(const FwdParams &p, const LayerDev &L)
     return true;
 }
 
+bool decode_tc_down_ok(const FwdParams &p, const LayerDev &L)
+{
+    return dtc_matrix_ok(L.down) && p.H % 128 == 0 && p.W % 128 == 0 && aligned16(p.aq) && aligned16(p.ad) &&
+           aligned16(p.as);
+}
+
+cudaError_t launch_decode_tc_down(const FwdParams &p, const LayerDev &L, const LayerMaps &maps, int num_sms,
+                                  cudaStream_t st)
+{
+    if (!decode_tc_down_ok(p, L)) return cudaErrorInvalidValue;
+    return L.down.type == FMT_Q4_K ? launch_dtc<FMT_Q4_K, 1>(p, L, maps, 0, num_sms, st)
+                                   : launch_dtc<FMT_Q8_0, 1>(p, L, maps, 0, num_sms, st);
+}
+
 cudaError_t launch_decode_tc(const FwdParams &p, const LayerDev &L, const LayerMaps &maps, int num_sms,
                              const Marker &mk, cudaStream_t st, bool shared_only)
 {

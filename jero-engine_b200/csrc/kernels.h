@@ -69,6 +69,11 @@ cudaError_t launch_prefill(const FwdParams &p, const LayerDev &L, const LayerMap
 bool decode_tc_ok(const FwdParams &p, const LayerDev &L);
 cudaError_t launch_decode_tc(const FwdParams &p, const LayerDev &L, const LayerMaps &maps, int num_sms,
                              const Marker &mk, cudaStream_t st, bool shared_only = false);
+// The down launch alone over the routed problems (one matrix of rows of p.H,
+// K = p.W): the LM head's product. decode_tc_down_ok: formats, shapes, buffers.
+bool decode_tc_down_ok(const FwdParams &p, const LayerDev &L);
+cudaError_t launch_decode_tc_down(const FwdParams &p, const LayerDev &L, const LayerMaps &maps, int num_sms,
+                                  cudaStream_t st);
 
 // The expert FFN of small batches as one persistent launch on the tensor
 // cores with f16 operands (experts_tc.cu): gate/up + SwiGLU and down, the
@@ -89,8 +94,8 @@ cudaError_t launch_fused_i8(const FwdParams &p, const LayerDev &L, const LayerMa
 // LM head (lm_head.cu): the problem entry of its product on the down-projection
 // kernels, the rows past the head's rows, the synthetic logits without a head.
 cudaError_t launch_lm_head_prep(Problem *prob, int32_t *n_active, int T, cudaStream_t st);
-cudaError_t launch_lm_head_scatter(const float *y, int target, const float *normed, int hidden, float *logits, int n,
-                                   int T, int num_sms, cudaStream_t st);
+cudaError_t launch_lm_head_scatter(const float *y, int ystride, int target, const float *normed, int hidden,
+                                   float *logits, int n, int T, int num_sms, cudaStream_t st);
 cudaError_t launch_lm_head_synth(const float *normed, int hidden, float *logits, int n, int T, cudaStream_t st);
 
 // Expert-parallel exchange (ep.cu): bytes of one packed token row, and the

@@ -20,16 +20,16 @@ __global__ void lm_head_prep_kernel(Problem *prob, int32_t *n_active, int T)
     *n_active = 1;
 }
 
-// logits[t][i] for i < target from the product rows y [T][target], and for
+// logits[t][i] for i < target from the product rows y [T][ystride], and for
 // target <= i < n the reference's filler normed[t][i mod hidden] * 0.05.
-__global__ void lm_head_scatter_kernel(const float *y, int target, const float *normed, int hidden, float *logits,
-                                       int n, int T)
+__global__ void lm_head_scatter_kernel(const float *y, int ystride, int target, const float *normed, int hidden,
+                                       float *logits, int n, int T)
 {
     const long long total = (long long)T * n;
     for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
          i += (long long)gridDim.x * blockDim.x) {
         const int t = (int)(i / n), c = (int)(i - (long long)t * n);
-        logits[i] = c < target ? y[(size_t)t * target + c] : __fmul_rn(normed[(size_t)t * hidden + c % hidden], 0.05f);
+        logits[i] = c < target ? y[(size_t)t * ystride + c] : __fmul_rn(normed[(size_t)t * hidden + c % hidden], 0.05f);
     }
 }
 
@@ -59,14 +59,14 @@ cudaError_t launch_lm_head_prep(Problem *prob, int32_t *n_active, int T, cudaStr
     return cudaGetLastError();
 }
 
-cudaError_t launch_lm_head_scatter(const float *y, int target, const float *normed, int hidden, float *logits, int n,
-                                   int T, int num_sms, cudaStream_t st)
+cudaError_t launch_lm_head_scatter(const float *y, int ystride, int target, const float *normed, int hidden,
+                                   float *logits, int n, int T, int num_sms, cudaStream_t st)
 {
     const long long total = (long long)T * n;
     long long blocks = (total + 255) / 256;
     if (blocks > 4LL * num_sms) blocks = 4LL * num_sms;
     if (blocks < 1) blocks = 1;
-    lm_head_scatter_kernel<<<(int)blocks, 256, 0, st>>>(y, target, normed, hidden, logits, n, T);
+    lm_head_scatter_kernel<<<(int)blocks, 256, 0, st>>>(y, ystride, target, normed, hidden, logits, n, T);
     return cudaGetLastError();
 }
 

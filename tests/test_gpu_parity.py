@@ -589,18 +589,20 @@ def _lm_head_case(quant, hidden, rows, seed):
 
 
 @pytest.mark.parametrize("quant", [jm.F32, jm.Q8_0, jm.Q4_K])
-@pytest.mark.parametrize("T", [1, 7, 64])
-def test_gpu_lm_head(quant, T):
+@pytest.mark.parametrize("T", [1, 7, 8, 64])
+@pytest.mark.parametrize("rows", [10000, 10240])
+def test_gpu_lm_head(quant, T, rows):
     """moe_lm_head against the oracle's project_lm_head: fewer logits than
     head rows (the first rows), more (the rows past the head are
     normed * 0.05, bit for bit), and the tied token_embd head when
-    output.weight is absent. Rows within 1e-2 max relative error."""
-    hidden, rows = 1024, 10000
+    output.weight is absent. Rows within 1e-2 max relative error. 10240 rows
+    (whole 128-row tiles) take the int8 tensor-core launch from 8 tokens on."""
+    hidden = 1024
     head = _lm_head_case(quant, hidden, rows, 3)
     x = np.random.default_rng(T).standard_normal((T, hidden)).astype(np.float32)
     with jm.Context(0, 64, 1) as ctx:
         ctx.lm_head_upload(head, None, hidden)
-        for n in (9000, 10050):
+        for n in (9000, rows + 50):
             got = ctx.lm_head(x, n)
             ref = orc.lm_head(head, hidden, x, n)
             assert np.all(np.isfinite(got))
@@ -648,3 +650,19 @@ def test_gpu_lm_head_flat_synthetic_device_pointers_and_errors():
                                          np.zeros(4 * 420, np.uint8)), None, hidden)
         with pytest.raises(jm.TensorBoundsError):
             ctx.lm_head_upload(jm.Tensor(jm.Q8_0, [hidden, 4], np.zeros(10, np.uint8)), None, hidden)
+
+
+@pytest.mark.parametrize("quant", [jm.Q8_0, jm.Q4_K])
+def test_gpu_lm_head_tensor_cores_match_streaming(quant):
+    """The int8 tensor-core product and the streaming one over the same head
+    and rows: the same integer block sums, f32 sums in another order."""
+    hidden, rows, T = 2048, 4096, 24
+    head = _lm_head_case(quant, hidden, rows, 8)
+    x = np.random.default_rng(2).standard_normal((T, hidden)).astype(np.float32)
+    outs = []
+    for flags in (jm.FLAG_INT8_TENSOR_CORES_NEVER, jm.FLAG_INT8_TENSOR_CORES_ALWAYS):
+        with jm.Context(0, T, 1, flags=flags) as ctx:
+            ctx.lm_head_upload(head, None, hidden)
+            outs.append(ctx.lm_head(x, 3000))
+    assert row_rel_err(outs[1], outs[0]).max() <= 1e-5
+    assert row_rel_err(outs[1], orc.lm_head(head, hidden, x, 3000)).max() <= OUT_TOL
