@@ -138,6 +138,12 @@ typedef struct moe_device_spec {
 #define MOE_FLAG_FUSED_I8_NEVER 64
 #define MOE_FLAG_FUSED_I8_ALWAYS 128
 #define MOE_FUSED_I8_MAX_SLOTS_PER_EXPERT 8
+/* A forward of fewer than MOE_FUSED_MIN_TOKENS tokens (one token: each routed
+ * expert has one slot) runs the streaming int8 kernels rather than a fused
+ * launch: their short per-tile chains beat the fused launch's serial K steps
+ * when only k experts stream. MOE_FLAG_FUSED_I8_NEVER / ALWAYS still force the
+ * fused launch. */
+#define MOE_FUSED_MIN_TOKENS 2
 
 /* Memory the admission check compares against. The real inspector reads
  * cudaMemGetInfo on spec->device; tests pass a fixed one, as the reference's

@@ -508,6 +508,8 @@ bool use_fused_tc(const moe_device_spec &spec, int T)
 {
     if (spec.flags & (MOE_FLAG_FUSED_TC_NEVER | MOE_FLAG_INT8_TENSOR_CORES_NEVER | MOE_FLAG_INT8_TENSOR_CORES_ALWAYS))
         return false;
+    // below MOE_FUSED_MIN_TOKENS the streaming kernels, unless a flag names a fused form
+    if (T < MOE_FUSED_MIN_TOKENS && !(spec.flags & (MOE_FLAG_FUSED_I8_NEVER | MOE_FLAG_FUSED_I8_ALWAYS))) return false;
     return T < MOE_TENSOR_CORE_MIN_TOKENS;
 }
 
