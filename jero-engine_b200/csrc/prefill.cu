@@ -35,7 +35,10 @@ constexpr int kM = 128;                         // weight rows per item (MMA M, 
 constexpr int kKS = 64;                         // K per stage: one 128-byte swizzled row of f16
 constexpr int kCapGU = 128, kCapDN = 256;       // slots per item (MMA N) of the gate/up and down launches
 constexpr int kXBoxRows = 32, kXBoxBytes = kXBoxRows * 128;
-constexpr int kWarpTma = 0, kWarpMma = 1, kDeqWarp0 = 2, kDeqWarps = 8, kEpiWarp0 = 10, kEpiWarps = 4;
+// two MMA-issuing warps: one thread completes about one tcgen05 instruction per
+// 130-250 cycles, so gate/up (eight MMAs per K step) issues matrix m from warp
+// kWarpMma + m; down (four) uses the first only
+constexpr int kWarpTma = 0, kWarpMma = 1, kMmaWarps = 2, kDeqWarp0 = 3, kDeqWarps = 8, kEpiWarp0 = 11, kEpiWarps = 4;
 constexpr int kTcThreads = (kEpiWarp0 + kEpiWarps) * 32;
 constexpr int kMaxStages = 6;
 constexpr int kTmemCols = 512, kAccCols = 256;  // two accumulator buffers of 256 columns
@@ -113,8 +116,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     // weight tiles (dequant warps, w_full); one tensor-core commit frees both
     uint64_t *x_full = bars, *w_full = x_full + kMaxStages, *k_empty = w_full + kMaxStages;
     uint64_t *q_full = k_empty + kMaxStages, *q_empty = q_full + kMaxStages;
-    uint64_t *acc_full = q_empty + kMaxStages, *acc_empty = acc_full + 2, *drain_bar = acc_empty + 2;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain_bar + 1);
+    uint64_t *acc_full = q_empty + kMaxStages, *acc_empty = acc_full + 2, *drain_bar = acc_empty + 2;   // [2]
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain_bar + 2);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -135,11 +138,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         for (int i = 0; i < c.kst; i++) {
             mbar_init(&x_full[i], 1);
             mbar_init(&w_full[i], kDeqWarps);
-            mbar_init(&k_empty[i], 1);
+            mbar_init(&k_empty[i], NMAT);   // one commit per issuing warp
         }
         for (int i = 0; i < c.qst; i++) { mbar_init(&q_full[i], 1); mbar_init(&q_empty[i], kDeqWarps); }
-        for (int i = 0; i < 2; i++) { mbar_init(&acc_full[i], 1); mbar_init(&acc_empty[i], kEpiWarps); }
-        mbar_init(drain_bar, 1);
+        for (int i = 0; i < 2; i++) { mbar_init(&acc_full[i], NMAT); mbar_init(&acc_empty[i], kEpiWarps); }
+        mbar_init(&drain_bar[0], 1);
+        mbar_init(&drain_bar[1], 1);
         *abort_flag = 0;
         fence_barrier_init();
     }
@@ -195,8 +199,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     drain_wait(&q_full[g % c.qst], (g / c.qst) & 1);
             }
         }
-    } else if (warp == kWarpMma) {
-        if (lane == 0) {
+    } else if (warp < kWarpMma + kMmaWarps) {
+        // issuer mi: matrix mi of every K step (gate/up), or all of them (down, mi = 0)
+        const int mi = warp - kWarpMma;
+        if (lane == 0 && mi < NMAT) {
             RingPos kr, ar;
             bool ok = true, issued = false;
             // smem descriptors of stage 0; a stage, matrix or 16-value K step moves the
@@ -219,10 +225,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                         !tc_wait(&w_full[st], kr.phase, abort_flag, p.err)) { ok = false; break; }
                     tc_fence_after();
                     const uint64_t bd = b_desc0 + (uint64_t)((st * c.x_bytes) >> 4);
-#pragma unroll
-                    for (int m = 0; m < NMAT; m++) {
-                        const uint64_t ad = a_desc0 + (uint64_t)(((st * NMAT + m) * kWTileBytes) >> 4);
-                        const uint32_t d = dbase + (uint32_t)(m * kCapGU);
+                    {
+                        const uint64_t ad = a_desc0 + (uint64_t)(((st * NMAT + mi) * kWTileBytes) >> 4);
+                        const uint32_t d = dbase + (uint32_t)(mi * kCapGU);
 #pragma unroll
                         for (int k16 = 0; k16 < kKS / 16; k16++)
                             tc_mma_f16(d, ad + 2 * k16, bd + 2 * k16, idesc, (kk | k16) != 0);
@@ -235,9 +240,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 tc_commit(&acc_full[ar.slot]);
                 ar.advance(2);
             }
-            if (issued) {   // every MMA has completed before the CTA may release TMEM
-                tc_commit(drain_bar);
-                drain_wait(drain_bar, 0);
+            if (issued) {   // every MMA of this issuer has completed before the CTA may release TMEM
+                tc_commit(&drain_bar[mi]);
+                drain_wait(&drain_bar[mi], 0);
             }
         }
     } else if (warp < kEpiWarp0) {
@@ -483,7 +488,7 @@ cudaError_t launch_tc(const FwdParams &p, const LayerDev &L, const LayerMaps &lm
     c.smem_q = c.smem_w + c.kst * NMAT * kWTileBytes;
     c.smem_tab = c.smem_q + c.qst * NMAT * kQBytes;
     c.smem_bar = c.smem_tab + (((c.max_q + 4) & ~3) * 4 + c.max_q * 16 + 15) / 16 * 16;
-    const size_t smem = (size_t)c.smem_bar + (5 * kMaxStages + 5) * 8 + 16 + 1024;   // barriers + alignment slack
+    const size_t smem = (size_t)c.smem_bar + (5 * kMaxStages + 6) * 8 + 16 + 1024;   // barriers + alignment slack
     if (smem > 232448) return cudaErrorInvalidValue;
     if ((e = cudaFuncSetAttribute(tc_expert_kernel<FMT, NMAT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   (int)smem)) != cudaSuccess)
