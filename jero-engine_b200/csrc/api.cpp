@@ -1280,8 +1280,12 @@ int moe_lm_head_upload(moe_ctx *ctx, const moe_tensor *output_weight, const moe_
 }
 
 // Rows of normed activations from which the LM head's product runs on the
-// int8 tensor cores (decode_tc.cu down launch) instead of the streaming kernel.
+// int8 tensor cores (decode_tc.cu down launch) instead of the streaming kernel,
+// and from which on the f16 tensor-core GEMM (prefill.cu, one dense problem):
+// measured crossovers on a 151936 x 2048 head (Q4_K: f16 159 us vs int8 206 at
+// 16 rows; Q8_0: int8 147 vs f16 166 at 16, f16 167 vs int8 309 at 32).
 constexpr int kLmHeadTcMinTokens = 8;
+constexpr int kLmHeadF16MinTokensQ4K = 16, kLmHeadF16MinTokensQ80 = 24;
 
 // logits [T x n_logits] of T normed rows [T x hidden], each row as
 // project_lm_head: the head's first min(n_logits, rows) rows as a quantised
@@ -1304,11 +1308,22 @@ int moe_lm_head(moe_ctx *ctx, int32_t T, const float *normed, float *logits, int
     const int H = hd.hidden;
     const bool product = hd.has && hd.rows > 0 && (hd.shaped || hd.rows == n_logits);
     const int target = product ? std::min(n_logits, hd.rows) : 0;
-    // int8 tensor cores from kLmHeadTcMinTokens rows on: items of 128 head rows,
-    // so the product covers target rounded up to 128 (at most the head's rows)
-    const bool tc = product && hd.tc &&
-                    !(ctx->spec.flags & MOE_FLAG_INT8_TENSOR_CORES_NEVER) &&
-                    ((ctx->spec.flags & MOE_FLAG_INT8_TENSOR_CORES_ALWAYS) || T >= kLmHeadTcMinTokens);
+    // the product's kernel: 0 streaming, 1 int8 tensor cores (from
+    // kLmHeadTcMinTokens rows), 2 f16 tensor-core GEMM (from kLmHeadF16MinTokens);
+    // the flags force one. Tensor-core items cover 128 head rows, so the product
+    // then spans target rounded up to 128 (at most the head's rows).
+    const unsigned fl = (unsigned)ctx->spec.flags;
+    int path = 0;
+    if (product && hd.tc) {
+        if (fl & MOE_FLAG_INT8_TENSOR_CORES_NEVER) path = 0;
+        else if (fl & MOE_FLAG_INT8_TENSOR_CORES_ALWAYS) path = 1;
+        else if (fl & MOE_FLAG_TENSOR_CORES_ALWAYS) path = 2;
+        else if (T >= (hd.m.type == FMT_Q4_K ? kLmHeadF16MinTokensQ4K : kLmHeadF16MinTokensQ80) &&
+                 !(fl & MOE_FLAG_TENSOR_CORES_NEVER))
+            path = 2;
+        else if (T >= kLmHeadTcMinTokens) path = 1;
+    }
+    const bool tc = path != 0;
     const int yrows = tc ? (target + 127) / 128 * 128 : target;
     const bool direct = ptr_kind == MOE_PTR_DEVICE && target == n_logits && yrows == target;
     // call buffers: the status word and the problem first (fixed offsets, so the
@@ -1318,7 +1333,8 @@ int moe_lm_head(moe_ctx *ctx, int32_t T, const float *normed, float *logits, int
     auto take = [&](size_t b) { size_t o = off; off += align_up(b ? b : 1, 256); return o; };
     const size_t o_e = take(16), o_p = take(sizeof(Problem) + 16), o_x = take((size_t)T * H * 4),
                  o_q = take((size_t)T * H), o_d = take((size_t)T * (H / 32) * 4), o_s = take((size_t)T * (H / 32) * 4),
-                 o_y = take(direct ? 0 : (size_t)T * std::max(yrows, 1) * 4), o_l = take((size_t)T * n_logits * 4);
+                 o_y = take(direct ? 0 : (size_t)T * std::max(yrows, 1) * 4), o_l = take((size_t)T * n_logits * 4),
+                 o_h = take(path == 2 ? (size_t)T * H * 2 : 0), o_t = take(path == 2 ? 4 * kTileOffStride * 4 : 0);
     if (hd.buf_bytes < off) {
         CUDA_TRY(ctx, cudaStreamSynchronize(st), "cudaStreamSynchronize");
         if (hd.buf) cudaFree(hd.buf);
@@ -1364,10 +1380,20 @@ int moe_lm_head(moe_ctx *ctx, int32_t T, const float *normed, float *logits, int
             if ((e = (cudaError_t)launch_quantize_rows(x, T, H, pl.aq, pl.ad, pl.as, st)) != cudaSuccess)
                 return cuda_fail(ctx, e, "LM head activation blocks");
         }
-        if ((e = launch_lm_head_prep(pl.problems, pl.n_active, T, st)) != cudaSuccess)
+        if (path == 2) {
+            pl.xq = pl.aq;
+            pl.xd = pl.ad;
+            pl.a16dn = b + o_h;
+            pl.a16dn_stride = H;
+            pl.slots_cap = T;
+            pl.tile_off = reinterpret_cast<int32_t *>(b + o_t);
+        }
+        if (path != 2 && (e = launch_lm_head_prep(pl.problems, pl.n_active, T, st)) != cudaSuccess)
             return cuda_fail(ctx, e, "LM head problem");
-        e = tc && decode_tc_down_ok(pl, Lh) ? launch_decode_tc_down(pl, Lh, lm, ctx->num_sms, st)
-                                            : launch_down(pl, Lh, lm, 0, ctx->num_sms, st);
+        if (path == 2 && dense_f16_ok(pl, Lh)) e = launch_dense_f16(pl, Lh, lm, ctx->num_sms, st);
+        else if (path == 1 && decode_tc_down_ok(pl, Lh)) e = launch_decode_tc_down(pl, Lh, lm, ctx->num_sms, st);
+        else if (path == 0) e = launch_down(pl, Lh, lm, 0, ctx->num_sms, st);
+        else e = cudaErrorInvalidValue;   // the checks above admit every tensor-core head
         if (e != cudaSuccess) return cuda_fail(ctx, e, "LM head");
         if (!direct && (e = launch_lm_head_scatter(pl.y, yrows, target, x, H, lg, n_logits, T, ctx->num_sms, st)) !=
                            cudaSuccess)

@@ -61,6 +61,13 @@ cudaError_t launch_rmsnorm(const FwdParams &p, cudaStream_t st);
 // down GEMMs); replaces launch_gate_up / launch_down for large token counts.
 cudaError_t launch_prefill(const FwdParams &p, const LayerDev &L, const LayerMaps &maps, int num_sms,
                            const Marker &mk, cudaStream_t st);
+// One dense problem on the f16 tensor-core down launch: slots 0 .. p.T-1 (the
+// int8 blocks p.xq / p.xd of rows of p.W values, expanded to f16 into p.a16dn)
+// times the p.H rows of L.down, into p.y [T][p.H]; item offsets in p.tile_off.
+// The LM head's product for larger batches.
+bool dense_f16_ok(const FwdParams &p, const LayerDev &L);
+cudaError_t launch_dense_f16(const FwdParams &p, const LayerDev &L, const LayerMaps &maps, int num_sms,
+                             cudaStream_t st);
 
 // Tensor-core expert path with integer operands for small batches: the gate/up
 // and down launches (routed problems, plus the shared expert when p.S > 0), or

@@ -390,18 +390,19 @@ __device__ __forceinline__ float q8_to_f32(uint32_t flipped, int byte_idx)
     return __int_as_float((int)b) - 8388736.0f;   // 2^23 + 128
 }
 
-__global__ void __launch_bounds__(256) gather_act_f16_kernel(FwdParams p, int n_slots)
+// perm: slot -> token row, or null for slot s = row s.
+__global__ void __launch_bounds__(256) gather_act_f16_kernel(const int32_t *perm, const int8_t *xq, const float *xd,
+                                                             int H, __half *a16, int stride, int n_slots)
 {
-    const int H = p.H, chunks = H >> 4;
+    const int chunks = H >> 4;
     const int lane = threadIdx.x & 31;
     const int warp = (int)((blockIdx.x * (size_t)blockDim.x + threadIdx.x) >> 5);
     const int n_warps = (int)((gridDim.x * (size_t)blockDim.x) >> 5);
-    __half *a16 = static_cast<__half *>(p.a16);
     for (int s = warp; s < n_slots; s += n_warps) {
-        const size_t tok = (size_t)p.perm_token[s];
-        const int8_t *xr = p.xq + tok * H;
-        const float *dr = p.xd + tok * (H >> 5);
-        __half *dst = a16 + (size_t)s * p.a16_stride;
+        const size_t tok = perm ? (size_t)perm[s] : (size_t)s;
+        const int8_t *xr = xq + tok * H;
+        const float *dr = xd + tok * (H >> 5);
+        __half *dst = a16 + (size_t)s * stride;
         for (int c = lane; c < chunks; c += 32) {
             const uint4 q = *reinterpret_cast<const uint4 *>(xr + 16 * c);
             const float d = dr[c >> 1];
@@ -446,6 +447,18 @@ __global__ void tile_plan_kernel(FwdParams p, int rows_gu, int rows_gu_sh, int r
     dn_sh[0] = 0;
     gu_sh[1] = sh_gu;
     dn_sh[1] = sh_dn;
+}
+
+// One problem of T slots over the rows of a single matrix (the down layout):
+// its entry, the active count and its item offsets.
+__global__ void dense_plan_kernel(Problem *prob, int32_t *n_active, int32_t *tile_off, int T, int rows)
+{
+    prob[0] = Problem{0, 0, T, 0};
+    *n_active = 1;
+    int32_t *dn = tile_off + 2 * kTileOffStride;
+    dn[0] = 0;
+    dn[1] = chunk_count(T, kCapDN) * (rows / kM);
+    dn[2] = dn[1];
 }
 
 // f16 activation operand [rows][cols] with row stride stride_elems: box 64 x 32, 128-byte swizzle.
@@ -504,7 +517,8 @@ cudaError_t launch_prefill(const FwdParams &p, const LayerDev &L, const LayerMap
 {
     cudaError_t e;
     const int n_slots = p.T * p.k + (p.S > 0 ? p.T : 0);
-    gather_act_f16_kernel<<<num_sms * 8, 256, 0, st>>>(p, n_slots);
+    gather_act_f16_kernel<<<num_sms * 8, 256, 0, st>>>(p.perm_token, p.xq, p.xd, p.H, static_cast<__half *>(p.a16),
+                                                       p.a16_stride, n_slots);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     tile_plan_kernel<<<1, 32, 0, st>>>(p, L.gate.rows, p.S > 0 ? L.sh_gate.rows : 0, p.H);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
@@ -529,6 +543,27 @@ cudaError_t launch_prefill(const FwdParams &p, const LayerDev &L, const LayerMap
     if (has_sh && !same_dn && (e = dn(1)) != cudaSuccess) return e;
     mk.mark("down_tc");
     return cudaSuccess;
+}
+
+bool dense_f16_ok(const FwdParams &p, const LayerDev &L)
+{
+    const DevMatrix &m = L.down;
+    return (m.type == FMT_Q4_K || m.type == FMT_Q8_0) && m.rows % kM == 0 && m.cols % kKS == 0 && p.H == m.rows &&
+           p.W == m.cols && p.a16dn && p.tile_off && p.a16dn_stride % 8 == 0 && p.slots_cap >= p.T;
+}
+
+cudaError_t launch_dense_f16(const FwdParams &p, const LayerDev &L, const LayerMaps &maps, int num_sms,
+                             cudaStream_t st)
+{
+    if (!dense_f16_ok(p, L)) return cudaErrorInvalidValue;
+    gather_act_f16_kernel<<<num_sms * 4, 256, 0, st>>>(nullptr, p.xq, p.xd, p.W, static_cast<__half *>(p.a16dn),
+                                                       p.a16dn_stride, p.T);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    dense_plan_kernel<<<1, 1, 0, st>>>(p.problems, p.n_active, p.tile_off, p.T, L.down.rows);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    return L.down.type == FMT_Q4_K ? launch_tc<FMT_Q4_K, 1>(p, L, maps, 0, num_sms, st)
+                                   : launch_tc<FMT_Q8_0, 1>(p, L, maps, 0, num_sms, st);
 }
 
 }  // namespace jmoe
