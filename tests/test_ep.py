@@ -122,16 +122,16 @@ def test_gpu_ep_requires_init_and_split():
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("flags,exact", [(STREAM, True),
-                                         (STREAM | jm.FLAG_EP_NCCL_ONLY, True),
-                                         (INT8, True),
-                                         (0, False),
-                                         (jm.FLAG_TENSOR_CORES_ALWAYS, False)])
-def test_gpu_ep_two_ranks(flags, exact):
+@pytest.mark.parametrize("flags,exact,T", [(STREAM, True, 40),
+                                           (STREAM | jm.FLAG_EP_NCCL_ONLY, True, 40),
+                                           (INT8, True, 40),
+                                           (0, False, 40),
+                                           (0, False, 1),   # one token per rank: the streaming local stage
+                                           (jm.FLAG_TENSOR_CORES_ALWAYS, False, 300)])
+def test_gpu_ep_two_ranks(flags, exact, T):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     over = dict(E=16, k=4, I=384, S=512, H=512)
-    T = 300 if flags & jm.FLAG_TENSOR_CORES_ALWAYS else 40
     mp.spawn(gpu_worker, args=(2, free_port(), 3, over, T, flags, exact), nprocs=2, join=True)
 
 
