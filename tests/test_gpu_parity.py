@@ -613,7 +613,14 @@ def test_gpu_lm_head(quant, T, rows):
         ctx.lm_head_upload(None, head, hidden)   # tied embeddings
         got = ctx.lm_head(x, rows)
         assert row_rel_err(got, orc.lm_head(head, hidden, x, rows)).max() <= OUT_TOL
+        # device pointers with every logit a head row: the product writes the
+        # caller's buffer directly; bit for bit the host call
+        import torch
+        xd = torch.from_numpy(x).cuda()
+        od = torch.full((T, rows), float("nan"), dtype=torch.float32, device="cuda")
+        ctx.lm_head_ptrs(T, xd.data_ptr(), od.data_ptr(), rows)
         assert ctx.device_status() == 0
+        np.testing.assert_array_equal(od.cpu().numpy(), got)
 
 
 def test_gpu_lm_head_flat_synthetic_device_pointers_and_errors():
