@@ -618,6 +618,7 @@ def test_gpu_lm_head(quant, T, rows):
         import torch
         xd = torch.from_numpy(x).cuda()
         od = torch.full((T, rows), float("nan"), dtype=torch.float32, device="cuda")
+        torch.cuda.synchronize()   # the fill runs on torch's stream, the head on the context's
         ctx.lm_head_ptrs(T, xd.data_ptr(), od.data_ptr(), rows)
         assert ctx.device_status() == 0
         np.testing.assert_array_equal(od.cpu().numpy(), got)
