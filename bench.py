@@ -355,6 +355,21 @@ class Timer:
             self.ctx.set_profiling(False)
         return [a.elapsed_time(b) for a, b in evs], prof
 
+    def stages(self, t, n):
+        """Per-stage times from n profiled forwards, one at a time: for each
+        stage the median over the forwards of its time per forward, so a single
+        slow forward (a clock dip, a first launch) does not move the figure.
+        Returns ({stage: (ms per forward, launches per forward)}, n)."""
+        import statistics
+        per = {}
+        for _ in range(n):
+            _, (prof, _) = self.run(t, 1, True)
+            for k, (ms, launches) in prof.items():
+                a = per.setdefault(k, ([], []))
+                a[0].append(ms)
+                a[1].append(launches)
+        return {k: (statistics.median(v[0]), int(statistics.median(v[1]))) for k, v in per.items()}, n
+
 
 def probe_peaks(jm):
     """This GPU's dense tensor peaks from the library's probe (one issuing warp
@@ -391,7 +406,7 @@ def extra_config(torch, jm, synth, cid, T, stream, flush, tensor_peaks, steps=10
         tm = Timer(torch, ctx, stream, flush, step, lambda: None, 1)
         tm.run(T, 3, False)
         ms, _ = tm.run(T, steps, False)
-        _, (prof, _) = tm.run(T, max(3, steps // 2), True)
+        prof, _ = tm.stages(T, max(5, steps // 2))
         sel = si_dev.cpu().numpy()
         kb = kernel_bytes(cfg, weights, sel, T)
         wl = f"{cfg.name} T={T}"
@@ -489,7 +504,7 @@ def run_ours(args):
     clocks = sampler.stop()
     # per-stage breakdown from a second pass with an event at every stage
     # boundary (the events serialise the stages, so it is not the timed pass)
-    _, (prof, n_fwd) = tm.run(T, args.steps, True)
+    prof, n_fwd = tm.stages(T, args.steps)
     total_ms = sum(step_ms)
     if world > 1:
         tt = torch.tensor([total_ms], device="cuda")
@@ -499,8 +514,9 @@ def run_ours(args):
     wl = f"{cfg.name} T={T}"
     roofline = roofline_of(cfg, T, prof, kb, wl, kb["routed_rows"] if ep else None, ep=ep, tensor_peaks=tensor_peaks)
     layer_ms = total_ms / args.steps
-    kernels = {k: {"avg_us": round(1e3 * v[0] / v[1], 2), "launches": v[1]} for k, v in prof.items()}
-    launches = sum(v[1] for v in prof.values())
+    # per launch (median forward), and the launches of the timed pass
+    kernels = {k: {"avg_us": round(1e3 * v[0] / v[1], 2), "launches": v[1] * args.steps} for k, v in prof.items()}
+    launches = sum(v[1] for v in prof.values()) * args.steps
 
     # parity of the timed run's output, outside the timed region: sampled rows
     # against the CPU oracle; with expert parallelism also every row against a
