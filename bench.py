@@ -368,7 +368,7 @@ class Timer:
                 a = per.setdefault(k, ([], []))
                 a[0].append(ms)
                 a[1].append(launches)
-        return {k: (statistics.median(v[0]), int(statistics.median(v[1]))) for k, v in per.items()}, n
+        return {k: (statistics.median(v[0]), max(1, int(statistics.median(v[1])))) for k, v in per.items()}, n
 
 
 def probe_peaks(jm):
