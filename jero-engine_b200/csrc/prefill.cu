@@ -37,7 +37,8 @@ constexpr int kCapGU = 128, kCapDN = 256;       // slots per item (MMA N) of the
 constexpr int kXBoxRows = 32, kXBoxBytes = kXBoxRows * 128;
 // two MMA-issuing warps: one thread completes about one tcgen05 instruction per
 // 130-250 cycles, so gate/up (eight MMAs per K step) issues matrix m from warp
-// kWarpMma + m; down (four) uses the first only
+// kWarpMma + m; down items of at most 128 slots split each K step's four MMAs
+// over the two (own accumulators, added by the epilogue), larger ones use the first
 constexpr int kWarpTma = 0, kWarpMma = 1, kMmaWarps = 2, kDeqWarp0 = 3, kDeqWarps = 8, kEpiWarp0 = 11, kEpiWarps = 4;
 constexpr int kTcThreads = (kEpiWarp0 + kEpiWarps) * 32;
 constexpr int kMaxStages = 6;
@@ -138,10 +139,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         for (int i = 0; i < c.kst; i++) {
             mbar_init(&x_full[i], 1);
             mbar_init(&w_full[i], kDeqWarps);
-            mbar_init(&k_empty[i], NMAT);   // one commit per issuing warp
+            mbar_init(&k_empty[i], kMmaWarps);   // one commit per issuing warp
         }
         for (int i = 0; i < c.qst; i++) { mbar_init(&q_full[i], 1); mbar_init(&q_empty[i], kDeqWarps); }
-        for (int i = 0; i < 2; i++) { mbar_init(&acc_full[i], NMAT); mbar_init(&acc_empty[i], kEpiWarps); }
+        for (int i = 0; i < 2; i++) { mbar_init(&acc_full[i], kMmaWarps); mbar_init(&acc_empty[i], kEpiWarps); }
         mbar_init(&drain_bar[0], 1);
         mbar_init(&drain_bar[1], 1);
         *abort_flag = 0;
@@ -200,9 +201,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             }
         }
     } else if (warp < kWarpMma + kMmaWarps) {
-        // issuer mi: matrix mi of every K step (gate/up), or all of them (down, mi = 0)
+        // issuer mi: gate/up, matrix mi of every K step; down, the 16-value sub-steps
+        // 2 mi and 2 mi + 1 of every step into the accumulator at column 128 mi when
+        // the item has at most 128 slots, else (mi = 0) all of them. Both issuers
+        // wait for every stage and commit every stage and item, so the barrier
+        // counts never depend on the item.
         const int mi = warp - kWarpMma;
-        if (lane == 0 && mi < NMAT) {
+        if (lane == 0) {
             RingPos kr, ar;
             bool ok = true, issued = false;
             // smem descriptors of stage 0; a stage, matrix or 16-value K step moves the
@@ -225,14 +230,29 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                         !tc_wait(&w_full[st], kr.phase, abort_flag, p.err)) { ok = false; break; }
                     tc_fence_after();
                     const uint64_t bd = b_desc0 + (uint64_t)((st * c.x_bytes) >> 4);
-                    {
+                    if (NMAT == 2) {
                         const uint64_t ad = a_desc0 + (uint64_t)(((st * NMAT + mi) * kWTileBytes) >> 4);
                         const uint32_t d = dbase + (uint32_t)(mi * kCapGU);
 #pragma unroll
                         for (int k16 = 0; k16 < kKS / 16; k16++)
                             tc_mma_f16(d, ad + 2 * k16, bd + 2 * k16, idesc, (kk | k16) != 0);
+                        issued = true;
+                    } else if (npad <= 128) {
+                        const uint64_t ad = a_desc0 + (uint64_t)((st * kWTileBytes) >> 4);
+                        const uint32_t d = dbase + (uint32_t)(mi * 128);
+#pragma unroll
+                        for (int h = 0; h < 2; h++) {
+                            const int k16 = 2 * mi + h;
+                            tc_mma_f16(d, ad + 2 * k16, bd + 2 * k16, idesc, (kk | h) != 0);
+                        }
+                        issued = true;
+                    } else if (mi == 0) {
+                        const uint64_t ad = a_desc0 + (uint64_t)((st * kWTileBytes) >> 4);
+#pragma unroll
+                        for (int k16 = 0; k16 < kKS / 16; k16++)
+                            tc_mma_f16(dbase, ad + 2 * k16, bd + 2 * k16, idesc, (kk | k16) != 0);
+                        issued = true;
                     }
-                    issued = true;
                     tc_commit(&k_empty[st]);
                     kr.advance(c.kst);
                 }
@@ -350,7 +370,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                         if (i < n_here) dst[(size_t)i * p.a16dn_stride] = __float2half_rn(q * dq);
                     }
                 } else {
-                    tmem_ld_wait();
+                    if (x.n <= 128) {   // two issuers' accumulators: columns c and 128 + c
+                        uint32_t g2[32];
+                        tmem_ld32(tb + 128 + 32 * cc, g2);
+                        tmem_ld_wait();
+#pragma unroll
+                        for (int i = 0; i < 32; i++)
+                            g[i] = __float_as_uint(__fadd_rn(__uint_as_float(g[i]), __uint_as_float(g2[i])));
+                    } else {
+                        tmem_ld_wait();
+                    }
                     const size_t s0 = (size_t)x.slot + 32 * cc;
                     if (p.y_rows) {   // expert parallel: the output row of each slot is its received row
 #pragma unroll
