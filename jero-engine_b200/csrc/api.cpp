@@ -1282,10 +1282,10 @@ int moe_lm_head_upload(moe_ctx *ctx, const moe_tensor *output_weight, const moe_
 // Rows of normed activations from which the LM head's product runs on the
 // int8 tensor cores (decode_tc.cu down launch) instead of the streaming kernel,
 // and from which on the f16 tensor-core GEMM (prefill.cu, one dense problem):
-// measured crossovers on a 151936 x 2048 head (Q4_K: f16 159 us vs int8 206 at
-// 16 rows; Q8_0: int8 147 vs f16 166 at 16, f16 167 vs int8 309 at 32).
+// measured crossovers on a 151936 x 2048 head (16 rows: Q4_K f16 145 us vs int8
+// 206, Q8_0 f16 137 vs int8 147; 8 rows: int8 100-126 vs f16 about 140).
 constexpr int kLmHeadTcMinTokens = 8;
-constexpr int kLmHeadF16MinTokensQ4K = 16, kLmHeadF16MinTokensQ80 = 24;
+constexpr int kLmHeadF16MinTokensQ4K = 16, kLmHeadF16MinTokensQ80 = 16;
 
 // logits [T x n_logits] of T normed rows [T x hidden], each row as
 // project_lm_head: the head's first min(n_logits, rows) rows as a quantised

@@ -479,14 +479,14 @@ __global__ void tile_plan_kernel(FwdParams p, int rows_gu, int rows_gu_sh, int r
 }
 
 // One problem of T slots over the rows of a single matrix (the down layout):
-// its entry, the active count and its item offsets.
-__global__ void dense_plan_kernel(Problem *prob, int32_t *n_active, int32_t *tile_off, int T, int rows)
+// its entry, the active count and its item offsets for slot chunks of cap.
+__global__ void dense_plan_kernel(Problem *prob, int32_t *n_active, int32_t *tile_off, int T, int rows, int cap)
 {
     prob[0] = Problem{0, 0, T, 0};
     *n_active = 1;
     int32_t *dn = tile_off + 2 * kTileOffStride;
     dn[0] = 0;
-    dn[1] = chunk_count(T, kCapDN) * (rows / kM);
+    dn[1] = chunk_count(T, cap) * (rows / kM);
     dn[2] = dn[1];
 }
 
@@ -497,9 +497,11 @@ cudaError_t encode_f16_map(CUtensorMap *m, const void *base, uint64_t rows, uint
                                                                                           : cudaErrorInvalidValue;
 }
 
+// cap > 0 (down only): slot chunks of cap (a multiple of 32) instead of
+// kCapDN, and as many K-step stages as the smaller activation tiles leave room for.
 template <int FMT, int NMAT>
 cudaError_t launch_tc(const FwdParams &p, const LayerDev &L, const LayerMaps &lm, int mode, int num_sms,
-                      cudaStream_t st)
+                      cudaStream_t st, int cap = 0)
 {
     TcMaps maps;
     const DevMatrix &A0 = NMAT == 2 ? (mode == 1 ? L.sh_gate : L.gate) : (mode == 1 ? L.sh_down : L.down);
@@ -524,6 +526,14 @@ cudaError_t launch_tc(const FwdParams &p, const LayerDev &L, const LayerMaps &lm
     // down: x 32 + w 16), a quantised stage 36 KB (gate/up) or 18 KB (down)
     c.kst = 3;
     c.qst = NMAT == 2 ? 2 : 3;
+    if (NMAT == 1 && cap > 0) {
+        if (cap % kXBoxRows != 0 || cap > kCapDN) return cudaErrorInvalidValue;
+        c.cap = cap;
+        c.x_bytes = cap * 128;
+        const int room = 200 * 1024 - c.qst * kQBytes;
+        c.kst = room / (c.x_bytes + kWTileBytes);
+        c.kst = c.kst < 3 ? 3 : (c.kst > kMaxStages ? kMaxStages : c.kst);
+    }
     c.max_q = p.max_problems;
     c.smem_x = 0;
     c.smem_w = c.smem_x + c.kst * c.x_bytes;
@@ -589,10 +599,12 @@ cudaError_t launch_dense_f16(const FwdParams &p, const LayerDev &L, const LayerM
                                                        p.a16dn_stride, p.T);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
-    dense_plan_kernel<<<1, 1, 0, st>>>(p.problems, p.n_active, p.tile_off, p.T, L.down.rows);
+    // a few rows (decode batches): chunks of 64 slots, six K-step stages
+    const int cap = p.T <= 64 ? 64 : kCapDN;
+    dense_plan_kernel<<<1, 1, 0, st>>>(p.problems, p.n_active, p.tile_off, p.T, L.down.rows, cap);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
-    return L.down.type == FMT_Q4_K ? launch_tc<FMT_Q4_K, 1>(p, L, maps, 0, num_sms, st)
-                                   : launch_tc<FMT_Q8_0, 1>(p, L, maps, 0, num_sms, st);
+    return L.down.type == FMT_Q4_K ? launch_tc<FMT_Q4_K, 1>(p, L, maps, 0, num_sms, st, cap)
+                                   : launch_tc<FMT_Q8_0, 1>(p, L, maps, 0, num_sms, st, cap);
 }
 
 }  // namespace jmoe

@@ -597,7 +597,7 @@ def test_gpu_lm_head(quant, T, rows):
     normed * 0.05, bit for bit), and the tied token_embd head when
     output.weight is absent. Rows within 1e-2 max relative error. 10240 rows
     (whole 128-row tiles) take the int8 tensor-core launch from 8 tokens and
-    the f16 tensor-core GEMM from 16 (Q4_K) or 24 (Q8_0)."""
+    the f16 tensor-core GEMM from 16."""
     hidden = 1024
     head = _lm_head_case(quant, hidden, rows, 3)
     x = np.random.default_rng(T).standard_normal((T, hidden)).astype(np.float32)
