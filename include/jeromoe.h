@@ -250,12 +250,15 @@ int moe_prefill_ffn_layers(moe_ctx *ctx, int32_t first_layer, int32_t n_layers, 
  * head. */
 int moe_lm_head_upload(moe_ctx *ctx, const moe_tensor *output_weight, const moe_tensor *token_embd, int32_t hidden);
 /* logits [T x n_logits] of T final-normed rows normed [T x hidden]: per row
- * the head's first min(n_logits, rows) rows (the product with int8 activation
- * blocks, as the expert matrices), then normed[i mod hidden] * 0.05 for the
- * logits past them; without a usable head base + normed[i mod hidden] * 0.1 +
- * (i mod 13) * 0.01 with base = tanh(sum(normed) / 16). T <= max_tokens.
- * MOE_PTR_HOST: synchronous; MOE_PTR_DEVICE: asynchronous on the context's
- * stream (status via moe_device_status once a layer is uploaded). */
+ * the head's first min(n_logits, rows) rows, then normed[i mod hidden] * 0.05
+ * for the logits past them; without a usable head base + normed[i mod hidden]
+ * * 0.1 + (i mod 13) * 0.01 with base = tanh(sum(normed) / 16). T <= max_tokens.
+ * The product uses the int8 activation blocks of the expert paths: integer
+ * block sums below 16 rows (streaming kernel, or the int8 tensor cores from 8
+ * rows on heads of whole 128-row tiles), the f16 tensor-core GEMM from 16
+ * rows on such heads (within the same 1e-2 row tolerance); the MOE_FLAG_*
+ * tensor-core flags force a form. MOE_PTR_HOST: synchronous; MOE_PTR_DEVICE:
+ * asynchronous on the context's stream (status via moe_device_status). */
 int moe_lm_head(moe_ctx *ctx, int32_t T, const float *normed, float *logits, int32_t n_logits, int32_t ptr_kind);
 
 int moe_residency_summary(const moe_ctx *ctx, moe_residency *out);
