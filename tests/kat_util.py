@@ -85,3 +85,14 @@ def row_rel_err(y, ref):
     num = np.max(np.abs(y - ref), axis=-1)
     den = np.maximum(np.max(np.abs(ref), axis=-1), 1e-30)
     return num / den
+
+
+def tied_embedding_fixture():
+    """The token embedding of the reference's tied-embedding test
+    (build_qwen_dense_weights, src/qwen_deepseek.rs:2465-2479): GGUF shape
+    [hidden 8, vocab 16], element i = ((i mod 19) - 9) * 0.04; with no
+    output.weight the head is this tensor (test at :2501-2546)."""
+    hidden, vocab = 8, 16
+    i = np.arange(vocab * hidden)
+    emb = (((i % 19).astype(np.float32) - np.float32(9.0)) * np.float32(0.04)).astype(np.float32)
+    return hidden, vocab, jm.f32_tensor(emb, [hidden, vocab])

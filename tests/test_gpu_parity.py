@@ -675,3 +675,17 @@ def test_gpu_lm_head_tensor_cores_match_streaming(quant):
             outs.append(ctx.lm_head(x, 3000))
     assert row_rel_err(outs[1], outs[0]).max() <= 1e-5
     assert row_rel_err(outs[1], orc.lm_head(head, hidden, x, 3000)).max() <= OUT_TOL
+
+
+def test_gpu_lm_head_tied_embedding_fixture():
+    """The tied token embedding of the reference's own test model (f32,
+    [hidden 8, vocab 16]) as the head when output.weight is absent: finite,
+    not all zero, and the oracle's logits within 1e-5."""
+    from kat_util import tied_embedding_fixture
+    hidden, vocab, emb = tied_embedding_fixture()
+    x = np.random.default_rng(3).standard_normal((2, hidden)).astype(np.float32)
+    with jm.Context(0, 4, 1) as ctx:
+        ctx.lm_head_upload(None, emb, hidden)
+        got = ctx.lm_head(x, vocab)
+    assert np.all(np.isfinite(got)) and np.any(np.abs(got) > 1e-6)
+    np.testing.assert_allclose(got, orc.lm_head(emb, hidden, x, vocab), rtol=1e-5, atol=1e-6)

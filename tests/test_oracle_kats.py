@@ -6,7 +6,7 @@ import pytest
 import jeromoe as jm
 import oracle as orc
 import synth
-from kat_util import check_dispatch_expect, kat_weights, load_kats, load_seeded, seeded_case
+from kat_util import check_dispatch_expect, kat_weights, load_kats, load_seeded, seeded_case, tied_embedding_fixture
 
 KATS = load_kats()
 
@@ -217,3 +217,16 @@ def test_oracle_lm_head_quantised(quant):
     ref = _lm_head_numpy(hidden, x, n_logits, Wd)
     err = np.abs(got - ref).max(axis=1) / np.abs(ref).max(axis=1)
     assert err.max() <= 1e-2, err
+
+
+def test_oracle_lm_head_tied_embedding_fixture():
+    """The reference's checks on that model's logits (finite, not all zero,
+    `assert_eq!(out_alias.shape(), &[8, 16])`), and each logit the f32 dot of
+    the tied row with the normed activations."""
+    hidden, vocab, emb = tied_embedding_fixture()
+    assert list(emb.shape) == [8, 16]
+    x = np.random.default_rng(3).standard_normal((2, hidden)).astype(np.float32)
+    got = orc.lm_head(emb, hidden, x, vocab)
+    assert np.all(np.isfinite(got)) and np.any(np.abs(got) > 1e-6)
+    ref = x.astype(np.float64) @ emb.data.reshape(vocab, hidden).astype(np.float64).T
+    np.testing.assert_allclose(got, ref, rtol=1e-5, atol=1e-6)
